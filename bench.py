@@ -1,0 +1,436 @@
+"""Benchmark of the MoE-layer hot path (H=2048, I=768, E=128, top-8, bf16).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
+
+One step = one MoE-layer forward over T tokens.  At N=1 the workload is the
+single-B200 fused MoE layer at T=16384 (router, sort, gather, w13+SwiGLU, w2,
+combine) through ``moe_layer_forward``; ``value`` is tokens/s with inputs
+resident in HBM, ``e2e`` the same through ``PermutedSparseMoE.forward`` with the
+input copied from pinned host memory and the output copied back inside the
+timed region.  At N>1 every rank runs the expert-parallel all_to_all schedule
+(``EPSparseMoE``, C7 semantics) on its own T tokens with E/N experts
+(weak scaling).  ``--impl reference`` times the reference algorithm's CPU
+restatement (the oracle) on the host cores on a bounded sample of the same
+workload.  Rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "MoE layer tokens/s (H=2048,I=768,E=128,top8,bf16), 1/2/4/8 B200, % of roofline"
+H, I, E, K_TOP = 2048, 768, 128, 8
+PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def layer_flops(T: int) -> float:
+    return float(T) * (2 * H * E + K_TOP * 6 * H * I)
+
+
+def layer_bytes(n_active: int, T: int) -> float:
+    return n_active * 3 * H * I * 2 + 2 * H * E + 4 * T * H
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ----------------------------------------------------------------------------- inputs
+
+
+def make_device_inputs(T: int, device, seed: int = 0, experts_per_rank: int = E, e0: int = 0):
+    """Seeded synthetic inputs: x ~ N(0,1), weights ~ N(0, 0.02), bf16 on the device."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=g, device=device).to(bf)
+    wr = (torch.randn(E, H, generator=g, device=device) * 0.02).to(bf)
+    g2 = torch.Generator(device=device)
+    g2.manual_seed(1000 + seed)
+    wg = torch.empty(experts_per_rank, I, H, dtype=bf, device=device)
+    wu = torch.empty_like(wg)
+    wd = torch.empty(experts_per_rank, H, I, dtype=bf, device=device)
+    for t in (wg, wu, wd):
+        for e in range(experts_per_rank):
+            t[e] = (torch.randn(t.shape[1:], generator=g2, device=device) * 0.02).to(bf)
+    return x, wr, wg, wu, wd
+
+
+# ----------------------------------------------------------------------------- CPU arm
+
+
+def cpu_layer_sample(x, wr, wg, wu, wd, tokens: int, reps: int):
+    """Time the oracle's restatement of PermutedSparseMoE.forward on host cores."""
+    from oracle import moe_oracle as mo
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max((d.get("num_threads", 1) for d in threadpool_info()), default=os.cpu_count())
+    except Exception:  # threadpoolctl missing: numpy BLAS uses every core by default
+        threads = os.cpu_count()
+    xs = x[:tokens]
+    mo.permuted_moe(xs, wr, wg, wu, wd, K_TOP, True, mode="ref")  # warm-up
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        mo.permuted_moe(xs, wr, wg, wu, wd, K_TOP, True, mode="ref")
+        times.append(time.perf_counter() - t0)
+    return times, threads
+
+
+def host_f32(*ts):
+    return [t.float().cpu().numpy() for t in ts]
+
+
+def run_reference(args):
+    """--impl reference: the oracle port of the reference path on host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    T = args.tokens
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    x, wr, wg, wu, wd = make_device_inputs(min(T, 1024), dev)
+    xf, wrf, wgf, wuf, wdf = host_f32(x, wr, wg, wu, wd)
+    del x, wr, wg, wu, wd
+    # Size each step's sample so that warm-up + steps stay within ~2 minutes.
+    t_probe, threads = cpu_layer_sample(xf, wrf, wgf, wuf, wdf, 64, 1)
+    per_tok = t_probe[0] / 64
+    budget = 100.0 / max(1, args.steps + args.warmup)
+    tokens = int(max(8, min(256, budget / max(per_tok, 1e-9))))
+    times, threads = cpu_layer_sample(xf, wrf, wgf, wuf, wdf, tokens, args.warmup + args.steps)
+    times = times[args.warmup:] if len(times) > args.warmup else times
+    total = sum(times)
+    value = tokens * len(times) / total
+    sample = (f"{tokens} of the {T} tokens per step (H=2048 I=768 E=128 k=8), numpy port of "
+              f"C5 PermutedSparseMoE.forward with bf16 rounding, {len(times)} steps")
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / len(times), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_block(T, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+
+def config_block(T: int, n: int) -> dict:
+    if n == 1:
+        wl = f"single-B200 fused MoE layer (C5/C9 path), T={T} tokens"
+        par = "single"
+    else:
+        wl = f"expert-parallel all_to_all MoE layer (C7 path), {T} tokens per rank, E/{n} experts per rank"
+        par = f"ep{n}"
+    return {"workload": wl, "tokens_per_rank": T, "hidden": H, "intermediate": I, "experts": E,
+            "top_k": K_TOP, "routing": "uniform (router N(0,0.02), no bias)", "parallelism": par,
+            "l2": "inputs larger than L2: 1.21 GB of expert weights streamed per step"}
+
+
+class Timer:
+    def __init__(self, stream):
+        self.stream = stream
+        self.a = torch.cuda.Event(enable_timing=True)
+        self.b = torch.cuda.Event(enable_timing=True)
+
+    def __enter__(self):
+        self.a.record(self.stream)
+        return self
+
+    def __exit__(self, *exc):
+        self.b.record(self.stream)
+
+    def ms(self):
+        return self.a.elapsed_time(self.b)
+
+
+def run_ours_single(args):
+    from moe_inference_verify_microbench_b200 import PermutedSparseMoE, ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    T = args.tokens
+    peaks, peak_kind = load_peaks()
+    x, wr, wg, wu, wd = make_device_inputs(T, dev)
+    stream = torch.cuda.current_stream(dev)
+    ws = torch.empty(ops.layer_workspace_bytes(T, H, I, E, K_TOP), dtype=torch.uint8, device=dev)
+    y = torch.empty_like(x)
+
+    def step():
+        ops.moe_layer(x, wr, wg, wu, wd, K_TOP, out=y, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    time.sleep(0.3)
+    # --- main timed region: whole layer through moe_layer_forward
+    torch.cuda.synchronize()
+    with Timer(stream) as tm:
+        for _ in range(args.steps):
+            step()
+    torch.cuda.synchronize()
+    ms_total = tm.ms()
+
+    # --- per-kernel breakdown: the same launches issued one C-ABI call at a time
+    ev = {n: [] for n in ("router", "sort", "gather", "w13", "w2", "combine")}
+    bufs = {}
+
+    def step_split():
+        marks = []
+        e0 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        marks.append(e0)
+
+        def mark():
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            marks.append(e)
+
+        ids, w, _ = ops.router_topk(x, wr, K_TOP)
+        mark()
+        s = ops.sort_align(ids, E)
+        mark()
+        sx = ops.gather_rows(x, s.perm, K_TOP, out=bufs.get("sx"))
+        bufs["sx"] = sx
+        mark()
+        h = ops.grouped_w13_swiglu(sx, s.tiles, s.num_tiles, s.max_tiles, wg, wu, out=bufs.get("h"))
+        bufs["h"] = h
+        mark()
+        sl = ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, wd, row_map=s.perm,
+                            slot_scale=w.reshape(-1), out=bufs.get("sl"))
+        bufs["sl"] = sl
+        mark()
+        ops.combine(sl, T, K_TOP, out=y)
+        mark()
+        return marks, s
+
+    n_split = max(3, min(args.steps, 50))
+    all_marks = []
+    for _ in range(n_split):
+        marks, s = step_split()
+        all_marks.append(marks)
+    torch.cuda.synchronize()
+    for marks in all_marks:
+        for i, n in enumerate(ev):
+            ev[n].append(marks[i].elapsed_time(marks[i + 1]))
+    counts = s.counts.cpu().numpy()
+    n_active = int((counts > 0).sum())
+
+    # --- e2e: PermutedSparseMoE.forward with host copies inside the timed region
+    with torch.device(dev):
+        mod = PermutedSparseMoE(H, I, E, K_TOP).to(torch.bfloat16)
+    bwg, bwu, bwd = mod.pack()
+    with torch.no_grad():
+        mod.gate.weight.copy_(wr)
+        bwg.copy_(wg)
+        bwu.copy_(wu)
+        bwd.copy_(wd)
+    del wg, wu, wd
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+    n_e2e = max(3, min(args.steps, 100))
+    with torch.no_grad():
+        for _ in range(2):
+            y_host.copy_(mod(x_host.to(dev, non_blocking=True)), non_blocking=True)
+        torch.cuda.synchronize()
+        with Timer(stream) as te:
+            for _ in range(n_e2e):
+                xd = x_host.to(dev, non_blocking=True)
+                y_host.copy_(mod(xd), non_blocking=True)
+        torch.cuda.synchronize()
+    clk = clocks.stop()
+    ops.check_status(dev)
+
+    ms_step = ms_total / args.steps
+    value = T / (ms_step * 1e-3)
+    avg = {n: statistics.mean(v) for n, v in ev.items()}
+    w13_flop = 2.0 * T * K_TOP * (2 * I) * H
+    w13_tflops = w13_flop / (avg["w13"] * 1e-3) / 1e12
+    peak_tc = peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]
+    t_roof = max(layer_flops(T) / (peak_tc * 1e12), layer_bytes(n_active, T) / (peaks["hbm_gbs"] * 1e9))
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded x~N(0,1), weights~N(0,0.02), random-init Qwen3-30B-A3B MoE shapes)",
+        "config": config_block(T, 1),
+        "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel<256,SwiGLU> (w13)",
+                     "achieved": w13_tflops, "peak": peak_tc, "unit": "TFLOP/s",
+                     "frac": w13_tflops / peak_tc, "traffic": None,
+                     "peak_source": f"{peak_kind} bf16_tflops_sustained",
+                     "algorithmic_per_launch": f"2*T*k*(2I)*H = {w13_flop:.4g} FLOP"},
+        "layer_roofline": {"t_roof_ms": t_roof * 1e3, "frac": t_roof * 1e3 / ms_step,
+                           "flop_per_step": layer_flops(T), "bytes_per_step": layer_bytes(n_active, T),
+                           "active_experts": n_active},
+        "breakdown_ms": {n: round(v, 5) for n, v in avg.items()},
+        "e2e": {"value": T * n_e2e / (te.ms() * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
+                "api": "PermutedSparseMoE.forward", "steps": n_e2e},
+        "gpu_launches": 8 * args.steps,
+        "clocks": clk,
+    }
+    if args.cpu_baseline:
+        xf, wrf = host_f32(x[:256], wr)
+        wgf, wuf, wdf = host_f32(bwg, bwu, bwd)
+        times, threads = cpu_layer_sample(xf, wrf, wgf, wuf, wdf, 256, 3)
+        line["cpu_baseline"] = {"value": 256 / statistics.median(times), "unit": "tokens/s",
+                                "cores": threads, "kind": "port",
+                                "sample": "T=256 tokens of the same weights, numpy port of C5 "
+                                          "PermutedSparseMoE.forward, median of 3 after 1 warm-up"}
+    if args.sweep:
+        line["sweep_tokens_per_s"] = sweep(dev, [int(t) for t in args.sweep.split(",")], wr,
+                                           bwg, bwu, bwd, peaks)
+    print(json.dumps(line), flush=True)
+
+
+def sweep(dev, token_counts, wr, wg, wu, wd, peaks):
+    """Decode / prefill sweep: CUDA-graph-captured layer, inputs resident."""
+    from moe_inference_verify_microbench_b200 import ops
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    for T in token_counts:
+        g = torch.Generator(device=dev)
+        g.manual_seed(T)
+        x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+        ws = torch.empty(ops.layer_workspace_bytes(T, H, I, E, K_TOP), dtype=torch.uint8, device=dev)
+        y = torch.empty_like(x)
+        for _ in range(3):
+            ops.moe_layer(x, wr, wg, wu, wd, K_TOP, out=y, workspace=ws)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            ops.moe_layer(x, wr, wg, wu, wd, K_TOP, out=y, workspace=ws)
+        n = 200 if T <= 1024 else 40
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        with Timer(stream) as t:
+            for _ in range(n):
+                graph.replay()
+        torch.cuda.synchronize()
+        ms = t.ms() / n
+        ids, _, _ = ops.router_topk(x, wr, K_TOP)
+        n_act = int(torch.bincount(ids.reshape(-1).long(), minlength=E).gt(0).sum())
+        peak_tc = peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]
+        t_roof = max(layer_flops(T) / (peak_tc * 1e12), layer_bytes(n_act, T) / (peaks["hbm_gbs"] * 1e9))
+        out[str(T)] = {"tokens_per_s": T / (ms * 1e-3), "us_per_layer": ms * 1e3,
+                       "roofline_frac": t_roof * 1e3 / ms, "active_experts": n_act}
+        del graph
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--sweep", default="1,16,128,1024,4096",
+                    help="comma-separated token counts for the graph-captured sweep ('' = none)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 or args.gpus > 1:
+        from moe_inference_verify_microbench_b200.ep_bench import run_ep
+        run_ep(args, METRIC, config_block, ClockSampler, make_device_inputs)
+        return
+    run_ours_single(args)
+
+
+if __name__ == "__main__":
+    main()

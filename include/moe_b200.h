@@ -1,0 +1,163 @@
+/*
+ * moe_b200.h — C ABI of the B200 (sm_100a) MoE-layer hot path.
+ *
+ * Drop-in kernels for the MoE layer of weidotwisc/moe_inference_verify_microbench
+ * (Qwen3-30B-A3B shapes: H=2048, I=768, E=128, top-8, bf16).  Every entry point:
+ *   - takes plain device pointers, sizes and a cudaStream_t; no torch types;
+ *   - is stream-ordered and never synchronises the host;
+ *   - returns an int: 0 on success, a negative MOE_RC_* code for a host-side
+ *     argument / shape / launch problem (nothing is launched then);
+ *   - writes device-side failures (expert id out of range, a bounded wait that
+ *     ran out) into the caller's device status word `status` (int32, may be
+ *     NULL); the first failure wins, 0 means none.  Read it after the stream
+ *     has finished; moe_error_string() names both kinds of code.
+ * The caller owns all memory.  Scratch space is passed in as `workspace`, with
+ * its size given by the matching *_workspace_bytes() query.
+ *
+ * Layouts (row-major, bf16 unless noted):
+ *   x [T, H]; router weight [E, H]; w_gate, w_up [E, I, H]; w_down [E, H, I];
+ *   top-k ids int32 [T, k], weights fp32 [T, k]; a "slot" is s = n*k + j.
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#if defined(__GNUC__)
+#define MOE_API __attribute__((visibility("default")))
+#else
+#define MOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_B200_ABI_VERSION 1
+
+#define MOE_RC_OK 0
+#define MOE_RC_BAD_ARGUMENT (-1)
+#define MOE_RC_UNSUPPORTED (-2)
+#define MOE_RC_CUDA_ERROR (-3)
+#define MOE_RC_TENSOR_MAP (-4)
+#define MOE_RC_WORKSPACE (-5)
+
+/* Rows per M-tile of the grouped GEMMs (the C9 BLOCK_M, fixed at 128 here). */
+#define MOE_BLOCK_M 128
+
+MOE_API int moe_abi_version(void);
+
+/* Text for a MOE_RC_* return code or a device status code. */
+MOE_API const char* moe_error_string(int code);
+
+/*
+ * Router: logits = bf16(x @ Wr^T [+ bias]) on tcgen05, then per token the
+ * top-k experts (value descending, lower expert id first among equal values)
+ * and their weights: softmax over the k selected logits when norm_topk_prob,
+ * else the softmax over all E gathered at the selected ids.
+ * Replaces C5/python/solution.py:124-129 (same in C6:127-133, C7:141-146,
+ * C8:171-176).  `router_bias` (fp32 [E]) may be NULL; `logits` (bf16 [T, E])
+ * may be NULL.  Needs H % 64 == 0, E % 16 == 0, 16 <= E <= 256, 1 <= k <= 8.
+ */
+MOE_API int moe_router_topk(const void* x, const void* router_weight, const float* router_bias, int T,
+                    int H, int E, int top_k, int norm_topk_prob, int32_t* topk_ids,
+                    float* topk_weights, void* logits, int32_t* status, cudaStream_t stream);
+
+/*
+ * Stable counting sort of R = T*k routing records by expert, restricted to
+ * experts [e_begin, e_begin + E_local) (all records when e_begin = 0 and
+ * E_local = E).  Outputs, all on the device:
+ *   counts[E_local], offsets[E_local + 1] (int32, offsets[0] = 0) and
+ *   optionally offsets64 (int64, the C9 `offsets` argument);
+ *   perm[p] = slot of the p-th record in expert order (stable: slot order
+ *   inside an expert), p < offsets[E_local];
+ *   inv[s] = position of slot s, or -1 for a record outside the range (may be NULL);
+ *   tiles[max_tiles][4] = {local expert, row_begin, row_end, 0} per 128-row
+ *   M-tile and num_tiles[0] = their count (the C9 _build_meta_data).
+ * Replaces C5/python/solution.py:131-136 (torch.sort + bincount), the
+ * local-expert filter and stable sort of C6/python/solution.py:137-160, and
+ * C9/python/solution.py:142-159 (_build_meta_data), with no host sync.
+ * max_tiles must be >= moe_max_tiles(R, E_local).
+ */
+MOE_API size_t moe_sort_align_workspace_bytes(int R, int E_local);
+MOE_API int moe_max_tiles(int R, int E_local);
+MOE_API int moe_sort_align(const int32_t* topk_ids, int R, int E, int e_begin, int E_local,
+                   void* workspace, size_t workspace_bytes, int32_t* counts, int32_t* offsets,
+                   int64_t* offsets64, int32_t* perm, int32_t* inv, int32_t* tiles,
+                   int max_tiles, int32_t* num_tiles, int32_t* status, cudaStream_t stream);
+
+/*
+ * Tile table from caller-given int64 offsets[E + 1] (the C9 interface, where
+ * the caller already holds sorted rows).  Replaces
+ * C9/python/solution.py:142-159.
+ */
+MOE_API int moe_tiles_from_offsets(const int64_t* offsets, int E, int32_t* tiles, int max_tiles,
+                           int32_t* num_tiles, int32_t* status, cudaStream_t stream);
+
+/*
+ * dst[p, :] = src[index[p] / index_div, :] for p < R, and p < count[0] when
+ * `count` (a device int32, e.g. offsets + E_local) is not NULL; rows of H bf16.
+ * With index = perm and index_div = k this is the permuted gather
+ * x_flat[token_ids_rep[perm]] of C5/python/solution.py:135-137.  H % 8 == 0.
+ */
+MOE_API int moe_gather_rows(const void* src, int src_rows, const int32_t* index, int R,
+                    const int32_t* count, int index_div, int H, void* dst, int32_t* status,
+                    cudaStream_t stream);
+
+/*
+ * Grouped gate/up GEMM with the SwiGLU fused in the epilogue:
+ *   h[r, :] = silu(A[r] @ w_gate[e]^T) * (A[r] @ w_up[e]^T) for rows r of tile
+ *   entries {e, row_begin, row_end}; A is [M, H], h is [M, I].
+ * Replaces the gate/up grouped matmuls and silu*mul of
+ * C9/python/solution.py:218-220 (and C5/python/solution.py:79-80 per expert).
+ * Needs H % 64 == 0, I % 64 == 0.
+ */
+MOE_API int moe_grouped_w13_swiglu(const void* sorted_x, int M, const int32_t* tiles,
+                           const int32_t* num_tiles, int max_tiles, const void* w_gate,
+                           const void* w_up, int E, int H, int I, void* h, int32_t* status,
+                           cudaStream_t stream);
+
+/*
+ * Grouped down GEMM with a scatter/scale epilogue:
+ *   out[m(r), :] = s(m(r)) * (h[r] @ w_down[e]^T), m = row_map (identity when
+ *   NULL), s = slot_scale (1 when NULL).  With row_map = perm and slot_scale =
+ *   the flat top-k weights, each slot's weighted expert output lands in row
+ *   n*k + j.  Replaces C9/python/solution.py:221 and the weight scale of
+ *   C5/python/solution.py:158.  Needs I % 64 == 0, H % 128 == 0.
+ */
+MOE_API int moe_grouped_w2(const void* h, int M, const int32_t* tiles, const int32_t* num_tiles,
+                   int max_tiles, const void* w_down, int E, int H, int I,
+                   const int32_t* row_map, const float* slot_scale, void* out, int out_rows,
+                   int32_t* status, cudaStream_t stream);
+
+/*
+ * y[n, :] = sum_j w_j * rows[src_j, :], j < k, fp32 accumulate in slot order:
+ * src_j = slot_src[n*k+j] (n*k+j when NULL), w_j = slot_w[n*k+j] (1 when NULL);
+ * slots with src_j < 0 or an expert id ids[n*k+j] outside [e_begin, e_end)
+ * (no filter when ids is NULL) add nothing.  Replaces the index_add_
+ * un-permute of C5/python/solution.py:160, C6/python/solution.py:175-176,
+ * C7/python/solution.py:259-261 and C8/python/solution.py:221-224.
+ */
+MOE_API int moe_combine(const void* rows, int n_rows, const int32_t* slot_src, const float* slot_w,
+                const int32_t* ids, int e_begin, int e_end, int T, int k, int H, void* y,
+                int32_t* status, cudaStream_t stream);
+
+/*
+ * Whole single-device MoE layer, PermutedSparseMoE.forward
+ * (C5/python/solution.py:108-161): router -> sort -> gather -> w13+SwiGLU ->
+ * w2 (weighted, to slot rows) -> k-way combine into y [T, H].  Eight kernel
+ * launches, no host sync.  workspace >= moe_layer_workspace_bytes(...).
+ */
+MOE_API size_t moe_layer_workspace_bytes(int T, int H, int I, int E, int top_k);
+MOE_API int moe_layer_forward(const void* x, const void* router_weight, const float* router_bias,
+                      const void* w_gate, const void* w_up, const void* w_down, int T, int H,
+                      int I, int E, int top_k, int norm_topk_prob, void* workspace,
+                      size_t workspace_bytes, void* y, int32_t* status, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

@@ -1,0 +1,197 @@
+// extern "C" entry points declared in include/moe_b200.h.
+#include "../../include/moe_b200.h"
+#include "internal.h"
+
+using namespace moe;
+
+namespace {
+
+constexpr size_t kAlign = 256;
+
+size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
+
+// Carves aligned sub-buffers out of the caller's workspace.
+struct Carver {
+  uint8_t* base;
+  size_t used = 0;
+  explicit Carver(void* p) : base(static_cast<uint8_t*>(p)) {}
+  template <class T>
+  T* take(size_t count) {
+    T* p = reinterpret_cast<T*>(base + used);
+    used = align_up(used + count * sizeof(T));
+    return p;
+  }
+};
+
+struct LayerPlan {
+  long long R;
+  int max_tiles;
+  size_t sort_ws;
+};
+
+LayerPlan plan_layer(int T, int E, int k) {
+  LayerPlan p;
+  p.R = static_cast<long long>(T) * k;
+  p.max_tiles = max_tiles_bound(p.R, E, MOE_BLOCK_M);
+  p.sort_ws = sort_workspace_bytes(static_cast<int>(p.R), E);
+  return p;
+}
+
+template <class Body>
+size_t layer_layout(int T, int H, int I, int E, int k, void* ws, Body&& body) {
+  const LayerPlan p = plan_layer(T, E, k);
+  Carver c(ws);
+  int* ids = c.take<int>(p.R);
+  float* w = c.take<float>(p.R);
+  void* sort_ws = c.take<uint8_t>(p.sort_ws);
+  int* counts = c.take<int>(E);
+  int* offsets = c.take<int>(E + 1);
+  int* perm = c.take<int>(p.R);
+  int4* tiles = c.take<int4>(p.max_tiles);
+  int* num_tiles = c.take<int>(1);
+  void* sorted_x = c.take<__nv_bfloat16>(p.R * H);
+  void* h = c.take<__nv_bfloat16>(p.R * I);
+  void* slots = c.take<__nv_bfloat16>(p.R * H);
+  body(p, ids, w, sort_ws, counts, offsets, perm, tiles, num_tiles, sorted_x, h, slots);
+  return c.used;
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_abi_version(void) { return MOE_B200_ABI_VERSION; }
+
+const char* moe_error_string(int code) {
+  switch (code) {
+    case kRcOk: return "ok";
+    case kRcBadArgument: return "bad argument (null pointer, negative or inconsistent size, misaligned buffer)";
+    case kRcUnsupported: return "shape not supported by these kernels";
+    case kRcCudaError: return "CUDA runtime error while launching";
+    case kRcTensorMap: return "tensor map encoding failed";
+    case kRcWorkspace: return "workspace smaller than required";
+    case kErrTimeoutFull: return "device: MMA warp timed out waiting for a shared-memory stage";
+    case kErrTimeoutEmpty: return "device: TMA producer timed out waiting for a free stage";
+    case kErrTimeoutAccFull: return "device: epilogue timed out waiting for the accumulator";
+    case kErrTimeoutAccEmpty: return "device: MMA warp timed out waiting for the epilogue";
+    case kErrBadExpert: return "device: expert id out of range";
+    case kErrBadRow: return "device: row index out of range";
+    default: return "unknown code";
+  }
+}
+
+int moe_router_topk(const void* x, const void* router_weight, const float* router_bias, int T,
+                    int H, int E, int top_k, int norm_topk_prob, int32_t* topk_ids,
+                    float* topk_weights, void* logits, int32_t* status, cudaStream_t stream) {
+  return launch_router(x, router_weight, router_bias, T, H, E, top_k, norm_topk_prob, topk_ids,
+                       topk_weights, logits, status, stream);
+}
+
+size_t moe_sort_align_workspace_bytes(int R, int E_local) {
+  if (R < 0 || E_local <= 0) return 0;
+  return sort_workspace_bytes(R, E_local);
+}
+
+int moe_max_tiles(int R, int E_local) {
+  if (R < 0 || E_local <= 0) return 0;
+  return max_tiles_bound(R, E_local, MOE_BLOCK_M);
+}
+
+int moe_sort_align(const int32_t* topk_ids, int R, int E, int e_begin, int E_local,
+                   void* workspace, size_t workspace_bytes, int32_t* counts, int32_t* offsets,
+                   int64_t* offsets64, int32_t* perm, int32_t* inv, int32_t* tiles,
+                   int max_tiles, int32_t* num_tiles, int32_t* status, cudaStream_t stream) {
+  if ((R > 0 && (topk_ids == nullptr || perm == nullptr)) || counts == nullptr ||
+      offsets == nullptr || workspace == nullptr || tiles == nullptr || num_tiles == nullptr)
+    return kRcBadArgument;
+  if (R < 0 || E_local <= 0 || max_tiles < moe_max_tiles(R, E_local)) return kRcBadArgument;
+  if (workspace_bytes < sort_workspace_bytes(R, E_local)) return kRcWorkspace;
+  return launch_sort_align(topk_ids, R, E, e_begin, E_local, MOE_BLOCK_M, workspace, counts,
+                           offsets, reinterpret_cast<long long*>(offsets64), perm, inv,
+                           reinterpret_cast<int4*>(tiles), max_tiles, num_tiles, status, stream);
+}
+
+int moe_tiles_from_offsets(const int64_t* offsets, int E, int32_t* tiles, int max_tiles,
+                           int32_t* num_tiles, int32_t* status, cudaStream_t stream) {
+  if (offsets == nullptr || tiles == nullptr || num_tiles == nullptr || max_tiles < 0)
+    return kRcBadArgument;
+  return launch_tiles_from_offsets(reinterpret_cast<const long long*>(offsets), E, MOE_BLOCK_M,
+                                   reinterpret_cast<int4*>(tiles), max_tiles, num_tiles, status,
+                                   stream);
+}
+
+int moe_gather_rows(const void* src, int src_rows, const int32_t* index, int R,
+                    const int32_t* count, int index_div, int H, void* dst, int32_t* status,
+                    cudaStream_t stream) {
+  if (R > 0 && (src == nullptr || index == nullptr || dst == nullptr)) return kRcBadArgument;
+  return launch_gather_rows(src, src_rows, index, R, count, index_div, H, dst, status, stream);
+}
+
+int moe_grouped_w13_swiglu(const void* sorted_x, int M, const int32_t* tiles,
+                           const int32_t* num_tiles, int max_tiles, const void* w_gate,
+                           const void* w_up, int E, int H, int I, void* h, int32_t* status,
+                           cudaStream_t stream) {
+  return launch_w13_swiglu(sorted_x, M, reinterpret_cast<const int4*>(tiles), num_tiles, max_tiles,
+                           w_gate, w_up, E, H, I, h, status, stream);
+}
+
+int moe_grouped_w2(const void* h, int M, const int32_t* tiles, const int32_t* num_tiles,
+                   int max_tiles, const void* w_down, int E, int H, int I,
+                   const int32_t* row_map, const float* slot_scale, void* out, int out_rows,
+                   int32_t* status, cudaStream_t stream) {
+  return launch_w2(h, M, reinterpret_cast<const int4*>(tiles), num_tiles, max_tiles, w_down, E, H,
+                   I, row_map, slot_scale, out, out_rows, status, stream);
+}
+
+int moe_combine(const void* rows, int n_rows, const int32_t* slot_src, const float* slot_w,
+                const int32_t* ids, int e_begin, int e_end, int T, int k, int H, void* y,
+                int32_t* status, cudaStream_t stream) {
+  if (T > 0 && (rows == nullptr || y == nullptr)) return kRcBadArgument;
+  return launch_combine(rows, n_rows, slot_src, slot_w, ids, e_begin, e_end, T, k, H, y, status,
+                        stream);
+}
+
+size_t moe_layer_workspace_bytes(int T, int H, int I, int E, int top_k) {
+  if (T < 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0) return 0;
+  return layer_layout(T, H, I, E, top_k, nullptr, [](auto&&...) {});
+}
+
+int moe_layer_forward(const void* x, const void* router_weight, const float* router_bias,
+                      const void* w_gate, const void* w_up, const void* w_down, int T, int H,
+                      int I, int E, int top_k, int norm_topk_prob, void* workspace,
+                      size_t workspace_bytes, void* y, int32_t* status, cudaStream_t stream) {
+  if (x == nullptr || router_weight == nullptr || w_gate == nullptr || w_up == nullptr ||
+      w_down == nullptr || y == nullptr || workspace == nullptr || T < 0 || H <= 0 || I <= 0 ||
+      E <= 0 || top_k <= 0 || top_k > E)
+    return kRcBadArgument;
+  if (static_cast<long long>(T) * top_k > 0x7fffffffLL) return kRcUnsupported;
+  if (workspace_bytes < moe_layer_workspace_bytes(T, H, I, E, top_k)) return kRcWorkspace;
+  if (T == 0) return kRcOk;
+  int rc = kRcOk;
+  layer_layout(T, H, I, E, top_k, workspace,
+               [&](const LayerPlan& p, int* ids, float* w, void* sort_ws, int* counts,
+                   int* offsets, int* perm, int4* tiles, int* num_tiles, void* sorted_x, void* h,
+                   void* slots) {
+                 const int R = static_cast<int>(p.R);
+                 rc = launch_router(x, router_weight, router_bias, T, H, E, top_k, norm_topk_prob,
+                                    ids, w, nullptr, status, stream);
+                 if (rc == kRcOk)
+                   rc = launch_sort_align(ids, R, E, 0, E, MOE_BLOCK_M, sort_ws, counts, offsets,
+                                          nullptr, perm, nullptr, tiles, p.max_tiles, num_tiles,
+                                          status, stream);
+                 if (rc == kRcOk)
+                   rc = launch_gather_rows(x, T, perm, R, nullptr, top_k, H, sorted_x, status, stream);
+                 if (rc == kRcOk)
+                   rc = launch_w13_swiglu(sorted_x, R, tiles, num_tiles, p.max_tiles, w_gate, w_up,
+                                          E, H, I, h, status, stream);
+                 if (rc == kRcOk)
+                   rc = launch_w2(h, R, tiles, num_tiles, p.max_tiles, w_down, E, H, I, perm, w,
+                                  slots, R, status, stream);
+                 if (rc == kRcOk)
+                   rc = launch_combine(slots, R, nullptr, nullptr, nullptr, 0, E, T, top_k, H, y,
+                                       status, stream);
+               });
+  return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,204 @@
+// Host launchers for the tcgen05 kernels: tensor-map encoding, tile-width
+// selection, grid sizing (one persistent CTA per SM at most).
+#include <atomic>
+#include <mutex>
+
+#include "grouped_gemm.cuh"
+#include "internal.h"
+
+namespace moe {
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor map with 128-byte swizzle.  dims[0] is the contiguous extent in
+// elements; strides (bytes) are given for dims 1..rank-1.
+int make_map(CUtensorMap* m, const void* base, int rank, const cuuint64_t* dims,
+             const cuuint64_t* strides, const cuuint32_t* box) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return kRcTensorMap;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return kRcBadArgument;
+  for (int i = 0; i < rank - 1; ++i)
+    if ((strides[i] & 15u) != 0) return kRcBadArgument;
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
+                         const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kRcOk : kRcTensorMap;
+}
+
+// Row-major [rows, cols] operand, box [box_rows, 64].
+int map_2d(CUtensorMap* m, const void* base, long long rows, int cols, int box_rows) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+  return make_map(m, base, 2, dims, strides, box);
+}
+
+// Expert-stacked [E, rows, cols] weights, box [1, box_rows, 64].
+int map_3d(CUtensorMap* m, const void* base, int E, int rows, int cols, int box_rows) {
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(E)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 2,
+                                 static_cast<cuuint64_t>(rows) * static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows), 1u};
+  return make_map(m, base, 3, dims, strides, box);
+}
+
+constexpr int kMaxDevices = 64;
+
+int device_sms() {
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 148;
+  int v = cache[dev].load(std::memory_order_relaxed);
+  if (v <= 0) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0)
+      v = 148;
+    cache[dev].store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
+template <int BN, int EPI, int STAGES>
+int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                const GemmArgs& args, long long work_units, cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES>;
+  static std::atomic<uint64_t> attr_done{0};  // one bit per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kRcCudaError;
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((attr_done.load(std::memory_order_acquire) & bit) == 0) {
+    if (cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, STAGES>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) != cudaSuccess)
+      return kRcCudaError;
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const long long sms = device_sms();
+  const int grid = static_cast<int>(work_units < sms ? work_units : sms);
+  if (grid <= 0) return kRcOk;
+  grouped_gemm_kernel<BN, EPI, STAGES><<<grid, 256, L::kTotal, stream>>>(a, b0, b1, args);
+  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+GemmArgs blank_args(int* status) {
+  GemmArgs g{};
+  g.status = status;
+  g.top_k = 1;
+  g.norm_topk_prob = 1;
+  return g;
+}
+
+}  // namespace
+
+int launch_router(const void* x, const void* wr, const float* bias, int T, int H, int E, int k,
+                  int norm_topk_prob, int* ids_out, float* w_out, void* logits_out, int* status,
+                  cudaStream_t stream) {
+  if (x == nullptr || wr == nullptr || ids_out == nullptr || w_out == nullptr || T < 0 || H <= 0)
+    return kRcBadArgument;
+  if ((H % kBK) != 0 || (E % 16) != 0 || E < 16 || E > 256 || k < 1 || k > kRouterMaxK || k > E)
+    return kRcUnsupported;
+  if (T == 0) return kRcOk;
+  CUtensorMap ma, mb;
+  int rc = map_2d(&ma, x, T, H, kBM);
+  if (rc == kRcOk) rc = map_3d(&mb, wr, 1, E, H, E);
+  if (rc != kRcOk) return rc;
+  GemmArgs g = blank_args(status);
+  g.max_tiles = (T + kBM - 1) / kBM;
+  g.n_tiles = 1;
+  g.num_kb = H / kBK;
+  g.b_rows = E;
+  g.a_rows = T;
+  g.num_experts = 1;
+  g.bias = bias;
+  g.top_k = k;
+  g.norm_topk_prob = norm_topk_prob;
+  g.ids_out = ids_out;
+  g.w_out = w_out;
+  g.logits_out = static_cast<__nv_bfloat16*>(logits_out);
+  return launch_gemm<256, kEpiRouter, 4>(ma, mb, mb, g, g.max_tiles, stream);
+}
+
+int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_tiles, int max_tiles,
+                      const void* w_gate, const void* w_up, int E, int H, int I, void* h_out,
+                      int* status, cudaStream_t stream) {
+  if (a == nullptr || tiles == nullptr || num_tiles == nullptr || w_gate == nullptr ||
+      w_up == nullptr || h_out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0)
+    return kRcBadArgument;
+  if ((H % kBK) != 0 || (I % 64) != 0) return kRcUnsupported;
+  if (M == 0 || max_tiles == 0) return kRcOk;
+  const int bn = (I % 128 == 0) ? 256 : 128;
+  CUtensorMap ma, mg, mu;
+  int rc = map_2d(&ma, a, M, H, kBM);
+  if (rc == kRcOk) rc = map_3d(&mg, w_gate, E, I, H, bn / 2);
+  if (rc == kRcOk) rc = map_3d(&mu, w_up, E, I, H, bn / 2);
+  if (rc != kRcOk) return rc;
+  GemmArgs g = blank_args(status);
+  g.tiles = tiles;
+  g.num_tiles = num_tiles;
+  g.max_tiles = max_tiles;
+  g.n_tiles = I / (bn / 2);
+  g.num_kb = H / kBK;
+  g.b_rows = bn;
+  g.a_rows = M;
+  g.num_experts = E;
+  g.out = static_cast<__nv_bfloat16*>(h_out);
+  g.out_ld = I;
+  g.out_rows = M;
+  const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
+  return bn == 256 ? launch_gemm<256, kEpiSwiGLU, 4>(ma, mg, mu, g, units, stream)
+                   : launch_gemm<128, kEpiSwiGLU, 6>(ma, mg, mu, g, units, stream);
+}
+
+int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
+              const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
+              void* out, int out_rows, int* status, cudaStream_t stream) {
+  if (h == nullptr || tiles == nullptr || num_tiles == nullptr || w_down == nullptr ||
+      out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0 || out_rows < 0)
+    return kRcBadArgument;
+  if ((I % kBK) != 0 || (H % 128) != 0) return kRcUnsupported;
+  if (M == 0 || max_tiles == 0) return kRcOk;
+  const int bn = (H % 256 == 0) ? 256 : 128;
+  CUtensorMap ma, md;
+  int rc = map_2d(&ma, h, M, I, kBM);
+  if (rc == kRcOk) rc = map_3d(&md, w_down, E, H, I, bn);
+  if (rc != kRcOk) return rc;
+  GemmArgs g = blank_args(status);
+  g.tiles = tiles;
+  g.num_tiles = num_tiles;
+  g.max_tiles = max_tiles;
+  g.n_tiles = H / bn;
+  g.num_kb = I / kBK;
+  g.b_rows = bn;
+  g.a_rows = M;
+  g.num_experts = E;
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.out_ld = H;
+  g.out_rows = out_rows;
+  g.row_map = row_map;
+  g.row_scale = row_scale;
+  const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
+  return bn == 256 ? launch_gemm<256, kEpiStore, 4>(ma, md, md, g, units, stream)
+                   : launch_gemm<128, kEpiStore, 6>(ma, md, md, g, units, stream);
+}
+
+}  // namespace moe

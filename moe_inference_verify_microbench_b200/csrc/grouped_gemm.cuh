@@ -1,0 +1,389 @@
+// Persistent tcgen05 grouped GEMM over ragged per-expert row blocks.
+//
+// Replaces the reference's per-expert loop (C5/python/solution.py:142-157)
+// and its Triton grouped_matmul_kernel (C9/python/solution.py:58-129).
+//
+// Work unit: one (M-tile, N-tile) pair.  An M-tile is 128 consecutive rows of
+// the A operand that all belong to one expert (tile table entry
+// {expert, row_begin, row_end}); rows past row_end inside the 128-row box are
+// computed but never stored.  The tile table lives in device memory and its
+// length is read on the device, so no host synchronisation is needed between
+// the sort and the GEMM.
+//
+// CTA layout (256 threads, one CTA per SM, grid = min(#SMs, #work units)):
+//   warp 0      TMA producer: A box [128 x 64] + B box [BN x 64] per stage
+//   warp 1      MMA issuer: 4 x tcgen05.mma (M=128, N=BN, K=16) per stage
+//   warp 2      tensor-memory allocator (2 accumulators of BN fp32 columns)
+//   warps 4..7  epilogue: tcgen05.ld of its 32 TMEM lanes -> registers -> HBM
+// Shared-memory stages are released by tcgen05.commit; the two accumulators
+// let the epilogue of tile i overlap the main loop of tile i+1.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace moe {
+
+enum EpiKind : int {
+  kEpiSwiGLU = 0,  // out[row, nt*BN/2 + c] = silu(acc[c]) * acc[BN/2 + c]
+  kEpiStore = 1,   // out[map(row), nt*BN + c] = scale(map(row)) * acc[c]
+  kEpiRouter = 2,  // per row: bf16 logits -> top-k -> softmax
+};
+
+struct GemmArgs {
+  const int4* tiles;     // [max_tiles] {expert, row_begin, row_end, 0}; null = dense rows
+  const int* num_tiles;  // device count of valid tile entries; null = max_tiles
+  int max_tiles;         // host bound on the tile count (grid sizing / clamp)
+  int n_tiles;           // N-tiles per M-tile
+  int num_kb;            // K / 64
+  int b_rows;            // rows of B per stage (BN, or E for the router)
+  int a_rows;            // rows of the A operand (bounds check / dense tiling)
+  int num_experts;       // experts addressed by the tile table (bounds check)
+  // kEpiSwiGLU / kEpiStore
+  __nv_bfloat16* out;
+  int out_ld;            // elements between output rows
+  int out_rows;          // output rows (bounds check)
+  const int* row_map;    // kEpiStore: out row = row_map[row] (null = identity)
+  const float* row_scale;  // kEpiStore: multiplier indexed by the mapped row (null = 1)
+  // kEpiRouter
+  const float* bias;     // [E] fp32 added before bf16 rounding (null = none)
+  int top_k;
+  int norm_topk_prob;
+  int* ids_out;          // [T, k] int32
+  float* w_out;          // [T, k] fp32
+  __nv_bfloat16* logits_out;  // [T, E] bf16 (null = not written)
+  int* status;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kRouterMaxK = 8;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kTotal = 1024 + STAGES * kStageBytes + kBarrierBytes;
+};
+
+__device__ __forceinline__ int4 load_tile(const GemmArgs& a, int mt) {
+  if (a.tiles != nullptr) return a.tiles[mt];
+  const int r0 = mt * kBM;
+  return make_int4(0, r0, min(a.a_rows, r0 + kBM), 0);
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+// Top-k insertion keeping (value desc, expert id asc): the reference's
+// torch.topk with ties broken toward the lower expert id.
+__device__ __forceinline__ void topk_insert(float (&v)[kRouterMaxK], int (&id)[kRouterMaxK],
+                                            float cv, int ci) {
+#pragma unroll
+  for (int i = 0; i < kRouterMaxK; ++i) {
+    const bool better = (cv > v[i]) || (cv == v[i] && ci < id[i]);
+    const float tv = better ? v[i] : cv;
+    const int ti = better ? id[i] : ci;
+    v[i] = better ? cv : v[i];
+    id[i] = better ? ci : id[i];
+    cv = tv;
+    ci = ti;
+  }
+}
+
+template <int BN, int EPI, int STAGES>
+__global__ void __launch_bounds__(256, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB0,
+                        const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
+  using L = GemmSmem<BN, STAGES>;
+  constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of 2");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * L::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * L::kBBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB0);
+    if (EPI == kEpiSwiGLU) tma_prefetch_desc(&tmB1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  int num_tiles = args.num_tiles != nullptr ? *args.num_tiles : args.max_tiles;
+  num_tiles = max(0, min(num_tiles, args.max_tiles));
+  const int total = num_tiles * args.n_tiles;
+  const uint32_t stage_tx = static_cast<uint32_t>(L::kABytes + args.b_rows * kBK * 2);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
+        const int mt = w / args.n_tiles;
+        const int nt = w - mt * args.n_tiles;
+        const int4 t = load_tile(args, mt);
+        if (t.x < 0 || t.x >= args.num_experts || t.y < 0 || t.z > args.a_rows || t.y >= t.z) {
+          record_status(args.status, t.x < 0 || t.x >= args.num_experts ? kErrBadExpert : kErrBadRow);
+          *abort_flag = 1;
+          break;
+        }
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, args.status, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], stage_tx);
+          tma_load_2d(sA + s * L::kABytes, &tmA, &full[s], kb * kBK, t.y);
+          uint8_t* b = sB + s * L::kBBytes;
+          if (EPI == kEpiSwiGLU) {
+            tma_load_3d(b, &tmB0, &full[s], kb * kBK, nt * (BN / 2), t.x);
+            tma_load_3d(b + L::kBBytes / 2, &tmB1, &full[s], kb * kBK, nt * (BN / 2), t.x);
+          } else {
+            tma_load_3d(b, &tmB0, &full[s], kb * kBK, nt * BN, t.x);
+          }
+          ++issued;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Let every copy still in flight land before the CTA exits.
+        const uint32_t first = issued > STAGES ? issued - STAGES : 0u;
+        for (uint32_t i = first; i < issued; ++i) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1u)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      const uint32_t idesc = idesc_bf16_f32(kBM, static_cast<uint32_t>(args.b_rows));
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < total; w += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_ph = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag, args.status, kErrTimeoutAccEmpty))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, args.status, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * L::kABytes);
+          const uint32_t b0 = smem_u32(sB + s * L::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            tc_mma_bf16(d, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32), idesc,
+                        (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) tc_commit(&acc_full[acc]);
+      }
+      // Every MMA issued by this thread has finished once `drain` completes.
+      tc_commit(drain);
+      const unsigned long long t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+    }
+  } else if (warp >= 4) {
+    // -------------------------------------------------------------- epilogue
+    const int q = warp - 4;  // TMEM lane quarter owned by this warp
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    int it = 0;
+    for (int w = blockIdx.x; w < total; w += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_ph = (it >> 1) & 1;
+      const int mt = w / args.n_tiles;
+      const int nt = w - mt * args.n_tiles;
+      const int4 t = load_tile(args, mt);
+      bool ok = mbar_wait(&acc_full[acc], acc_ph, abort_flag, args.status, kErrTimeoutAccFull);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int row = t.y + q * 32 + lane;
+      const bool valid = row < t.z;
+      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
+
+      if constexpr (EPI == kEpiSwiGLU) {
+        __nv_bfloat16* orow = args.out + static_cast<size_t>(row) * args.out_ld + nt * (BN / 2);
+        const bool st = valid && row < args.out_rows;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tb + c0, g);
+          tmem_ld32(tb + BN / 2 + c0, u);
+          tc_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float g0 = __uint_as_float(g[2 * j]), g1 = __uint_as_float(g[2 * j + 1]);
+            const float u0 = __uint_as_float(u[2 * j]), u1 = __uint_as_float(u[2 * j + 1]);
+            pk[j] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+          }
+          if (st) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          }
+        }
+      } else if constexpr (EPI == kEpiStore) {
+        int orow_idx = row;
+        float scale = 1.0f;
+        bool st = valid;
+        if (st) {
+          if (args.row_map != nullptr) orow_idx = args.row_map[row];
+          if (orow_idx < 0 || orow_idx >= args.out_rows) {
+            record_status(args.status, kErrBadRow);
+            st = false;
+          } else if (args.row_scale != nullptr) {
+            scale = args.row_scale[orow_idx];
+          }
+        }
+        __nv_bfloat16* orow = args.out + static_cast<size_t>(st ? orow_idx : 0) * args.out_ld + nt * BN;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tb + c0, r);
+          tc_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            pk[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * scale, __uint_as_float(r[2 * j + 1]) * scale);
+          if (st) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          }
+        }
+      } else {
+        // Router: the row's E logits -> bf16 -> top-k (value desc, id asc) -> softmax.
+        const int E = args.b_rows;
+        float tv[kRouterMaxK];
+        int ti[kRouterMaxK];
+#pragma unroll
+        for (int i = 0; i < kRouterMaxK; ++i) {
+          tv[i] = -INFINITY;
+          ti[i] = 0x7fffffff;
+        }
+        float run_max = -INFINITY, run_sum = 0.0f;  // softmax over all E (norm_topk_prob=False)
+#pragma unroll 1
+        for (int c0 = 0; c0 < E; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(tb + c0, r);
+          tc_wait_ld();
+          float lv[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float v = __uint_as_float(r[j]);
+            if (args.bias != nullptr) v += args.bias[c0 + j];
+            lv[j] = bf16_round_f(v);
+          }
+          if (valid && args.logits_out != nullptr) {
+            uint4* dst = reinterpret_cast<uint4*>(args.logits_out + static_cast<size_t>(row) * E + c0);
+            dst[0] = make_uint4(pack_bf16x2(lv[0], lv[1]), pack_bf16x2(lv[2], lv[3]),
+                                pack_bf16x2(lv[4], lv[5]), pack_bf16x2(lv[6], lv[7]));
+            dst[1] = make_uint4(pack_bf16x2(lv[8], lv[9]), pack_bf16x2(lv[10], lv[11]),
+                                pack_bf16x2(lv[12], lv[13]), pack_bf16x2(lv[14], lv[15]));
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            topk_insert(tv, ti, lv[j], c0 + j);
+            if (!args.norm_topk_prob) {
+              const float m = fmaxf(run_max, lv[j]);
+              run_sum = run_sum * expf(run_max - m) + expf(lv[j] - m);
+              run_max = m;
+            }
+          }
+        }
+        if (valid) {
+          const int k = args.top_k;
+          float den = 0.0f, ref = tv[0];
+          if (args.norm_topk_prob) {
+#pragma unroll
+            for (int i = 0; i < kRouterMaxK; ++i)
+              if (i < k) den += expf(tv[i] - ref);
+          } else {
+            den = run_sum;
+            ref = run_max;
+          }
+          const float inv = 1.0f / den;
+#pragma unroll
+          for (int i = 0; i < kRouterMaxK; ++i) {
+            if (i < k) {
+              args.ids_out[static_cast<size_t>(row) * k + i] = ti[i];
+              args.w_out[static_cast<size_t>(row) * k + i] = expf(tv[i] - ref) * inv;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace moe

@@ -1,0 +1,51 @@
+// Internal launchers shared by the C-ABI layer (capi.cu).  Nothing here
+// crosses the library boundary.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include "ptx.cuh"
+
+namespace moe {
+
+// Host-side return codes of the C-ABI entry points.
+enum ReturnCode : int {
+  kRcOk = 0,
+  kRcBadArgument = -1,    // null pointer, negative size, inconsistent sizes
+  kRcUnsupported = -2,    // a shape this build's kernels do not handle
+  kRcCudaError = -3,      // a CUDA runtime call or launch failed
+  kRcTensorMap = -4,      // cuTensorMapEncodeTiled rejected a tensor map
+  kRcWorkspace = -5,      // caller workspace smaller than required
+};
+
+int sort_num_blocks(int R);
+size_t sort_workspace_bytes(int R, int E_local);
+int launch_sort_align(const int* ids, int R, int E, int e_begin, int E_local, int block_m,
+                      void* workspace, int* counts, int* offsets, long long* offsets64, int* perm,
+                      int* inv, int4* tiles, int max_tiles, int* num_tiles, int* status,
+                      cudaStream_t stream);
+int launch_tiles_from_offsets(const long long* offsets, int E, int block_m, int4* tiles,
+                              int max_tiles, int* num_tiles, int* status, cudaStream_t stream);
+
+int launch_gather_rows(const void* src, int src_rows, const int* idx, int R, const int* count,
+                       int idx_div, int H, void* dst, int* status, cudaStream_t stream);
+int launch_combine(const void* rows, int n_rows, const int* slot_src, const float* slot_w,
+                   const int* ids, int e_begin, int e_end, int T, int k, int H, void* y,
+                   int* status, cudaStream_t stream);
+
+int launch_router(const void* x, const void* wr, const float* bias, int T, int H, int E, int k,
+                  int norm_topk_prob, int* ids_out, float* w_out, void* logits_out, int* status,
+                  cudaStream_t stream);
+int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_tiles, int max_tiles,
+                      const void* w_gate, const void* w_up, int E, int H, int I, void* h_out,
+                      int* status, cudaStream_t stream);
+int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
+              const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
+              void* out, int out_rows, int* status, cudaStream_t stream);
+
+inline int max_tiles_bound(long long R, int E, int block_m) {
+  return static_cast<int>((R + block_m - 1) / block_m + E);
+}
+
+}  // namespace moe

@@ -1,0 +1,123 @@
+// Row movement kernels: the permutation gather and the top-k combine.
+//
+// gather_rows   dst[p] = src[idx[p] / idx_div], p < min(R, *count)  (C5:135-137 gather
+//               x_flat[token_ids_rep[perm]]; C7:167, C7:227 re-sort of received rows)
+// combine_rows  y[n] = sum_j  w_j * rows[src_j]               (C5:158-160
+//               weight scale + index_add_, C7:259-261, C8:221-224)
+//               with src_j = slot_src ? slot_src[n*k+j] : n*k+j and w_j = slot_w ?
+//               slot_w[n*k+j] : 1; a slot is skipped when src_j < 0 or when its
+//               expert id (ids[n*k+j]) lies outside [e_begin, e_end).
+//
+// Both are HBM-bound copies: one warp per row, 16-byte vector accesses, fp32
+// accumulation of the k contributions in slot order (deterministic, unlike
+// the atomic index_add_ of the reference on CUDA).
+#include "internal.h"
+
+namespace moe {
+
+constexpr int kRowsThreads = 256;
+constexpr int kRowsWarps = kRowsThreads / 32;
+
+__global__ void __launch_bounds__(kRowsThreads) gather_rows(const uint4* __restrict__ src,
+                                                            int src_rows,
+                                                            const int* __restrict__ idx, int R,
+                                                            const int* __restrict__ count,
+                                                            int idx_div, int vec_per_row,
+                                                            uint4* __restrict__ dst, int* status) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = count != nullptr ? min(R, *count) : R;
+  for (int p = blockIdx.x * kRowsWarps + warp; p < rows; p += gridDim.x * kRowsWarps) {
+    const int s = idx[p] / idx_div;
+    if (s < 0 || s >= src_rows) {
+      if (lane == 0) record_status(status, kErrBadRow);
+      continue;
+    }
+    const uint4* a = src + static_cast<size_t>(s) * vec_per_row;
+    uint4* b = dst + static_cast<size_t>(p) * vec_per_row;
+    for (int v = lane; v < vec_per_row; v += 32) b[v] = __ldg(a + v);
+  }
+}
+
+__device__ __forceinline__ void acc_bf16x8(float (&acc)[8], const uint4& v, float w) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    acc[2 * i] = fmaf(w, f.x, acc[2 * i]);
+    acc[2 * i + 1] = fmaf(w, f.y, acc[2 * i + 1]);
+  }
+}
+
+__global__ void __launch_bounds__(kRowsThreads) combine_rows(
+    const uint4* __restrict__ rows, int n_rows, const int* __restrict__ slot_src,
+    const float* __restrict__ slot_w, const int* __restrict__ ids, int e_begin, int e_end, int T,
+    int k, int vec_per_row, uint4* __restrict__ y, int* status) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int n = blockIdx.x * kRowsWarps + warp; n < T; n += gridDim.x * kRowsWarps) {
+    // Resolve the k source rows (lane j < k holds slot j).
+    int src = -1;
+    float w = 0.0f;
+    if (lane < k) {
+      const int s = n * k + lane;
+      src = slot_src != nullptr ? slot_src[s] : s;
+      w = slot_w != nullptr ? slot_w[s] : 1.0f;
+      if (ids != nullptr) {
+        const int e = ids[s];
+        if (e < e_begin || e >= e_end) src = -1;
+      }
+      if (src >= n_rows) {
+        record_status(status, kErrBadRow);
+        src = -1;
+      }
+    }
+    for (int v0 = 0; v0 < vec_per_row; v0 += 32) {
+      const int v = v0 + lane;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < k; ++j) {
+        const int sj = __shfl_sync(0xffffffffu, src, j);
+        const float wj = __shfl_sync(0xffffffffu, w, j);
+        if (sj >= 0 && v < vec_per_row) acc_bf16x8(acc, __ldg(rows + static_cast<size_t>(sj) * vec_per_row + v), wj);
+      }
+      if (v < vec_per_row) {
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        y[static_cast<size_t>(n) * vec_per_row + v] = o;
+      }
+    }
+  }
+}
+
+static int rows_grid(long long rows) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long want = (rows + kRowsWarps - 1) / kRowsWarps;
+  const long long cap = static_cast<long long>(sms) * 8;
+  return static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
+}
+
+int launch_gather_rows(const void* src, int src_rows, const int* idx, int R, const int* count,
+                       int idx_div, int H, void* dst, int* status, cudaStream_t stream) {
+  if (R < 0 || H <= 0 || idx_div <= 0 || (H % 8) != 0) return kRcBadArgument;
+  if (R == 0) return kRcOk;
+  gather_rows<<<rows_grid(R), kRowsThreads, 0, stream>>>(static_cast<const uint4*>(src), src_rows,
+                                                         idx, R, count, idx_div, H / 8,
+                                                         static_cast<uint4*>(dst), status);
+  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+int launch_combine(const void* rows, int n_rows, const int* slot_src, const float* slot_w,
+                   const int* ids, int e_begin, int e_end, int T, int k, int H, void* y,
+                   int* status, cudaStream_t stream) {
+  if (T < 0 || k <= 0 || k > 32 || H <= 0 || (H % 8) != 0) return kRcBadArgument;
+  if (T == 0) return kRcOk;
+  combine_rows<<<rows_grid(T), kRowsThreads, 0, stream>>>(
+      static_cast<const uint4*>(rows), n_rows, slot_src, slot_w, ids, e_begin, e_end, T, k, H / 8,
+      static_cast<uint4*>(y), status);
+  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+}  // namespace moe

@@ -1,0 +1,245 @@
+// Token -> expert sort and tile alignment, without any host synchronisation.
+//
+// Replaces the reference's argsort/bincount/offset construction
+// (C5/python/solution.py:131-136, C6/python/solution.py:137-160,
+// C7/python/solution.py:160-164,224-226) and the C9 tile metadata
+// (C9/python/solution.py:142-159, which needs a host sync for its
+// repeat_interleave).
+//
+// Three launches over R = T*k routing records (flat slot index s = n*k + j):
+//   1. sa_hist     per-CTA expert histograms of a contiguous record chunk
+//   2. sa_scan     one CTA: per-expert counts, offsets[E+1], the per-CTA base of
+//                  every expert, and the 128-row tile table
+//   3. sa_scatter  per CTA, a stable rank of each record inside its expert
+//                  (warp match + per-warp counts), giving perm[p] = s and inv[s] = p
+// The permutation is stable: records of one expert keep increasing slot
+// order, i.e. torch.sort(ids, stable=True) (C6:152, C8:181).
+//
+// Records whose expert lies outside [e_begin, e_begin + E_local) are left out
+// (inv = -1): that is the local-expert filter of the replicated-input
+// expert-parallel schedule (C6/python/solution.py:141-149).
+#include "internal.h"
+
+namespace moe {
+
+constexpr int kSortThreads = 256;
+constexpr int kSortItems = 16;  // records per thread per CTA chunk
+constexpr int kSortChunk = kSortThreads * kSortItems;
+
+int sort_num_blocks(int R) { return (R + kSortChunk - 1) / kSortChunk; }
+
+size_t sort_workspace_bytes(int R, int E_local) {
+  return static_cast<size_t>(sort_num_blocks(R)) * static_cast<size_t>(E_local) * sizeof(int) + 256;
+}
+
+__device__ __forceinline__ int local_expert(const int* ids, int r, int E, int e_begin, int E_local,
+                                            int* status) {
+  const int g = ids[r];
+  if (g < 0 || g >= E) {
+    record_status(status, kErrBadExpert);
+    return -1;
+  }
+  const int e = g - e_begin;
+  return (e >= 0 && e < E_local) ? e : -1;
+}
+
+__global__ void __launch_bounds__(kSortThreads) sa_hist(const int* __restrict__ ids, int R, int E,
+                                                        int e_begin, int E_local,
+                                                        int* __restrict__ hist, int* status) {
+  extern __shared__ int sh[];
+  for (int e = threadIdx.x; e < E_local; e += blockDim.x) sh[e] = 0;
+  __syncthreads();
+  const int base = blockIdx.x * kSortChunk;
+  const int end = min(R, base + kSortChunk);
+  for (int r = base + threadIdx.x; r < end; r += blockDim.x) {
+    const int e = local_expert(ids, r, E, e_begin, E_local, status);
+    if (e >= 0) atomicAdd(&sh[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E_local; e += blockDim.x)
+    hist[static_cast<size_t>(blockIdx.x) * E_local + e] = sh[e];
+}
+
+// Exclusive scan of one value per thread over a block of up to 1024 threads.
+__device__ int block_exclusive_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int s = lane < nw ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane < nw) warp_sums[lane] = s;  // inclusive warp prefix
+    if (lane == nw - 1) *total = s;
+  }
+  __syncthreads();
+  const int before = warp > 0 ? warp_sums[warp - 1] : 0;
+  const int res = before + x - v;
+  __syncthreads();
+  return res;
+}
+
+// Tile table from per-expert counts held by threads e < E (E <= blockDim.x).
+__device__ void write_tiles(int e, int E, int count, int offset, int block_m, int4* tiles,
+                            int max_tiles, int* num_tiles, int* warp_sums, int* total) {
+  const int nt = (e < E) ? (count + block_m - 1) / block_m : 0;
+  const int first = block_exclusive_scan(nt, warp_sums, total);
+  if (e < E) {
+    for (int t = 0; t < nt; ++t) {
+      const int slot = first + t;
+      if (slot < max_tiles) {
+        const int r0 = offset + t * block_m;
+        tiles[slot] = make_int4(e, r0, min(offset + count, r0 + block_m), 0);
+      }
+    }
+  }
+  if (threadIdx.x == 0) *num_tiles = min(*total, max_tiles);
+}
+
+__global__ void __launch_bounds__(1024) sa_scan(int* __restrict__ hist, int nblk, int E_local,
+                                                int block_m, int* __restrict__ counts,
+                                                int* __restrict__ offsets,
+                                                long long* __restrict__ offsets64,
+                                                int4* __restrict__ tiles, int max_tiles,
+                                                int* __restrict__ num_tiles) {
+  __shared__ int warp_sums[32];
+  __shared__ int total;
+  const int e = threadIdx.x;
+  int run = 0;
+  if (e < E_local) {
+    for (int b = 0; b < nblk; ++b) {
+      int* h = hist + static_cast<size_t>(b) * E_local + e;
+      const int c = *h;
+      *h = run;  // records of expert e in earlier chunks
+      run += c;
+    }
+  }
+  const int off = block_exclusive_scan(e < E_local ? run : 0, warp_sums, &total);
+  if (e < E_local) {
+    counts[e] = run;
+    offsets[e] = off;
+    if (offsets64 != nullptr) offsets64[e] = off;
+    for (int b = 0; b < nblk; ++b) hist[static_cast<size_t>(b) * E_local + e] += off;
+  }
+  if (e == 0) {
+    offsets[E_local] = total;
+    if (offsets64 != nullptr) offsets64[E_local] = total;
+  }
+  __syncthreads();
+  if (tiles != nullptr) write_tiles(e, E_local, run, off, block_m, tiles, max_tiles, num_tiles, warp_sums, &total);
+}
+
+__global__ void __launch_bounds__(kSortThreads) sa_scatter(const int* __restrict__ ids, int R, int E,
+                                                           int e_begin, int E_local,
+                                                           const int* __restrict__ hist,
+                                                           int* __restrict__ perm,
+                                                           int* __restrict__ inv, int* status) {
+  extern __shared__ int sm[];
+  int* base = sm;                       // [E_local] next free position per expert
+  int* wcnt = sm + E_local;             // [8][E_local] per-warp counts of this round
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kWarps = kSortThreads / 32;
+  for (int e = threadIdx.x; e < E_local; e += blockDim.x) {
+    base[e] = hist[static_cast<size_t>(blockIdx.x) * E_local + e];
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) wcnt[w * E_local + e] = 0;
+  }
+  __syncthreads();
+  const int chunk0 = blockIdx.x * kSortChunk;
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int round = 0; round < kSortItems; ++round) {
+    const int r = chunk0 + round * kSortThreads + threadIdx.x;
+    int e = -1;
+    if (r < R) e = local_expert(ids, r, E, e_begin, E_local, status);
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & lt_mask);
+    if (e >= 0 && rank == 0) wcnt[warp * E_local + e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int p = base[e] + rank;
+      for (int w = 0; w < warp; ++w) p += wcnt[w * E_local + e];
+      perm[p] = r;
+      if (inv != nullptr) inv[r] = p;
+    } else if (r < R && inv != nullptr) {
+      inv[r] = -1;
+    }
+    __syncthreads();
+    for (int x = threadIdx.x; x < E_local; x += blockDim.x) {
+      int add = 0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        add += wcnt[w * E_local + x];
+        wcnt[w * E_local + x] = 0;
+      }
+      base[x] += add;
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(1024) tiles_from_offsets(const long long* __restrict__ offsets,
+                                                           int E, int block_m,
+                                                           int4* __restrict__ tiles, int max_tiles,
+                                                           int* __restrict__ num_tiles,
+                                                           int* status) {
+  __shared__ int warp_sums[32];
+  __shared__ int total;
+  const int e = threadIdx.x;
+  int count = 0, off = 0;
+  if (e < E) {
+    const long long a = offsets[e], b = offsets[e + 1];
+    if (a < 0 || b < a || b > 0x7fffffffLL) {
+      record_status(status, kErrBadRow);
+    } else {
+      off = static_cast<int>(a);
+      count = static_cast<int>(b - a);
+    }
+  }
+  write_tiles(e, E, count, off, block_m, tiles, max_tiles, num_tiles, warp_sums, &total);
+}
+
+int launch_sort_align(const int* ids, int R, int E, int e_begin, int E_local, int block_m,
+                      void* workspace, int* counts, int* offsets, long long* offsets64, int* perm,
+                      int* inv, int4* tiles, int max_tiles, int* num_tiles, int* status,
+                      cudaStream_t stream) {
+  if (R < 0 || E <= 0 || E_local <= 0 || E_local > 1024 || e_begin < 0 || e_begin + E_local > E ||
+      block_m <= 0)
+    return kRcBadArgument;
+  const int nblk = sort_num_blocks(R);
+  int* hist = static_cast<int*>(workspace);
+  const size_t sh_hist = static_cast<size_t>(E_local) * sizeof(int);
+  const size_t sh_scatter = static_cast<size_t>(E_local) * (1 + kSortThreads / 32) * sizeof(int);
+  // E_local <= 1024 keeps sh_scatter <= 36 KB, inside the default 48 KB limit.
+  if (nblk > 0) {
+    sa_hist<<<nblk, kSortThreads, sh_hist, stream>>>(ids, R, E, e_begin, E_local, hist, status);
+  }
+  const int scan_threads = ((E_local + 31) / 32) * 32;
+  sa_scan<<<1, scan_threads, 0, stream>>>(hist, nblk, E_local, block_m, counts, offsets, offsets64,
+                                          tiles, max_tiles, num_tiles);
+  if (nblk > 0) {
+    sa_scatter<<<nblk, kSortThreads, sh_scatter, stream>>>(ids, R, E, e_begin, E_local, hist, perm,
+                                                           inv, status);
+  }
+  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+int launch_tiles_from_offsets(const long long* offsets, int E, int block_m, int4* tiles,
+                              int max_tiles, int* num_tiles, int* status, cudaStream_t stream) {
+  if (E <= 0 || E > 1024 || block_m <= 0) return kRcBadArgument;
+  const int threads = ((E + 31) / 32) * 32;
+  tiles_from_offsets<<<1, threads, 0, stream>>>(offsets, E, block_m, tiles, max_tiles, num_tiles,
+                                                status);
+  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+}  // namespace moe

@@ -1,0 +1,192 @@
+"""Expert-parallel MoE schedules over NCCL, with the call signatures of the
+reference's components:
+
+* ``EPSparseMoELean``  C6/python/solution.py:57-182 (exported by ``ep_lean`` as
+  ``EPSparseMoE``): replicated input, full router on every rank, local experts
+  only, ONE all_reduce of the [N, H] partial output.
+* ``EPSparseMoEPure``  C7/python/solution.py:65-269 (exported by ``ep_pure`` as
+  ``EPSparseMoE``): distinct tokens per rank; count all_to_all, dispatch
+  all_to_all of rows and expert ids, local grouped compute, combine
+  all_to_all, weighted k-way combine.
+* ``HybridMoE``        C8/python/solution.py:59-230: 1/tp stripe of the
+  TP-replicated input, the C7 core on the EP group, all_gather on the TP group.
+
+Experts are sharded contiguously: rank r owns [r*E/ep, (r+1)*E/ep)
+(C6:87-89, C7:96-98, C8:110-112).  Every rank issues the same collectives in
+the same order as the reference (C8:12-19), so the schedules compose with
+the reference's TP attention.  The local compute is the sm_100a kernel set of
+``ops``; the only host synchronisation is the split-size exchange that NCCL's
+variable all_to_all needs (the reference's ``.tolist()``, C7:199-200).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from . import ops
+from .dist_primer import all_to_all_variable
+from .experts import ExpertBank, SwiGLU_MLP, router_bias_of
+
+
+class CudaKernels:
+    """The kernel contract the schedules are written against (all sm_100a)."""
+
+    router_topk = staticmethod(ops.router_topk)
+    sort_align = staticmethod(ops.sort_align)
+    gather_rows = staticmethod(ops.gather_rows)
+    combine = staticmethod(ops.combine)
+
+    @staticmethod
+    def expert_compute(xs, s, w_gate, w_up, w_down, row_map=None, slot_scale=None, out_rows=None):
+        h = ops.grouped_w13_swiglu(xs, s.tiles, s.num_tiles, s.max_tiles, w_gate, w_up)
+        return ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, w_down, row_map=row_map,
+                              slot_scale=slot_scale, out_rows=out_rows)
+
+
+class _EPBase(nn.Module):
+    def __init__(self, hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob):
+        super().__init__()
+        assert num_experts % ep_size == 0, (
+            f"num_experts={num_experts} not divisible by ep_size={ep_size}")
+        self.hidden = hidden
+        self.intermediate = intermediate
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.ep_size = ep_size
+        self.ep_rank = ep_rank
+        self.norm_topk_prob = norm_topk_prob
+        self.experts_per_rank = num_experts // ep_size
+        self.expert_start = ep_rank * self.experts_per_rank
+        self.expert_end = self.expert_start + self.experts_per_rank
+        # REPLICATED router; SHARDED experts (C6:91-96).
+        self.gate = nn.Linear(hidden, num_experts, bias=False)
+        self.experts = nn.ModuleList(SwiGLU_MLP(hidden, intermediate)
+                                     for _ in range(self.experts_per_rank))
+        self._bank = ExpertBank()
+        self._kernels = CudaKernels
+
+    def _apply(self, fn, *args, **kwargs):
+        self._bank.invalidate()
+        return super()._apply(fn, *args, **kwargs)
+
+    def pack(self):
+        return self._bank.bind(self.experts)
+
+    @torch.no_grad()
+    def weight_loader(self, gate_weight, expert_gate_weights, expert_up_weights,
+                      expert_down_weights) -> None:
+        """Copy the replicated router and this rank's expert shard
+        (C6/python/solution.py:98-110)."""
+        self.gate.weight.data.copy_(gate_weight)
+        wg, wu, wd = self.pack()
+        for local_e in range(self.experts_per_rank):
+            global_e = self.expert_start + local_e
+            wg[local_e].copy_(expert_gate_weights[global_e])
+            wu[local_e].copy_(expert_up_weights[global_e])
+            wd[local_e].copy_(expert_down_weights[global_e])
+
+    def _route(self, x_flat):
+        return self._kernels.router_topk(x_flat, self.gate.weight, self.top_k, self.norm_topk_prob,
+                                         bias=router_bias_of(self.gate))[:2]
+
+
+class EPSparseMoELean(_EPBase):
+    """Replicated-input EP with one all_reduce (C6/python/solution.py:57-182)."""
+
+    def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int, ep_size: int,
+                 ep_rank: int, group: dist.ProcessGroup | None = None,
+                 norm_topk_prob: bool = True) -> None:
+        super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
+        self.group = group
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        K = self._kernels
+        shape = x.shape
+        x_flat = x.reshape(-1, shape[-1]).contiguous()
+        N, k = x_flat.shape[0], self.top_k
+        ids, w = self._route(x_flat)                                   # full router (C6:127-133)
+        s = K.sort_align(ids, self.num_experts, self.expert_start,     # local filter + stable sort
+                         self.experts_per_rank)                        # (C6:141-160)
+        count = s.offsets[self.experts_per_rank:]
+        xs = K.gather_rows(x_flat, s.perm, k, count=count)             # (C6:156)
+        wg, wu, wd = self.pack()
+        slots = K.expert_compute(xs, s, wg, wu, wd, row_map=s.perm,    # weighted, to slot rows
+                                 slot_scale=w.reshape(-1), out_rows=N * k)  # (C6:163-170)
+        partial = K.combine(slots, N, k, ids=ids.reshape(-1),          # (C6:175-176)
+                            e_range=(self.expert_start, self.expert_end))
+        dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)  # (C6:180)
+        return partial.reshape(shape)
+
+
+def dispatch_combine(mod: _EPBase, local_x: torch.Tensor, group) -> torch.Tensor:
+    """The all_to_all EP core shared by C7 (C7/python/solution.py:120-269) and
+    C8's MoE (C8/python/solution.py:171-224), on this rank's tokens."""
+    K = mod._kernels
+    N, k, E, epr = local_x.shape[0], mod.top_k, mod.num_experts, mod.experts_per_rank
+    ids, w = mod._route(local_x)                                       # local router (C7:141-146)
+    s = K.sort_align(ids, E, want_inv=True)                           # sort by global id (C7:162)
+    xs = K.gather_rows(local_x, s.perm, k)                            # (C7:167)
+    sorted_eids = ids.reshape(-1).index_select(0, s.perm.long())
+    bounds = s.offsets[0::epr].to(torch.int64)                        # per-destination splits
+    send = bounds[1:] - bounds[:-1]                                   # (C7:186-187)
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=group)                   # count exchange (C7:190)
+    send_l, recv_l = send.tolist(), recv.tolist()                     # host sync (C7:199-200)
+    recv_x = all_to_all_variable(xs, send_l, recv_l, group)           # dispatch (C7:201)
+    recv_e = all_to_all_variable(sorted_eids, send_l, recv_l, group)  # (C7:203)
+    n_recv = recv_x.shape[0]
+    wg, wu, wd = mod.pack()
+    if n_recv > 0:
+        s2 = K.sort_align(recv_e, E, mod.expert_start, epr)           # local re-sort (C7:224-226)
+        xs2 = K.gather_rows(recv_x, s2.perm, 1)
+        y_t = K.expert_compute(xs2, s2, wg, wu, wd, row_map=s2.perm,  # back to received order
+                               out_rows=n_recv)                       # (C7:231-236)
+    else:
+        y_t = recv_x.new_empty((0, local_x.shape[1]))
+    y_ret = all_to_all_variable(y_t, recv_l, send_l, group)           # combine (C7:258)
+    return K.combine(y_ret, N, k, slot_src=s.inv, slot_w=w.reshape(-1))  # weight + index_add_
+    # (C7:259-261)
+
+
+class EPSparseMoEPure(_EPBase):
+    """Pure EP: distinct tokens per rank, dispatch/combine all_to_all
+    (C7/python/solution.py:65-269).  The group is kept as ``ep_group`` (C7:93)."""
+
+    def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int, ep_size: int,
+                 ep_rank: int, group: dist.ProcessGroup | None = None,
+                 norm_topk_prob: bool = True) -> None:
+        super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
+        self.ep_group = group
+
+    def forward(self, local_x: torch.Tensor) -> torch.Tensor:
+        shape = local_x.shape
+        x_flat = local_x.reshape(-1, self.hidden).contiguous()
+        return dispatch_combine(self, x_flat, self.ep_group).reshape(shape)
+
+
+class HybridMoE(_EPBase):
+    """TP-scoped stripe/all_gather + EP-scoped dispatch/combine
+    (C8/python/solution.py:59-230)."""
+
+    def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int, tp_size: int,
+                 tp_rank: int, tp_group: dist.ProcessGroup | None, ep_size: int, ep_rank: int,
+                 ep_group: dist.ProcessGroup | None, norm_topk_prob: bool = True) -> None:
+        super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
+        self.tp_size = tp_size
+        self.tp_rank = tp_rank
+        self.tp_group = tp_group
+        self.ep_group = ep_group
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        x_flat = x.reshape(-1, self.hidden)
+        N_tp = x_flat.shape[0]
+        assert N_tp % self.tp_size == 0
+        local_N = N_tp // self.tp_size
+        local_x = x_flat[self.tp_rank * local_N:(self.tp_rank + 1) * local_N].contiguous()  # (C8:160)
+        local_y = dispatch_combine(self, local_x, self.ep_group)
+        y_flat = torch.empty((N_tp, self.hidden), dtype=local_y.dtype, device=local_y.device)
+        dist.all_gather_into_tensor(y_flat, local_y, group=self.tp_group)            # (C8:227)
+        return y_flat.reshape(shape)

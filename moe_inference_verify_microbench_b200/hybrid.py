@@ -1,0 +1,148 @@
+"""C8 drop-ins: ``HybridMoE`` (the hot path, in ``ep``) and ``HybridBlock``
+(C8/python/solution.py:235-325), the pre-norm decoder block
+``h = x + attn(norm(x)); y = h + moe(norm(h))`` that hosts it.
+
+The attention and RMSNorm here are a plain PyTorch harness with the
+reference's interfaces (C4 ``TPGQA``, C4/python/solution.py:169-276, and the
+``RMSNorm(hidden, eps)`` that C8 imports): GQA with tensor-parallel heads,
+KV-head replication when tp > n_kv_heads (C4:127), RoPE, causal SDPA and a
+row-parallel output projection closed by an all_reduce on the TP group
+(C1/python/solution.py:142).  They are not part of the optimised path.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+from torch import nn
+
+from .ep import HybridMoE
+
+__all__ = ["HybridMoE", "HybridBlock", "RMSNorm", "TPGQA"]
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, hidden: int, eps: float = 1e-6) -> None:
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(hidden))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)
+        return (xf * self.weight.float()).to(x.dtype)
+
+
+def _rope(x: torch.Tensor, base: float) -> torch.Tensor:
+    """Rotate-half RoPE on [B, T, heads, d]."""
+    T, d = x.shape[1], x.shape[-1]
+    inv = 1.0 / (base ** (torch.arange(0, d, 2, device=x.device, dtype=torch.float32) / d))
+    f = torch.outer(torch.arange(T, device=x.device, dtype=torch.float32), inv)
+    cos = torch.cat([f, f], -1).cos()[None, :, None, :]
+    sin = torch.cat([f, f], -1).sin()[None, :, None, :]
+    x1, x2 = x[..., : d // 2], x[..., d // 2:]
+    rot = torch.cat([-x2, x1], -1)
+    return (x.float() * cos + rot.float() * sin).to(x.dtype)
+
+
+class _ShardLoader(nn.Module):
+    """Holds one rank's shard and copies it out of the full weight."""
+
+    def __init__(self, weight: torch.Tensor, loader) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(weight)
+        self._loader = loader
+
+    @torch.no_grad()
+    def weight_loader(self, full_weight: torch.Tensor, shard_id: str | None = None) -> None:
+        self._loader(self.weight, full_weight, shard_id)
+
+
+class TPGQA(nn.Module):
+    """Tensor-parallel grouped-query attention with KV replication."""
+
+    def __init__(self, hidden: int, n_heads: int, n_kv_heads: int, head_dim: int,
+                 rope_base: float = 10000.0, tp_size: int = 1, tp_rank: int = 0,
+                 group: dist.ProcessGroup | None = None) -> None:
+        super().__init__()
+        assert n_heads % tp_size == 0
+        self.hidden, self.head_dim, self.rope_base = hidden, head_dim, rope_base
+        self.tp_size, self.tp_rank, self.group = tp_size, tp_rank, group
+        self.q_per_rank = n_heads // tp_size
+        self.kv_per_rank = max(1, n_kv_heads // tp_size)
+        if tp_size > n_kv_heads:
+            assert tp_size % n_kv_heads == 0
+            self.kv_first = tp_rank // (tp_size // n_kv_heads)
+        else:
+            assert n_kv_heads % tp_size == 0
+            self.kv_first = tp_rank * self.kv_per_rank
+        qd, kvd = self.q_per_rank * head_dim, self.kv_per_rank * head_dim
+
+        def load_qkv(w, full, shard_id):
+            if shard_id == "q":
+                w[:qd].copy_(full[tp_rank * qd:(tp_rank + 1) * qd])
+            else:
+                off = qd if shard_id == "k" else qd + kvd
+                r0 = self.kv_first * head_dim
+                w[off:off + kvd].copy_(full[r0:r0 + kvd])
+
+        def load_o(w, full, _):
+            w.copy_(full[:, tp_rank * qd:(tp_rank + 1) * qd])
+
+        self.qkv_proj = _ShardLoader(torch.empty(qd + 2 * kvd, hidden), load_qkv)
+        self.o_proj = _ShardLoader(torch.empty(hidden, qd), load_o)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        B, T, _ = x.shape
+        d = self.head_dim
+        qkv = F.linear(x, self.qkv_proj.weight)
+        qd, kvd = self.q_per_rank * d, self.kv_per_rank * d
+        q = qkv[..., :qd].reshape(B, T, self.q_per_rank, d)
+        k = qkv[..., qd:qd + kvd].reshape(B, T, self.kv_per_rank, d)
+        v = qkv[..., qd + kvd:].reshape(B, T, self.kv_per_rank, d)
+        q, k = _rope(q, self.rope_base), _rope(k, self.rope_base)
+        rep = self.q_per_rank // self.kv_per_rank
+        k = k.repeat_interleave(rep, dim=2)
+        v = v.repeat_interleave(rep, dim=2)
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                           is_causal=True)
+        o = o.transpose(1, 2).reshape(B, T, qd)
+        out = F.linear(o, self.o_proj.weight)
+        if self.tp_size > 1:
+            dist.all_reduce(out, group=self.group)
+        return out
+
+
+class HybridBlock(nn.Module):
+    """Pre-norm block under TP x DP x EP (C8/python/solution.py:235-325)."""
+
+    def __init__(self, hidden: int, intermediate: int, n_heads: int, n_kv_heads: int,
+                 head_dim: int, num_experts: int, top_k: int, tp_size: int, tp_rank: int,
+                 tp_group: dist.ProcessGroup | None, ep_size: int, ep_rank: int,
+                 ep_group: dist.ProcessGroup | None, norm_topk_prob: bool = True,
+                 rope_base: float = 10000.0, rms_eps: float = 1e-6) -> None:
+        super().__init__()
+        self.attn_norm = RMSNorm(hidden, eps=rms_eps)
+        self.attn = TPGQA(hidden, n_heads, n_kv_heads, head_dim, rope_base=rope_base,
+                          tp_size=tp_size, tp_rank=tp_rank, group=tp_group)
+        self.moe_norm = RMSNorm(hidden, eps=rms_eps)
+        self.moe = HybridMoE(hidden, intermediate, num_experts, top_k, tp_size, tp_rank, tp_group,
+                             ep_size, ep_rank, ep_group, norm_topk_prob)
+
+    @torch.no_grad()
+    def weight_loader(self, attn_norm_weight, q_weight, k_weight, v_weight, o_weight,
+                      moe_norm_weight, gate_weight, expert_gate_weights, expert_up_weights,
+                      expert_down_weights) -> None:
+        self.attn_norm.weight.data.copy_(attn_norm_weight)
+        self.attn.qkv_proj.weight_loader(q_weight, "q")
+        self.attn.qkv_proj.weight_loader(k_weight, "k")
+        self.attn.qkv_proj.weight_loader(v_weight, "v")
+        self.attn.o_proj.weight_loader(o_weight)
+        self.moe_norm.weight.data.copy_(moe_norm_weight)
+        self.moe.weight_loader(gate_weight, expert_gate_weights, expert_up_weights,
+                               expert_down_weights)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        h = x + self.attn(self.attn_norm(x))
+        return h + self.moe(self.moe_norm(h))

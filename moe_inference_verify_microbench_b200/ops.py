@@ -1,0 +1,279 @@
+"""Torch-tensor wrappers over the C ABI (``include/moe_b200.h``).
+
+Each op checks devices, dtypes and contiguity, allocates its outputs with the
+torch caching allocator, and launches on the current CUDA stream.  Nothing
+here synchronises the host; device-side errors land in a per-device status
+word that ``check_status`` reads (tests and debugging only).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import NamedTuple
+
+import torch
+
+from . import _native
+
+BLOCK_M = 128
+
+
+class MoEKernelError(RuntimeError):
+    pass
+
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """The int32 device status word the kernels of ``device`` report into."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status[idx] = t
+    return t
+
+
+def check_status(device: torch.device | None = None, reset: bool = True) -> None:
+    """Synchronise and raise if any kernel on ``device`` reported an error."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    st = status_word(device)
+    code = int(st.item())
+    if reset and code:
+        st.zero_()
+    if code:
+        raise MoEKernelError(f"device status 0x{code:x}: {_native.error_string(code)}")
+
+
+def _p(t: torch.Tensor | None) -> ctypes.c_void_p | None:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _need(t: torch.Tensor, name: str, dtype: torch.dtype, ndim: int | None = None) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor: the MoE kernels have no CPU path")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if ndim is not None and t.dim() != ndim:
+        raise ValueError(f"{name} must have {ndim} dims, got shape {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _rc(rc: int, what: str) -> None:
+    if rc != 0:
+        raise MoEKernelError(f"{what}: {_native.error_string(rc)} (rc={rc})")
+
+
+# --------------------------------------------------------------------------- router
+
+
+def router_topk(x: torch.Tensor, router_weight: torch.Tensor, top_k: int,
+                norm_topk_prob: bool = True, bias: torch.Tensor | None = None,
+                return_logits: bool = False):
+    """Router GEMM + top-k + softmax (C5/python/solution.py:124-129).
+
+    Returns (ids int32 [T,k], weights fp32 [T,k], logits bf16 [T,E] or None).
+    """
+    _need(x, "x", torch.bfloat16, 2)
+    _need(router_weight, "router_weight", torch.bfloat16, 2)
+    T, H = x.shape
+    E = router_weight.shape[0]
+    if router_weight.shape[1] != H:
+        raise ValueError("router_weight must be [E, H]")
+    if bias is not None:
+        _need(bias, "bias", torch.float32, 1)
+    dev = x.device
+    ids = torch.empty((T, top_k), dtype=torch.int32, device=dev)
+    w = torch.empty((T, top_k), dtype=torch.float32, device=dev)
+    logits = torch.empty((T, E), dtype=torch.bfloat16, device=dev) if return_logits else None
+    lib = _native.load()
+    _rc(lib.moe_router_topk(_p(x), _p(router_weight), _p(bias), T, H, E, top_k,
+                            int(bool(norm_topk_prob)), _p(ids), _p(w), _p(logits),
+                            _p(status_word(dev)), _stream(dev)), "moe_router_topk")
+    return ids, w, logits
+
+
+# --------------------------------------------------------------------------- sort / align
+
+
+class SortResult(NamedTuple):
+    counts: torch.Tensor      # int32 [E_local]
+    offsets: torch.Tensor     # int32 [E_local + 1]
+    offsets64: torch.Tensor | None  # int64 [E_local + 1]
+    perm: torch.Tensor        # int32 [R]; valid below offsets[E_local]
+    inv: torch.Tensor | None  # int32 [R]; -1 for records outside the expert range
+    tiles: torch.Tensor       # int32 [max_tiles, 4]
+    num_tiles: torch.Tensor   # int32 [1]
+    max_tiles: int
+
+
+def max_tiles(R: int, e_local: int) -> int:
+    return int(_native.load().moe_max_tiles(int(R), int(e_local)))
+
+
+def sort_align(ids: torch.Tensor, num_experts: int, e_begin: int = 0, e_local: int | None = None,
+               want_inv: bool = False, want_offsets64: bool = False) -> SortResult:
+    """Stable sort of the flat routing records by expert plus the 128-row tile
+    table (C5/python/solution.py:131-136, C6/python/solution.py:141-160,
+    C9/python/solution.py:142-159)."""
+    _need(ids, "ids", torch.int32)
+    flat = ids.reshape(-1)
+    R = flat.numel()
+    e_local = num_experts if e_local is None else e_local
+    dev = ids.device
+    lib = _native.load()
+    mt = int(lib.moe_max_tiles(R, e_local))
+    ws_bytes = int(lib.moe_sort_align_workspace_bytes(R, e_local))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    counts = torch.empty(e_local, dtype=torch.int32, device=dev)
+    offsets = torch.empty(e_local + 1, dtype=torch.int32, device=dev)
+    off64 = torch.empty(e_local + 1, dtype=torch.int64, device=dev) if want_offsets64 else None
+    perm = torch.empty(max(R, 1), dtype=torch.int32, device=dev)[:R]
+    inv = torch.empty(R, dtype=torch.int32, device=dev) if want_inv else None
+    tiles = torch.empty((max(mt, 1), 4), dtype=torch.int32, device=dev)
+    num_tiles = torch.empty(1, dtype=torch.int32, device=dev)
+    _rc(lib.moe_sort_align(_p(flat), R, num_experts, e_begin, e_local, _p(ws), ws_bytes,
+                           _p(counts), _p(offsets), _p(off64), _p(perm), _p(inv), _p(tiles), mt,
+                           _p(num_tiles), _p(status_word(dev)), _stream(dev)), "moe_sort_align")
+    return SortResult(counts, offsets, off64, perm, inv, tiles, num_tiles, mt)
+
+
+def tiles_from_offsets(offsets: torch.Tensor, M: int):
+    """128-row tile table from int64 offsets[E+1] (C9/python/solution.py:142-159)."""
+    _need(offsets, "offsets", torch.int64, 1)
+    E = offsets.numel() - 1
+    dev = offsets.device
+    lib = _native.load()
+    mt = int(lib.moe_max_tiles(M, E))
+    tiles = torch.empty((max(mt, 1), 4), dtype=torch.int32, device=dev)
+    num_tiles = torch.empty(1, dtype=torch.int32, device=dev)
+    _rc(lib.moe_tiles_from_offsets(_p(offsets), E, _p(tiles), mt, _p(num_tiles),
+                                   _p(status_word(dev)), _stream(dev)), "moe_tiles_from_offsets")
+    return tiles, num_tiles, mt
+
+
+# --------------------------------------------------------------------------- rows
+
+
+def gather_rows(src: torch.Tensor, index: torch.Tensor, index_div: int = 1,
+                count: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """dst[p] = src[index[p] // index_div] (C5/python/solution.py:135-137)."""
+    _need(src, "src", torch.bfloat16, 2)
+    _need(index, "index", torch.int32, 1)
+    R = index.numel()
+    H = src.shape[1]
+    dst = out if out is not None else torch.empty((R, H), dtype=src.dtype, device=src.device)
+    if count is not None:
+        _need(count, "count", torch.int32)
+    lib = _native.load()
+    _rc(lib.moe_gather_rows(_p(src), src.shape[0], _p(index), R, _p(count), index_div, H, _p(dst),
+                            _p(status_word(src.device)), _stream(src.device)), "moe_gather_rows")
+    return dst
+
+
+def combine(rows: torch.Tensor, T: int, k: int, slot_src: torch.Tensor | None = None,
+            slot_w: torch.Tensor | None = None, ids: torch.Tensor | None = None,
+            e_range: tuple[int, int] | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[n] = sum_j w_j * rows[src_j] (C5/python/solution.py:158-160)."""
+    _need(rows, "rows", torch.bfloat16, 2)
+    H = rows.shape[1]
+    dev = rows.device
+    for name, t, dt in (("slot_src", slot_src, torch.int32), ("slot_w", slot_w, torch.float32),
+                        ("ids", ids, torch.int32)):
+        if t is not None:
+            _need(t, name, dt)
+            if t.numel() != T * k:
+                raise ValueError(f"{name} must hold T*k = {T * k} entries")
+    e0, e1 = e_range if e_range is not None else (0, 1 << 30)
+    y = out if out is not None else torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    lib = _native.load()
+    _rc(lib.moe_combine(_p(rows), rows.shape[0], _p(slot_src), _p(slot_w), _p(ids), e0, e1, T, k,
+                        H, _p(y), _p(status_word(dev)), _stream(dev)), "moe_combine")
+    return y
+
+
+# --------------------------------------------------------------------------- grouped GEMMs
+
+
+def grouped_w13_swiglu(a: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor,
+                       max_tiles_: int, w_gate: torch.Tensor, w_up: torch.Tensor,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """h = silu(a @ w_gate[e]^T) * (a @ w_up[e]^T) per tile (C9/python/solution.py:218-220)."""
+    _need(a, "a", torch.bfloat16, 2)
+    _need(w_gate, "w_gate", torch.bfloat16, 3)
+    _need(w_up, "w_up", torch.bfloat16, 3)
+    M, H = a.shape
+    E, I, H2 = w_gate.shape
+    if H2 != H or tuple(w_up.shape) != (E, I, H):
+        raise ValueError("w_gate / w_up must be [E, I, H] matching a [M, H]")
+    h = out if out is not None else torch.empty((M, I), dtype=torch.bfloat16, device=a.device)
+    lib = _native.load()
+    _rc(lib.moe_grouped_w13_swiglu(_p(a), M, _p(tiles), _p(num_tiles), max_tiles_, _p(w_gate),
+                                   _p(w_up), E, H, I, _p(h), _p(status_word(a.device)),
+                                   _stream(a.device)), "moe_grouped_w13_swiglu")
+    return h
+
+
+def grouped_w2(h: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor, max_tiles_: int,
+               w_down: torch.Tensor, row_map: torch.Tensor | None = None,
+               slot_scale: torch.Tensor | None = None, out: torch.Tensor | None = None,
+               out_rows: int | None = None) -> torch.Tensor:
+    """out[map(r)] = scale(map(r)) * (h[r] @ w_down[e]^T) (C9/python/solution.py:221)."""
+    _need(h, "h", torch.bfloat16, 2)
+    _need(w_down, "w_down", torch.bfloat16, 3)
+    M, I = h.shape
+    E, H, I2 = w_down.shape
+    if I2 != I:
+        raise ValueError("w_down must be [E, H, I] matching h [M, I]")
+    if row_map is not None:
+        _need(row_map, "row_map", torch.int32)
+    if slot_scale is not None:
+        _need(slot_scale, "slot_scale", torch.float32)
+    if out is None:
+        out = torch.empty((out_rows if out_rows is not None else M, H), dtype=torch.bfloat16,
+                          device=h.device)
+    lib = _native.load()
+    _rc(lib.moe_grouped_w2(_p(h), M, _p(tiles), _p(num_tiles), max_tiles_, _p(w_down), E, H, I,
+                           _p(row_map), _p(slot_scale), _p(out), out.shape[0],
+                           _p(status_word(h.device)), _stream(h.device)), "moe_grouped_w2")
+    return out
+
+
+# --------------------------------------------------------------------------- whole layer
+
+
+def moe_layer(x: torch.Tensor, router_weight: torch.Tensor, w_gate: torch.Tensor,
+              w_up: torch.Tensor, w_down: torch.Tensor, top_k: int, norm_topk_prob: bool = True,
+              bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Single-device MoE layer (C5/python/solution.py:108-161) in one C-ABI call."""
+    _need(x, "x", torch.bfloat16, 2)
+    for name, t in (("router_weight", router_weight), ("w_gate", w_gate), ("w_up", w_up),
+                    ("w_down", w_down)):
+        _need(t, name, torch.bfloat16)
+    if bias is not None:
+        _need(bias, "bias", torch.float32, 1)
+    T, H = x.shape
+    E, I, _ = w_gate.shape
+    lib = _native.load()
+    ws_bytes = int(lib.moe_layer_workspace_bytes(T, H, I, E, top_k))
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+    y = out if out is not None else torch.empty_like(x)
+    _rc(lib.moe_layer_forward(_p(x), _p(router_weight), _p(bias), _p(w_gate), _p(w_up),
+                              _p(w_down), T, H, I, E, top_k, int(bool(norm_topk_prob)),
+                              _p(workspace), workspace.numel(), _p(y), _p(status_word(x.device)),
+                              _stream(x.device)), "moe_layer_forward")
+    return y
+
+
+def layer_workspace_bytes(T: int, H: int, I: int, E: int, top_k: int) -> int:
+    return int(_native.load().moe_layer_workspace_bytes(T, H, I, E, top_k))

@@ -1,0 +1,57 @@
+"""``PermutedSparseMoE`` — drop-in for C5/python/solution.py:82-161.
+
+Same constructor, attributes (``gate``, ``experts[e].{gate,up,down}_proj``)
+and forward contract (``[..., H] -> same shape``).  The forward is one C-ABI
+call, ``moe_layer_forward``: router + top-k on tcgen05, a stable counting
+sort, the row gather, the w13 grouped GEMM with SwiGLU fused, the w2 grouped
+GEMM with the top-k weight fused, and a deterministic k-way combine.  It
+issues no host synchronisation (the reference syncs once per expert on
+``.item()``, C5:144).
+
+The module must be bf16 on a CUDA device: there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import ops
+from .experts import ExpertBank, SwiGLU_MLP, router_bias_of
+
+__all__ = ["PermutedSparseMoE", "SwiGLU_MLP"]
+
+
+class PermutedSparseMoE(nn.Module):
+    """Single-GPU sparse MoE with permutation + grouped compute (C5:82-161)."""
+
+    def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int,
+                 norm_topk_prob: bool = True) -> None:
+        super().__init__()
+        self.hidden = hidden
+        self.intermediate = intermediate
+        self.num_experts = num_experts
+        self.top_k = top_k
+        self.norm_topk_prob = norm_topk_prob
+        self.gate = nn.Linear(hidden, num_experts, bias=False)
+        self.experts = nn.ModuleList(SwiGLU_MLP(hidden, intermediate) for _ in range(num_experts))
+        self._bank = ExpertBank()
+
+    def _apply(self, fn, *args, **kwargs):
+        self._bank.invalidate()
+        return super()._apply(fn, *args, **kwargs)
+
+    def pack(self):
+        """Stacked expert weights (w_gate, w_up, w_down), binding the per-expert
+        parameters to views of them on first use."""
+        return self._bank.bind(self.experts)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        shape = x.shape
+        x_flat = x.reshape(-1, shape[-1])
+        if not x_flat.is_contiguous():
+            x_flat = x_flat.contiguous()
+        wg, wu, wd = self.pack()
+        y = ops.moe_layer(x_flat, self.gate.weight, wg, wu, wd, self.top_k, self.norm_topk_prob,
+                          bias=router_bias_of(self.gate))
+        return y.reshape(shape)

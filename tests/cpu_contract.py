@@ -1,0 +1,83 @@
+"""A torch-CPU stand-in for the kernel contract of ``ep.CudaKernels``.
+
+Test infrastructure only: it lets the expert-parallel schedules' host logic
+(split sizes, collective order, index bookkeeping) run on gloo ranks without
+a GPU.  It follows the same index conventions as the CUDA kernels (stable
+sort, slot = n*k + j, inv = -1 outside the expert range)."""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from moe_inference_verify_microbench_b200.ops import SortResult
+
+
+class CpuContractKernels:
+    @staticmethod
+    def router_topk(x, wr, k, norm_topk_prob=True, bias=None, return_logits=False):
+        acc = x.float() @ wr.float().T
+        if bias is not None:
+            acc = acc + bias.float()
+        logits = acc.to(torch.bfloat16).float()
+        ids = torch.sort(logits, dim=-1, descending=True, stable=True).indices[:, :k]
+        if norm_topk_prob:
+            w = torch.softmax(torch.gather(logits, 1, ids), dim=-1)
+        else:
+            w = torch.gather(torch.softmax(logits, dim=-1), 1, ids)
+        return ids.to(torch.int32), w.float(), logits.to(torch.bfloat16)
+
+    @staticmethod
+    def sort_align(ids, num_experts, e_begin=0, e_local=None, want_inv=False, want_offsets64=False):
+        e_local = num_experts if e_local is None else e_local
+        flat = ids.reshape(-1).long()
+        loc = flat - e_begin
+        keep = (loc >= 0) & (loc < e_local)
+        key = torch.where(keep, loc, torch.full_like(loc, e_local))
+        order = torch.sort(key, stable=True).indices
+        n = int(keep.sum())
+        counts = torch.bincount(loc[keep], minlength=e_local)
+        offsets = F.pad(counts.cumsum(0), (1, 0))
+        perm = torch.zeros(flat.numel(), dtype=torch.int32)
+        perm[:n] = order[:n].to(torch.int32)
+        inv = torch.full((flat.numel(),), -1, dtype=torch.int32)
+        inv[order[:n]] = torch.arange(n, dtype=torch.int32)
+        return SortResult(counts.to(torch.int32), offsets.to(torch.int32), offsets, perm, inv,
+                          None, torch.tensor([0]), 0)
+
+    @staticmethod
+    def gather_rows(src, index, index_div=1, count=None, out=None):
+        n = index.numel() if count is None else min(index.numel(), int(count.reshape(-1)[0]))
+        dst = torch.zeros((index.numel(), src.shape[1]), dtype=src.dtype)
+        dst[:n] = src[index[:n].long() // index_div]
+        return dst
+
+    @staticmethod
+    def expert_compute(xs, s, w_gate, w_up, w_down, row_map=None, slot_scale=None, out_rows=None):
+        M = xs.shape[0]
+        out = torch.zeros((out_rows if out_rows is not None else M, w_down.shape[1]),
+                          dtype=torch.bfloat16)
+        off = s.offsets.tolist()
+        for e in range(len(off) - 1):
+            a, b = off[e], off[e + 1]
+            if a == b:
+                continue
+            xe = xs[a:b].float()
+            h = (F.silu(xe @ w_gate[e].float().T) * (xe @ w_up[e].float().T)).to(torch.bfloat16)
+            o = h.float() @ w_down[e].float().T
+            rows = torch.arange(a, b) if row_map is None else row_map[a:b].long()
+            if slot_scale is not None:
+                o = o * slot_scale[rows][:, None]
+            out[rows] = o.to(torch.bfloat16)
+        return out
+
+    @staticmethod
+    def combine(rows, T, k, slot_src=None, slot_w=None, ids=None, e_range=None, out=None):
+        s = torch.arange(T * k) if slot_src is None else slot_src.reshape(-1).long()
+        w = torch.ones(T * k) if slot_w is None else slot_w.reshape(-1).float()
+        valid = s >= 0
+        if ids is not None and e_range is not None:
+            e = ids.reshape(-1).long()
+            valid &= (e >= e_range[0]) & (e < e_range[1])
+        contrib = rows.float()[s.clamp(min=0)] * (w * valid)[:, None]
+        return contrib.reshape(T, k, -1).sum(1).to(torch.bfloat16)

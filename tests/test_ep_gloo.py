@@ -1,0 +1,87 @@
+"""Expert-parallel schedules (C6 lean all_reduce, C7 all_to_all, C8 hybrid)
+on gloo CPU ranks, with a torch-CPU stand-in for the kernels, against the
+reference's own outputs for the same inputs (tests/golden/ep_*.npz)."""
+
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _worker(rank, world, port, name, q):
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
+    from cpu_contract import CpuContractKernels
+    from helpers import load_golden, to_t
+    from moe_inference_verify_microbench_b200.ep_lean import EPSparseMoE as Lean
+    from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
+    from moe_inference_verify_microbench_b200.hybrid import HybridMoE
+    from oracle import moe_oracle as mo
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = load_golden(name)
+        T, H, I, E, k, tp = (int(g[n]) for n in ("T", "H", "I", "E", "k", "tp"))
+        d = mo.make_inputs(T * world, H, I, E, int(g["seed"]))
+        xall = to_t(d["x"])
+        wr = to_t(d["wr"])
+        wg = [to_t(d["w_gate"][e]) for e in range(E)]
+        wu = [to_t(d["w_up"][e]) for e in range(E)]
+        wd = [to_t(d["w_down"][e]) for e in range(E)]
+        kind = str(g["kind"])
+        if kind == "c6":
+            mod = Lean(H, I, E, k, world, rank, group=None)
+            x = xall[:T]
+        elif kind == "c7":
+            mod = Pure(H, I, E, k, world, rank, group=None)
+            x = xall[rank * T:(rank + 1) * T]
+        else:
+            groups = [dist.new_group(list(range(i * tp, (i + 1) * tp))) for i in range(world // tp)]
+            mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None)
+            x = xall[(rank // tp) * T:(rank // tp + 1) * T]
+        mod = mod.to(torch.bfloat16)
+        mod._kernels = CpuContractKernels
+        mod.weight_loader(wr, wg, wu, wd)
+        if int(g["zipf"]):
+            lin = torch.nn.Linear(H, E, bias=True).to(torch.bfloat16)
+            lin.weight.data.copy_(wr)
+            lin.bias.data.copy_(torch.from_numpy(mo.zipf_bias(E)).to(torch.bfloat16))
+            mod.gate = lin
+        with torch.no_grad():
+            y = mod(x)
+            _, _, lg = CpuContractKernels.router_topk(x, mod.gate.weight, k, bias=getattr(mod.gate, "bias", None))
+        srt = torch.sort(lg.float(), dim=-1, descending=True).values
+        tie = (srt[:, k - 1] == srt[:, k]).numpy()
+        yref = mo.f32_from_bf16_bits(g[f"y_rank{rank}"])
+        err = mo.rel_err(y.float().numpy()[~tie], yref[~tie])
+        q.put((rank, err, float(tie.mean())))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name,world", [("ep_c6_w2.npz", 2), ("ep_c6_w4.npz", 4),
+                                        ("ep_c7_w2.npz", 2), ("ep_c7_w4_zipf.npz", 4),
+                                        ("ep_c8_w4_tp2.npz", 4)])
+def test_ep_schedule_matches_reference(name, world):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + abs(hash(name)) % 200
+    procs = [ctx.Process(target=_worker, args=(r, world, port, name, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, err, tie in res:
+        assert tie <= 0.2, (rank, tie)
+        assert err <= 2e-2, (rank, err)

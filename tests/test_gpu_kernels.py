@@ -1,0 +1,219 @@
+"""Parity of each CUDA kernel (through the C ABI) with the CPU oracle.
+
+Integer outputs (ids, counts, offsets, permutation, tile table) must be
+bit-exact; floating-point outputs must satisfy the tolerances written in
+each test.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import to_f32
+from moe_inference_verify_microbench_b200 import ops
+from oracle import moe_oracle as mo
+
+pytestmark = pytest.mark.gpu
+
+
+# ----------------------------------------------------------------------------- sort / align
+
+
+@pytest.mark.parametrize("R,E,e_begin,e_local", [
+    (1, 16, 0, 16), (37, 16, 0, 16), (4095, 128, 0, 128), (4096, 128, 0, 128),
+    (4097, 128, 0, 128), (40000, 128, 0, 128), (20000, 128, 32, 16), (9000, 64, 48, 16),
+])
+def test_sort_align_bit_exact(cuda, R, E, e_begin, e_local):
+    rng = np.random.default_rng(R + E)
+    ids = rng.integers(0, E, size=R).astype(np.int32)
+    ids[rng.random(R) < 0.3] = rng.integers(0, max(1, E // 8))  # skew + empty experts
+    res = ops.sort_align(torch.from_numpy(ids).to(cuda), E, e_begin, e_local, want_inv=True,
+                         want_offsets64=True)
+    ops.check_status(cuda)
+    loc = ids.astype(np.int64) - e_begin
+    keep = (loc >= 0) & (loc < e_local)
+    order = np.argsort(np.where(keep, loc, e_local), kind="stable")
+    n_keep = int(keep.sum())
+    perm_ref = order[:n_keep]
+    counts_ref = np.bincount(loc[keep], minlength=e_local)
+    offs_ref = np.concatenate([[0], np.cumsum(counts_ref)])
+    assert np.array_equal(res.counts.cpu().numpy(), counts_ref)
+    assert np.array_equal(res.offsets.cpu().numpy(), offs_ref)
+    assert np.array_equal(res.offsets64.cpu().numpy(), offs_ref)
+    assert np.array_equal(res.perm[:n_keep].cpu().numpy(), perm_ref)
+    inv_ref = np.full(R, -1, dtype=np.int64)
+    inv_ref[perm_ref] = np.arange(n_keep)
+    assert np.array_equal(res.inv.cpu().numpy(), inv_ref)
+    te, tie = mo.tile_metadata(offs_ref, ops.BLOCK_M)
+    nt = int(res.num_tiles.item())
+    assert nt == len(te)
+    tiles = res.tiles[:nt].cpu().numpy()
+    assert np.array_equal(tiles[:, 0], te)
+    rb = offs_ref[te] + tie * ops.BLOCK_M
+    assert np.array_equal(tiles[:, 1], rb)
+    assert np.array_equal(tiles[:, 2], np.minimum(offs_ref[te + 1], rb + ops.BLOCK_M))
+
+
+def test_sort_align_flags_bad_expert(cuda):
+    ids = torch.tensor([0, 3, 99, 1], dtype=torch.int32, device=cuda)
+    ops.sort_align(ids, 16)
+    with pytest.raises(ops.MoEKernelError, match="expert id out of range"):
+        ops.check_status(cuda)
+
+
+def test_tiles_from_offsets(cuda):
+    counts = np.array([5, 0, 128, 129, 0, 300, 1], dtype=np.int64)
+    offs = np.concatenate([[0], np.cumsum(counts)])
+    tiles, nt, mt = ops.tiles_from_offsets(torch.from_numpy(offs).to(cuda), int(offs[-1]))
+    te, tie = mo.tile_metadata(offs, ops.BLOCK_M)
+    n = int(nt.item())
+    assert n == len(te) <= mt
+    t = tiles[:n].cpu().numpy()
+    assert np.array_equal(t[:, 0], te)
+    assert np.array_equal(t[:, 1], offs[te] + tie * ops.BLOCK_M)
+
+
+# ----------------------------------------------------------------------------- rows
+
+
+def test_gather_rows_bit_exact(cuda):
+    rng = np.random.default_rng(3)
+    T, k, H = 300, 8, 256
+    x = torch.randn(T, H, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+    perm = rng.permutation(T * k).astype(np.int32)
+    out = ops.gather_rows(x.to(cuda), torch.from_numpy(perm).to(cuda), k)
+    ops.check_status(cuda)
+    assert torch.equal(out.cpu(), x[torch.from_numpy(perm // k).long()])
+
+
+def test_gather_rows_device_count(cuda):
+    x = torch.arange(40 * 8, dtype=torch.float32).reshape(40, 8).to(torch.bfloat16).to(cuda)
+    idx = torch.arange(39, -1, -1, dtype=torch.int32, device=cuda)
+    cnt = torch.tensor([7], dtype=torch.int32, device=cuda)
+    out = torch.zeros(40, 8, dtype=torch.bfloat16, device=cuda)
+    ops.gather_rows(x, idx, 1, count=cnt, out=out)
+    ops.check_status(cuda)
+    assert torch.equal(out[:7], x.flip(0)[:7])
+    assert torch.count_nonzero(out[7:]) == 0
+
+
+def test_combine_weighted_indirect(cuda):
+    g = torch.Generator().manual_seed(1)
+    T, k, H = 97, 8, 512
+    rows = torch.randn(T * k, H, generator=g).to(torch.bfloat16)
+    src = torch.randperm(T * k, generator=g).to(torch.int32)
+    w = torch.rand(T * k, generator=g)
+    ids = torch.randint(0, 16, (T * k,), generator=g, dtype=torch.int32)
+    y = ops.combine(rows.to(cuda), T, k, slot_src=src.to(cuda), slot_w=w.to(cuda),
+                    ids=ids.to(cuda), e_range=(4, 12))
+    ops.check_status(cuda)
+    keep = ((ids >= 4) & (ids < 12)).float()
+    ref = (rows.float()[src.long()] * (w * keep)[:, None]).reshape(T, k, H).sum(1)
+    assert (y.float().cpu() - ref).abs().max() <= 1e-2 * ref.abs().max()
+
+
+# ----------------------------------------------------------------------------- router
+
+
+@pytest.mark.parametrize("T,H,E,k,norm,bias", [
+    (1, 256, 16, 4, True, False), (5, 256, 128, 8, True, False), (128, 512, 128, 8, True, True),
+    (300, 2048, 128, 8, True, False), (257, 256, 64, 8, False, False), (1000, 2048, 128, 8, False, True),
+])
+def test_router_topk(cuda, T, H, E, k, norm, bias):
+    d = mo.make_inputs(T, H, 64, E, seed=T, experts=False)
+    x = mo.f32_from_bf16_bits(d["x"])
+    wr = mo.f32_from_bf16_bits(d["wr"])
+    b = mo.zipf_bias(E) if bias else None
+    xt = torch.from_numpy(x).to(torch.bfloat16).to(cuda)
+    wt = torch.from_numpy(wr).to(torch.bfloat16).to(cuda)
+    bt = torch.from_numpy(b).to(cuda) if bias else None
+    ids, w, logits = ops.router_topk(xt, wt, k, norm, bias=bt, return_logits=True)
+    ops.check_status(cuda)
+    lg = to_f32(logits)
+    # Logits: fp32 accumulation in another order may move the bf16 rounding by an
+    # ulp (more, relatively, for logits that nearly cancel to zero).
+    ref_lg = mo.router_logits(x, wr, b)
+    assert np.mean(lg != ref_lg) < 0.02
+    assert np.all(np.abs(lg - ref_lg) <= np.maximum(np.abs(ref_lg) * 2 ** -7, 1e-3))
+    # Routing on the kernel's own logits: ids bit-exact, weights to fp32 rounding.
+    vals, ref_ids = mo.topk_ids(lg, k)
+    assert np.array_equal(ids.cpu().numpy(), ref_ids)
+    ref_w = mo.topk_weights(lg, vals, ref_ids, norm, mode="fp32")
+    np.testing.assert_allclose(w.cpu().numpy(), ref_w, rtol=2e-6, atol=1e-7)
+
+
+def test_router_tie_rule(cuda):
+    """Equal logits: larger value first, then the lower expert id (stable sort order)."""
+    T, H, E, k = 4, 64, 32, 8
+    x = torch.zeros(T, H)
+    x[:, 0] = 1.0
+    wr = torch.zeros(E, H)
+    wr[:, 0] = torch.tensor([float(v) for v in [1, 2, 2, 0, 2, 3, 3, 1] * 4])
+    ids, w, _ = ops.router_topk(x.to(torch.bfloat16).to(cuda), wr.to(torch.bfloat16).to(cuda), k)
+    ops.check_status(cuda)
+    exp = torch.sort(wr[:, 0], descending=True, stable=True).indices[:k].to(torch.int32)
+    assert torch.equal(ids.cpu(), exp.expand(T, k))
+
+
+# ----------------------------------------------------------------------------- grouped GEMMs
+
+
+def _grouped_setup(cuda, counts, H, I, seed):
+    rng = np.random.default_rng(seed)
+    E = len(counts)
+    offs = np.concatenate([[0], np.cumsum(counts)]).astype(np.int64)
+    M = int(offs[-1])
+    a = (rng.standard_normal((M, H), dtype=np.float32)).astype(np.float32)
+    wg = rng.standard_normal((E, I, H), dtype=np.float32) * 0.05
+    wu = rng.standard_normal((E, I, H), dtype=np.float32) * 0.05
+    wd = rng.standard_normal((E, H, I), dtype=np.float32) * 0.05
+    bf = lambda v: torch.from_numpy(v).to(torch.bfloat16)  # noqa: E731
+    tb = {k: bf(v) for k, v in dict(a=a, wg=wg, wu=wu, wd=wd).items()}
+    fb = {k: v.float().numpy() for k, v in tb.items()}
+    tiles, nt, mt = ops.tiles_from_offsets(torch.from_numpy(offs).to(cuda), M)
+    return offs, M, tb, fb, tiles, nt, mt
+
+
+@pytest.mark.parametrize("counts,H,I", [
+    ([1, 0, 127, 128, 129, 300, 0, 5], 256, 128),   # BN=256 path
+    ([64, 0, 200, 1], 128, 64),                     # BN=128 path
+    ([513, 1024, 0, 3], 2048, 768),                 # production shapes
+])
+def test_w13_swiglu(cuda, counts, H, I):
+    offs, M, tb, fb, tiles, nt, mt = _grouped_setup(cuda, counts, H, I, sum(counts))
+    h = ops.grouped_w13_swiglu(tb["a"].to(cuda), tiles, nt, mt, tb["wg"].to(cuda), tb["wu"].to(cuda))
+    ops.check_status(cuda)
+    ref = np.zeros((M, I), dtype=np.float32)
+    for e in range(len(counts)):
+        s, t = offs[e], offs[e + 1]
+        if s == t:
+            continue
+        g = fb["a"][s:t] @ fb["wg"][e].T
+        u = fb["a"][s:t] @ fb["wu"][e].T
+        ref[s:t] = mo.silu_f32(g) * u
+    assert mo.rel_err(to_f32(h), ref) <= 1e-2
+
+
+@pytest.mark.parametrize("counts,H,I,mapped", [
+    ([1, 0, 127, 128, 129, 300, 0, 5], 256, 128, False),
+    ([1, 0, 127, 128, 129, 300, 0, 5], 256, 128, True),
+    ([64, 0, 200, 1], 128, 64, True),
+    ([513, 1024, 0, 3], 2048, 768, True),
+])
+def test_w2_scatter(cuda, counts, H, I, mapped):
+    offs, M, tb, fb, tiles, nt, mt = _grouped_setup(cuda, counts, H, I, 7 + sum(counts))
+    rng = np.random.default_rng(1)
+    h = torch.from_numpy(rng.standard_normal((M, I), dtype=np.float32)).to(torch.bfloat16)
+    hf = h.float().numpy()
+    rmap = rng.permutation(M).astype(np.int32) if mapped else np.arange(M, dtype=np.int32)
+    scale = rng.random(M).astype(np.float32) if mapped else np.ones(M, dtype=np.float32)
+    out = ops.grouped_w2(h.to(cuda), tiles, nt, mt, tb["wd"].to(cuda),
+                         row_map=torch.from_numpy(rmap).to(cuda) if mapped else None,
+                         slot_scale=torch.from_numpy(scale).to(cuda) if mapped else None)
+    ops.check_status(cuda)
+    ref = np.zeros((M, H), dtype=np.float32)
+    for e in range(len(counts)):
+        s, t = offs[e], offs[e + 1]
+        if s < t:
+            ref[rmap[s:t]] = (hf[s:t] @ fb["wd"][e].T) * scale[rmap[s:t]][:, None]
+    assert mo.rel_err(to_f32(out), ref) <= 1e-2
