@@ -89,6 +89,34 @@ MOE_API int moe_sort_align(const int32_t* topk_ids, int R, int E, int e_begin, i
                    int max_tiles, int32_t* num_tiles, int32_t* status, cudaStream_t stream);
 
 /*
+ * moe_sort_align without a workspace: the same kernels and the same outputs,
+ * with the per-CTA histogram scratch kept in a device array owned by the
+ * library (MOE_SORT_STATIC_SCRATCH_INTS int32 = 256 KiB, allocated on every
+ * GPU that loads the library and held until the process exits).  This entry
+ * point has no counterpart in the reference; it exists for callers that
+ * cannot allocate device memory themselves (a host framework that owns every
+ * device allocation, or a serving process that forbids allocation, and the
+ * device synchronisation cudaMalloc may bring, once it is running).  It calls
+ * no allocator.
+ * Limit: ceil(R / 4096) * E_local <= MOE_SORT_STATIC_SCRATCH_INTS (for
+ * E_local = 128, R <= 2,097,152 records); larger requests return
+ * MOE_RC_WORKSPACE and launch nothing.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All calls on a device share the one array, so
+ * calls whose kernels overlap on the GPU (different streams, no ordering
+ * between them) race and corrupt each other's results; calls ordered on one
+ * stream are safe.  The array keeps the last call's contents; every entry a
+ * call reads is first written by that call, so nothing needs clearing.
+ */
+#define MOE_SORT_STATIC_SCRATCH_INTS 65536
+MOE_API int moe_sort_align_static_scratch(const int32_t* topk_ids, int R, int E, int e_begin,
+                                          int E_local, int32_t* counts, int32_t* offsets,
+                                          int64_t* offsets64, int32_t* perm, int32_t* inv,
+                                          int32_t* tiles, int max_tiles, int32_t* num_tiles,
+                                          int32_t* status, cudaStream_t stream);
+
+/*
  * Tile table from caller-given int64 offsets[E + 1] (the C9 interface, where
  * the caller already holds sorted rows).  Replaces
  * C9/python/solution.py:142-159.

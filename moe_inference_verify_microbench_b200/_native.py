@@ -26,6 +26,8 @@ SIGNATURES: dict[str, tuple] = {
     "moe_max_tiles": (_c_int, [_c_int, _c_int]),
     "moe_sort_align": (_c_int, [_ptr, _c_int, _c_int, _c_int, _c_int, _ptr, _c_size, _ptr, _ptr,
                                 _ptr, _ptr, _ptr, _ptr, _c_int, _ptr, _ptr, _ptr]),
+    "moe_sort_align_static_scratch": (_c_int, [_ptr, _c_int, _c_int, _c_int, _c_int, _ptr, _ptr,
+                                               _ptr, _ptr, _ptr, _ptr, _c_int, _ptr, _ptr, _ptr]),
     "moe_tiles_from_offsets": (_c_int, [_ptr, _c_int, _ptr, _c_int, _ptr, _ptr, _ptr]),
     "moe_gather_rows": (_c_int, [_ptr, _c_int, _ptr, _c_int, _ptr, _c_int, _c_int, _ptr, _ptr,
                                  _ptr]),

@@ -19,7 +19,7 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libmoe_b200.so")
-SOURCES = ["capi.cu", "gemm.cu", "sort_align.cu", "rows.cu"]
+SOURCES = ["capi.cu", "gemm.cu", "sort_align.cu", "rows.cu", "sort_align_static.cu"]
 HEADERS = ["ptx.cuh", "grouped_gemm.cuh", "internal.h"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + [
