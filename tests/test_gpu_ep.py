@@ -1,0 +1,156 @@
+"""Expert-parallel schedules on real GPUs over NCCL (one process per GPU):
+C6 lean all_reduce, C7 all_to_all and C8 HybridMoE, against the reference's
+own outputs (tests/golden/ep_*.npz) and, at the benchmark's shapes, against
+the single-GPU layer.  Skipped when fewer GPUs than ranks are visible."""
+
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+pytestmark = pytest.mark.gpu
+
+
+def _need(world):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
+def _init(rank, world, port):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    return dev
+
+
+def _fixture_worker(rank, world, port, name, q):
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
+    from helpers import load_golden, to_t
+    from moe_inference_verify_microbench_b200 import ops
+    from moe_inference_verify_microbench_b200.ep_lean import EPSparseMoE as Lean
+    from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
+    from moe_inference_verify_microbench_b200.hybrid import HybridMoE
+    from oracle import moe_oracle as mo
+
+    dev = _init(rank, world, port)
+    try:
+        g = load_golden(name)
+        T, H, I, E, k, tp = (int(g[n]) for n in ("T", "H", "I", "E", "k", "tp"))
+        d = mo.make_inputs(T * world, H, I, E, int(g["seed"]))
+        xall = to_t(d["x"], dev)
+        wr = to_t(d["wr"], dev)
+        wg = [to_t(d["w_gate"][e], dev) for e in range(E)]
+        wu = [to_t(d["w_up"][e], dev) for e in range(E)]
+        wd = [to_t(d["w_down"][e], dev) for e in range(E)]
+        kind = str(g["kind"])
+        with torch.device(dev):
+            if kind == "c6":
+                mod = Lean(H, I, E, k, world, rank, group=None)
+                x = xall[:T]
+            elif kind == "c7":
+                mod = Pure(H, I, E, k, world, rank, group=None)
+                x = xall[rank * T:(rank + 1) * T]
+            else:
+                groups = [dist.new_group(list(range(i * tp, (i + 1) * tp))) for i in range(world // tp)]
+                mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None)
+                x = xall[(rank // tp) * T:(rank // tp + 1) * T]
+            mod = mod.to(torch.bfloat16)
+        mod.weight_loader(wr, wg, wu, wd)
+        bias = None
+        if int(g["zipf"]):
+            lin = torch.nn.Linear(H, E, bias=True).to(torch.bfloat16).to(dev)
+            lin.weight.data.copy_(wr)
+            lin.bias.data.copy_(torch.from_numpy(mo.zipf_bias(E)).to(torch.bfloat16))
+            mod.gate = lin
+            bias = lin.bias.float()
+        with torch.no_grad():
+            y = mod(x.contiguous())
+            _, _, lg = ops.router_topk(x.contiguous(), mod.gate.weight, k, bias=bias, return_logits=True)
+        torch.cuda.synchronize()
+        ops.check_status(dev)
+        srt = torch.sort(lg.float(), dim=-1, descending=True).values
+        tie = (srt[:, k - 1] == srt[:, k]).cpu().numpy()
+        yref = mo.f32_from_bf16_bits(g[f"y_rank{rank}"])
+        q.put((rank, mo.rel_err(y.float().cpu().numpy()[~tie], yref[~tie]), float(tie.mean())))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(target, world, args):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=target, args=(r, world) + args + (q,)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return res
+
+
+@pytest.mark.parametrize("name,world", [("ep_c6_w2.npz", 2), ("ep_c7_w2.npz", 2),
+                                        ("ep_c6_w4.npz", 4), ("ep_c7_w4_zipf.npz", 4),
+                                        ("ep_c8_w4_tp2.npz", 4)])
+def test_ep_schedule_on_gpus_matches_reference(name, world):
+    _need(world)
+    res = _spawn(_fixture_worker, world, (29800 + world, name))
+    for rank, err, tie in res:
+        assert tie <= 0.2, (rank, tie)
+        assert err <= 2e-2, (rank, err)
+
+
+def _full_worker(rank, world, port, kind, q):
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
+    from moe_inference_verify_microbench_b200 import ops
+    from moe_inference_verify_microbench_b200.ep_lean import EPSparseMoE as Lean
+    from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
+    from oracle import moe_oracle as mo
+
+    dev = _init(rank, world, port)
+    try:
+        H, I, E, k, T = 2048, 768, 128, 8, 1024
+        g = torch.Generator(device=dev)
+        g.manual_seed(3)
+        x_all = torch.randn(T * world, H, generator=g, device=dev).to(torch.bfloat16)
+        wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wg = (torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wu = (torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wd = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        with torch.device(dev):
+            cls = Lean if kind == "c6" else Pure
+            mod = cls(H, I, E, k, world, rank, group=None).to(torch.bfloat16)
+        mod.weight_loader(wr, list(wg), list(wu), list(wd))
+        x = x_all[:T] if kind == "c6" else x_all[rank * T:(rank + 1) * T]
+        with torch.no_grad():
+            y = mod(x.contiguous())
+            y_single = ops.moe_layer(x.contiguous(), wr, wg, wu, wd, k)
+        torch.cuda.synchronize()
+        ops.check_status(dev)
+        q.put((rank, mo.rel_err(y.float().cpu().numpy(), y_single.float().cpu().numpy())))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kind", ["c6", "c7"])
+def test_ep_full_shapes_match_single_gpu_layer(kind):
+    _need(2)
+    world = min(torch.cuda.device_count(), 8)
+    res = _spawn(_full_worker, world, (29900 + (kind == "c7"), kind))
+    for rank, err in res:
+        assert err <= 1e-2, (rank, err)
