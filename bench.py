@@ -260,50 +260,10 @@ def run_ours_single(args):
     torch.cuda.synchronize()
     ms_total = tm.ms()
 
-    # --- per-kernel breakdown: the same launches issued one C-ABI call at a time
-    ev = {n: [] for n in ("router", "sort", "gather", "w13", "w2", "combine")}
-    bufs = {}
-
-    def step_split():
-        marks = []
-        e0 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        marks.append(e0)
-
-        def mark():
-            e = torch.cuda.Event(enable_timing=True)
-            e.record(stream)
-            marks.append(e)
-
-        ids, w, _ = ops.router_topk(x, wr, K_TOP)
-        mark()
-        s = ops.sort_align(ids, E)
-        mark()
-        sx = ops.gather_rows(x, s.perm, K_TOP, out=bufs.get("sx"))
-        bufs["sx"] = sx
-        mark()
-        h = ops.grouped_w13_swiglu(sx, s.tiles, s.num_tiles, s.max_tiles, wg, wu, out=bufs.get("h"))
-        bufs["h"] = h
-        mark()
-        sl = ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, wd, row_map=s.perm,
-                            slot_scale=w.reshape(-1), out=bufs.get("sl"))
-        bufs["sl"] = sl
-        mark()
-        ops.combine(sl, T, K_TOP, out=y)
-        mark()
-        return marks, s
-
-    n_split = max(3, min(args.steps, 50))
-    all_marks = []
-    for _ in range(n_split):
-        marks, s = step_split()
-        all_marks.append(marks)
-    torch.cuda.synchronize()
-    for marks in all_marks:
-        for i, n in enumerate(ev):
-            ev[n].append(marks[i].elapsed_time(marks[i + 1]))
-    counts = s.counts.cpu().numpy()
-    n_active = int((counts > 0).sum())
+    # --- per-kernel breakdown: the launches of moe_layer_forward, issued one C-ABI
+    # call at a time into preallocated buffers, CUDA events between them.
+    ev, n_active = kernel_breakdown(dev, x, wr, wg, wu, wd, T, max(3, min(args.steps, 50)))
+    avg = {n: statistics.mean(v) for n, v in ev.items()}
 
     # --- e2e: PermutedSparseMoE.forward with host copies inside the timed region
     with torch.device(dev):
@@ -332,7 +292,6 @@ def run_ours_single(args):
 
     ms_step = ms_total / args.steps
     value = T / (ms_step * 1e-3)
-    avg = {n: statistics.mean(v) for n, v in ev.items()}
     w13_flop = 2.0 * T * K_TOP * (2 * I) * H
     w13_tflops = w13_flop / (avg["w13"] * 1e-3) / 1e12
     peak_tc = peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]
@@ -370,6 +329,73 @@ def run_ours_single(args):
         line["sweep_tokens_per_s"] = sweep(dev, [int(t) for t in args.sweep.split(",")], wr,
                                            bwg, bwu, bwd, peaks)
     print(json.dumps(line), flush=True)
+
+
+def kernel_breakdown(dev, x, wr, wg, wu, wd, T, n_steps):
+    """Per-kernel device time of the layer's launch sequence (router, sort,
+    gather, w13, w2, combine) through the C ABI, buffers preallocated so the
+    host enqueues fast; a sleep kernel first lets the host fill the queue, so
+    the events bracket GPU work only."""
+    import ctypes
+
+    from moe_inference_verify_microbench_b200 import _native, ops
+    lib = _native.load()
+    P = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    R = T * K_TOP
+    i32, bf = torch.int32, torch.bfloat16
+    ids = torch.empty(T, K_TOP, dtype=i32, device=dev)
+    w = torch.empty(T, K_TOP, dtype=torch.float32, device=dev)
+    mt = lib.moe_max_tiles(R, E)
+    wsb = lib.moe_sort_align_workspace_bytes(R, E)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    counts = torch.empty(E, dtype=i32, device=dev)
+    offs = torch.empty(E + 1, dtype=i32, device=dev)
+    perm = torch.empty(R, dtype=i32, device=dev)
+    tiles = torch.empty(mt, 4, dtype=i32, device=dev)
+    nt = torch.empty(1, dtype=i32, device=dev)
+    sx = torch.empty(R, H, dtype=bf, device=dev)
+    h = torch.empty(R, I, dtype=bf, device=dev)
+    sl = torch.empty(R, H, dtype=bf, device=dev)
+    y = torch.empty(T, H, dtype=bf, device=dev)
+    st = ops.status_word(dev)
+    S = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    names = ["router", "sort", "gather", "w13", "w2", "combine"]
+    calls = [
+        lambda: lib.moe_router_topk(P(x), P(wr), None, T, H, E, K_TOP, 1, P(ids), P(w), None, P(st), S),
+        lambda: lib.moe_sort_align(P(ids), R, E, 0, E, P(ws), wsb, P(counts), P(offs), None,
+                                   P(perm), None, P(tiles), mt, P(nt), P(st), S),
+        lambda: lib.moe_gather_rows(P(x), T, P(perm), R, None, K_TOP, H, P(sx), P(st), S),
+        lambda: lib.moe_grouped_w13_swiglu(P(sx), R, P(tiles), P(nt), mt, P(wg), P(wu), E, H, I,
+                                           P(h), P(st), S),
+        lambda: lib.moe_grouped_w2(P(h), R, P(tiles), P(nt), mt, P(wd), E, H, I, P(perm), P(w),
+                                   P(sl), R, P(st), S),
+        lambda: lib.moe_combine(P(sl), R, None, None, None, 0, E, T, K_TOP, H, P(y), P(st), S),
+    ]
+
+    def one(marks):
+        marks.append(torch.cuda.Event(enable_timing=True))
+        marks[-1].record()
+        for c in calls:
+            rc = c()
+            if rc != 0:
+                raise RuntimeError(_native.error_string(rc))
+            marks.append(torch.cuda.Event(enable_timing=True))
+            marks[-1].record()
+
+    for _ in range(3):
+        one([])
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(2e6) * n_steps)
+    all_marks = []
+    for _ in range(n_steps):
+        m = []
+        one(m)
+        all_marks.append(m)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    ev = {n: [m[i].elapsed_time(m[i + 1]) for m in all_marks] for i, n in enumerate(names)}
+    n_active = int((counts > 0).sum().item())
+    return ev, n_active
 
 
 def sweep(dev, token_counts, wr, wg, wu, wd, peaks):

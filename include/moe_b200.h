@@ -148,6 +148,19 @@ MOE_API int moe_grouped_w13_swiglu(const void* sorted_x, int M, const int32_t* t
                            cudaStream_t stream);
 
 /*
+ * moe_grouped_w13_swiglu with the row gather fused into the A-operand load:
+ * A row r is src[index[r] / index_div] (index = perm, index_div = k reads
+ * each routing record's token straight from x), so the [M, H] sorted copy of
+ * the activations (C5/python/solution.py:137) is never written.  Rows of a
+ * tile past its row_end are zero-filled.  src must be 16-byte aligned.
+ */
+MOE_API int moe_grouped_w13_swiglu_gather(const void* src, int src_rows, const int32_t* index,
+                                          int index_div, int M, const int32_t* tiles,
+                                          const int32_t* num_tiles, int max_tiles,
+                                          const void* w_gate, const void* w_up, int E, int H,
+                                          int I, void* h, int32_t* status, cudaStream_t stream);
+
+/*
  * Grouped down GEMM with a scatter/scale epilogue:
  *   out[m(r), :] = s(m(r)) * (h[r] @ w_down[e]^T), m = row_map (identity when
  *   NULL), s = slot_scale (1 when NULL).  With row_map = perm and slot_scale =
@@ -164,7 +177,7 @@ MOE_API int moe_grouped_w2(const void* h, int M, const int32_t* tiles, const int
  * y[n, :] = sum_j w_j * rows[src_j, :], j < k, fp32 accumulate in slot order:
  * src_j = slot_src[n*k+j] (n*k+j when NULL), w_j = slot_w[n*k+j] (1 when NULL);
  * slots with src_j < 0 or an expert id ids[n*k+j] outside [e_begin, e_end)
- * (no filter when ids is NULL) add nothing.  Replaces the index_add_
+ * (no filter when ids is NULL) add nothing; 1 <= k <= 8.  Replaces the index_add_
  * un-permute of C5/python/solution.py:160, C6/python/solution.py:175-176,
  * C7/python/solution.py:259-261 and C8/python/solution.py:221-224.
  */
@@ -175,8 +188,8 @@ MOE_API int moe_combine(const void* rows, int n_rows, const int32_t* slot_src, c
 /*
  * Whole single-device MoE layer, PermutedSparseMoE.forward
  * (C5/python/solution.py:108-161): router -> sort -> gather -> w13+SwiGLU ->
- * w2 (weighted, to slot rows) -> k-way combine into y [T, H].  Eight kernel
- * launches, no host sync.  workspace >= moe_layer_workspace_bytes(...).
+ * w2 (weighted, to slot rows) -> k-way combine into y [T, H].  No host sync.
+ * workspace >= moe_layer_workspace_bytes(...).
  */
 MOE_API size_t moe_layer_workspace_bytes(int T, int H, int I, int E, int top_k);
 MOE_API int moe_layer_forward(const void* x, const void* router_weight, const float* router_bias,

@@ -33,6 +33,9 @@ SIGNATURES: dict[str, tuple] = {
                                  _ptr]),
     "moe_grouped_w13_swiglu": (_c_int, [_ptr, _c_int, _ptr, _ptr, _c_int, _ptr, _ptr, _c_int,
                                         _c_int, _c_int, _ptr, _ptr, _ptr]),
+    "moe_grouped_w13_swiglu_gather": (_c_int, [_ptr, _c_int, _ptr, _c_int, _c_int, _ptr, _ptr,
+                                               _c_int, _ptr, _ptr, _c_int, _c_int, _c_int, _ptr,
+                                               _ptr, _ptr]),
     "moe_grouped_w2": (_c_int, [_ptr, _c_int, _ptr, _ptr, _c_int, _ptr, _c_int, _c_int, _c_int,
                                 _ptr, _ptr, _ptr, _c_int, _ptr, _ptr]),
     "moe_combine": (_c_int, [_ptr, _c_int, _ptr, _ptr, _ptr, _c_int, _c_int, _c_int, _c_int,

@@ -135,6 +135,16 @@ int moe_grouped_w13_swiglu(const void* sorted_x, int M, const int32_t* tiles,
                            w_gate, w_up, E, H, I, h, status, stream);
 }
 
+int moe_grouped_w13_swiglu_gather(const void* src, int src_rows, const int32_t* index,
+                                  int index_div, int M, const int32_t* tiles,
+                                  const int32_t* num_tiles, int max_tiles, const void* w_gate,
+                                  const void* w_up, int E, int H, int I, void* h,
+                                  int32_t* status, cudaStream_t stream) {
+  return launch_w13_swiglu_gather(src, src_rows, index, index_div, M,
+                                  reinterpret_cast<const int4*>(tiles), num_tiles, max_tiles,
+                                  w_gate, w_up, E, H, I, h, status, stream);
+}
+
 int moe_grouped_w2(const void* h, int M, const int32_t* tiles, const int32_t* num_tiles,
                    int max_tiles, const void* w_down, int E, int H, int I,
                    const int32_t* row_map, const float* slot_scale, void* out, int out_rows,
@@ -180,7 +190,8 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                                           nullptr, perm, nullptr, tiles, p.max_tiles, num_tiles,
                                           status, stream);
                  if (rc == kRcOk)
-                   rc = launch_gather_rows(x, T, perm, R, nullptr, top_k, H, sorted_x, status, stream);
+                   rc = launch_gather_rows(x, T, perm, R, nullptr, top_k, H, sorted_x, status,
+                                           stream);
                  if (rc == kRcOk)
                    rc = launch_w13_swiglu(sorted_x, R, tiles, num_tiles, p.max_tiles, w_gate, w_up,
                                           E, H, I, h, status, stream);

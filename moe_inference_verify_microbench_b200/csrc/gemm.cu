@@ -79,7 +79,7 @@ int device_sms() {
   return v;
 }
 
-template <int BN, int EPI, int STAGES>
+template <int BN, int EPI, int STAGES, bool GATHER_A = false>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                 const GemmArgs& args, long long work_units, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
@@ -88,7 +88,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
   if (cudaGetDevice(&dev) != cudaSuccess) return kRcCudaError;
   const uint64_t bit = 1ull << (dev & 63);
   if ((attr_done.load(std::memory_order_acquire) & bit) == 0) {
-    if (cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, STAGES>,
+    if (cudaFuncSetAttribute(grouped_gemm_kernel<BN, EPI, STAGES, GATHER_A>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) != cudaSuccess)
       return kRcCudaError;
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
@@ -96,8 +96,28 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
   const long long sms = device_sms();
   const int grid = static_cast<int>(work_units < sms ? work_units : sms);
   if (grid <= 0) return kRcOk;
-  grouped_gemm_kernel<BN, EPI, STAGES><<<grid, 256, L::kTotal, stream>>>(a, b0, b1, args);
+  grouped_gemm_kernel<BN, EPI, STAGES, GATHER_A>
+      <<<grid, gemm_threads<GATHER_A>(), L::kTotal, stream>>>(a, b0, b1, args);
   return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+// Widest N-tile (of those the shape allows) that still gives every SM a work
+// unit; narrow tiles only pay off for small batches (decode), where the
+// weights of a handful of experts must be streamed by all SMs at once.
+// `n_out` is the output width per expert, `out_per_bn` maps a tile width to
+// the output columns it produces, `rows` bounds the number of non-empty tiles.
+template <class OutPerBn>
+int pick_bn(int n_out, long long rows, int max_tiles, int allowed_mask, OutPerBn out_per_bn) {
+  const long long tiles = rows < max_tiles ? rows : max_tiles;
+  const long long sms = device_sms();
+  int best = 0;
+  for (int bn : {256, 128, 64}) {
+    const int bit = bn == 256 ? 1 : bn == 128 ? 2 : 4;
+    if (!(allowed_mask & bit) || n_out % out_per_bn(bn) != 0) continue;
+    best = bn;
+    if (tiles * (n_out / out_per_bn(bn)) >= sms) return bn;
+  }
+  return best;
 }
 
 GemmArgs blank_args(int* status) {
@@ -169,15 +189,54 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
                    : launch_gemm<128, kEpiSwiGLU, 6>(ma, mg, mu, g, units, stream);
 }
 
+int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, int index_div,
+                             int M, const int4* tiles, const int* num_tiles, int max_tiles,
+                             const void* w_gate, const void* w_up, int E, int H, int I,
+                             void* h_out, int* status, cudaStream_t stream) {
+  if (src == nullptr || tiles == nullptr || num_tiles == nullptr || w_gate == nullptr ||
+      w_up == nullptr || h_out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 ||
+      max_tiles < 0 || src_rows < 0 || index_div <= 0)
+    return kRcBadArgument;
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0) return kRcBadArgument;
+  if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
+  if (M == 0 || max_tiles == 0) return kRcOk;
+  const int bn = pick_bn(I, M, max_tiles, 7, [](int b) { return b / 2; });
+  CUtensorMap mg, mu;
+  int rc = map_3d(&mg, w_gate, E, I, H, bn / 2);
+  if (rc == kRcOk) rc = map_3d(&mu, w_up, E, I, H, bn / 2);
+  if (rc != kRcOk) return rc;
+  GemmArgs g = blank_args(status);
+  g.tiles = tiles;
+  g.num_tiles = num_tiles;
+  g.max_tiles = max_tiles;
+  g.n_tiles = I / (bn / 2);
+  g.num_kb = H / kBK;
+  g.b_rows = bn;
+  g.a_rows = M;
+  g.num_experts = E;
+  g.out = static_cast<__nv_bfloat16*>(h_out);
+  g.out_ld = I;
+  g.out_rows = M;
+  g.a_src = static_cast<const __nv_bfloat16*>(src);
+  g.a_src_rows = src_rows;
+  g.a_index = index;
+  g.a_index_div = index_div;
+  const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
+  // The A tensor map is unused when A is gathered; pass the gate map in its place.
+  if (bn == 256) return launch_gemm<256, kEpiSwiGLU, 4, true>(mg, mg, mu, g, units, stream);
+  if (bn == 128) return launch_gemm<128, kEpiSwiGLU, 6, true>(mg, mg, mu, g, units, stream);
+  return launch_gemm<64, kEpiSwiGLU, 8, true>(mg, mg, mu, g, units, stream);
+}
+
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
               void* out, int out_rows, int* status, cudaStream_t stream) {
   if (h == nullptr || tiles == nullptr || num_tiles == nullptr || w_down == nullptr ||
       out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0 || out_rows < 0)
     return kRcBadArgument;
-  if ((I % kBK) != 0 || (H % 128) != 0) return kRcUnsupported;
+  if ((I % kBK) != 0 || (H % 64) != 0) return kRcUnsupported;
   if (M == 0 || max_tiles == 0) return kRcOk;
-  const int bn = (H % 256 == 0) ? 256 : 128;
+  const int bn = pick_bn(H, M, max_tiles, 7, [](int b) { return b; });
   CUtensorMap ma, md;
   int rc = map_2d(&ma, h, M, I, kBM);
   if (rc == kRcOk) rc = map_3d(&md, w_down, E, H, I, bn);
@@ -197,8 +256,9 @@ int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int
   g.row_map = row_map;
   g.row_scale = row_scale;
   const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
-  return bn == 256 ? launch_gemm<256, kEpiStore, 4>(ma, md, md, g, units, stream)
-                   : launch_gemm<128, kEpiStore, 6>(ma, md, md, g, units, stream);
+  if (bn == 256) return launch_gemm<256, kEpiStore, 4>(ma, md, md, g, units, stream);
+  if (bn == 128) return launch_gemm<128, kEpiStore, 6>(ma, md, md, g, units, stream);
+  return launch_gemm<64, kEpiStore, 8>(ma, md, md, g, units, stream);
 }
 
 }  // namespace moe

@@ -17,6 +17,17 @@
 //   warps 4..7  epilogue: tcgen05.ld of its 32 TMEM lanes -> registers -> HBM
 // Shared-memory stages are released by tcgen05.commit; the two accumulators
 // let the epilogue of tile i overlap the main loop of tile i+1.
+//
+// GATHER_A (384 threads): the A operand is not a pre-gathered matrix but rows
+// of a source matrix picked through an index (row p of the tile reads source
+// row index[p] / index_div: the token of routing record perm[p]).  Each thread
+// of warps 8..11 owns one tile row and loads it with 16-byte cp.async into the
+// same 128-byte-swizzled layout TMA would write; cp.async.mbarrier.arrive.noinc
+// makes the stage barrier count the thread's arrival once its copies land, so
+// the loaders run up to STAGES ahead without waiting.  The MMA thread fences
+// the generic->async proxy after the barrier wait, before its tcgen05.mma reads
+// the stage.  Warp 0 then only loads B.  This fuses the permutation gather
+// (C5/python/solution.py:137) into the GEMM.
 #pragma once
 
 #include "ptx.cuh"
@@ -44,6 +55,11 @@ struct GemmArgs {
   int out_rows;          // output rows (bounds check)
   const int* row_map;    // kEpiStore: out row = row_map[row] (null = identity)
   const float* row_scale;  // kEpiStore: multiplier indexed by the mapped row (null = 1)
+  // GATHER_A
+  const __nv_bfloat16* a_src;  // source rows [a_src_rows, K]
+  int a_src_rows;
+  const int* a_index;          // A row p = a_src[a_index[p] / a_index_div] (null = p)
+  int a_index_div;
   // kEpiRouter
   const float* bias;     // [E] fp32 added before bf16 rounding (null = none)
   int top_k;
@@ -91,14 +107,23 @@ __device__ __forceinline__ void topk_insert(float (&v)[kRouterMaxK], int (&id)[k
   }
 }
 
-template <int BN, int EPI, int STAGES>
-__global__ void __launch_bounds__(256, 1)
+constexpr int kGatherWarp0 = 8;   // first of the four A-gather warps
+constexpr int kGatherThreads = 128;
+
+template <bool GATHER_A>
+constexpr int gemm_threads() {
+  return GATHER_A ? 384 : 256;
+}
+
+template <int BN, int EPI, int STAGES, bool GATHER_A = false>
+__global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB0,
                         const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
   using L = GemmSmem<BN, STAGES>;
   constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
-  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of 2");
+  static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512,
+                "TMEM allocation must be a power of 2 of at least 32 columns");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -118,7 +143,7 @@ __global__ void __launch_bounds__(256, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], GATHER_A ? 1 + kGatherThreads : 1);  // TMA (+ each gather thread)
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -135,7 +160,7 @@ __global__ void __launch_bounds__(256, 1)
     tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
+    if (!GATHER_A) tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB0);
     if (EPI == kEpiSwiGLU) tma_prefetch_desc(&tmB1);
   }
@@ -147,7 +172,8 @@ __global__ void __launch_bounds__(256, 1)
   int num_tiles = args.num_tiles != nullptr ? *args.num_tiles : args.max_tiles;
   num_tiles = max(0, min(num_tiles, args.max_tiles));
   const int total = num_tiles * args.n_tiles;
-  const uint32_t stage_tx = static_cast<uint32_t>(L::kABytes + args.b_rows * kBK * 2);
+  const uint32_t stage_tx =
+      static_cast<uint32_t>((GATHER_A ? 0 : L::kABytes) + args.b_rows * kBK * 2);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -171,7 +197,7 @@ __global__ void __launch_bounds__(256, 1)
             break;
           }
           mbar_arrive_expect_tx(&full[s], stage_tx);
-          tma_load_2d(sA + s * L::kABytes, &tmA, &full[s], kb * kBK, t.y);
+          if (!GATHER_A) tma_load_2d(sA + s * L::kABytes, &tmA, &full[s], kb * kBK, t.y);
           uint8_t* b = sB + s * L::kBBytes;
           if (EPI == kEpiSwiGLU) {
             tma_load_3d(b, &tmB0, &full[s], kb * kBK, nt * (BN / 2), t.x);
@@ -217,6 +243,7 @@ __global__ void __launch_bounds__(256, 1)
             ok = false;
             break;
           }
+          if (GATHER_A) fence_proxy_async_smem();  // cp.async (generic) writes -> MMA reads
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * L::kABytes);
           const uint32_t b0 = smem_u32(sB + s * L::kBBytes);
@@ -240,7 +267,49 @@ __global__ void __launch_bounds__(256, 1)
         if (globaltimer_ns() - t0 > kWaitLimitNs) break;
       }
     }
-  } else if (warp >= 4) {
+  } else if (GATHER_A && warp >= kGatherWarp0) {
+    // ---------------------------------------------------------- A-row gather
+    const int r = (warp - kGatherWarp0) * 32 + lane;  // row of the 128-row tile
+    const uint32_t swz = static_cast<uint32_t>(r & 7);
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
+      const int mt = w / args.n_tiles;
+      const int4 t = load_tile(args, mt);
+      const int p = t.y + r;
+      const __nv_bfloat16* src = args.a_src;  // any valid address when the row is absent
+      uint32_t nbytes = 0;
+      if (p < t.z) {
+        const int i = args.a_index != nullptr ? args.a_index[p] / args.a_index_div : p;
+        if (i >= 0 && i < args.a_src_rows) {
+          src = args.a_src + static_cast<size_t>(i) * (args.num_kb * kBK);
+          nbytes = 16;
+        } else {
+          record_status(args.status, kErrBadRow);
+        }
+      }
+      for (int kb = 0; kb < args.num_kb; ++kb) {
+        bool got = mbar_wait(&empty[s], ph ^ 1u, abort_flag, args.status, kErrTimeoutEmpty);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        const uint32_t dst = smem_u32(sA + s * L::kABytes) + static_cast<uint32_t>(r) * 128u;
+        const __nv_bfloat16* g = src + (nbytes ? kb * kBK : 0);
+#pragma unroll
+        for (uint32_t c = 0; c < 8; ++c) cp_async_16(dst + ((c ^ swz) << 4), g + c * 8, nbytes);
+        cp_async_arrive_noinc(&full[s]);
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+    // Every copy must have landed before the CTA may exit (also on abort).
+    cp_async_wait_all();
+  } else if (warp >= 4 && warp < 8) {
     // -------------------------------------------------------------- epilogue
     const int q = warp - 4;  // TMEM lane quarter owned by this warp
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
@@ -297,18 +366,22 @@ __global__ void __launch_bounds__(256, 1)
         }
         __nv_bfloat16* orow = args.out + static_cast<size_t>(st ? orow_idx : 0) * args.out_ld + nt * BN;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(tb + c0, r);
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(tb + c0, r0);
+          tmem_ld32(tb + c0 + 32, r1);
           tc_wait_ld();
-          uint32_t pk[16];
+          uint32_t pk[32];
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            pk[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * scale, __uint_as_float(r[2 * j + 1]) * scale);
+          for (int j = 0; j < 16; ++j) {
+            pk[j] = pack_bf16x2(__uint_as_float(r0[2 * j]) * scale, __uint_as_float(r0[2 * j + 1]) * scale);
+            pk[16 + j] =
+                pack_bf16x2(__uint_as_float(r1[2 * j]) * scale, __uint_as_float(r1[2 * j + 1]) * scale);
+          }
           if (st) {
             uint4* dst = reinterpret_cast<uint4*>(orow + c0);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
+            for (int j = 0; j < 8; ++j)
               dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
           }
         }

@@ -40,6 +40,10 @@ int launch_router(const void* x, const void* wr, const float* bias, int T, int H
 int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_tiles, int max_tiles,
                       const void* w_gate, const void* w_up, int E, int H, int I, void* h_out,
                       int* status, cudaStream_t stream);
+int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, int index_div,
+                             int M, const int4* tiles, const int* num_tiles, int max_tiles,
+                             const void* w_gate, const void* w_up, int E, int H, int I,
+                             void* h_out, int* status, cudaStream_t stream);
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
               void* out, int out_rows, int* status, cudaStream_t stream);

@@ -8,9 +8,9 @@
 //               slot_w[n*k+j] : 1; a slot is skipped when src_j < 0 or when its
 //               expert id (ids[n*k+j]) lies outside [e_begin, e_end).
 //
-// Both are HBM-bound copies: one warp per row, 16-byte vector accesses, fp32
-// accumulation of the k contributions in slot order (deterministic, unlike
-// the atomic index_add_ of the reference on CUDA).
+// Both are HBM-bound copies with 16-byte vector accesses; the combine sums the
+// k contributions in fp32 in slot order (deterministic, unlike the atomic
+// index_add_ of the reference on CUDA).
 #include "internal.h"
 
 namespace moe {
@@ -48,13 +48,64 @@ __device__ __forceinline__ void acc_bf16x8(float (&acc)[8], const uint4& v, floa
   }
 }
 
+constexpr int kCombineMaxK = 8;  // the router selects at most 8 experts
+
+// One thread per (token, 16-byte column vector): the k source rows' vectors are
+// loaded independently (no dependent chain of round trips), summed in fp32 in
+// slot order, and stored once.
 __global__ void __launch_bounds__(kRowsThreads) combine_rows(
+    const uint4* __restrict__ rows, int n_rows, const int* __restrict__ slot_src,
+    const float* __restrict__ slot_w, const int* __restrict__ ids, int e_begin, int e_end, int T,
+    int k, int vec_per_row, uint4* __restrict__ y, int* status) {
+  const long long total = static_cast<long long>(T) * vec_per_row;
+  for (long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; g < total;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int n = static_cast<int>(g / vec_per_row);
+    const int v = static_cast<int>(g - static_cast<long long>(n) * vec_per_row);
+    uint4 val[kCombineMaxK];
+    float wt[kCombineMaxK];
+#pragma unroll
+    for (int j = 0; j < kCombineMaxK; ++j) {
+      wt[j] = 0.0f;
+      val[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (j < k) {
+        const int s = n * k + j;
+        int src = slot_src != nullptr ? __ldg(slot_src + s) : s;
+        if (ids != nullptr) {
+          const int e = __ldg(ids + s);
+          if (e < e_begin || e >= e_end) src = -1;
+        }
+        if (src >= n_rows) {
+          record_status(status, kErrBadRow);
+          src = -1;
+        }
+        if (src >= 0) {
+          wt[j] = slot_w != nullptr ? __ldg(slot_w + s) : 1.0f;
+          val[j] = __ldg(rows + static_cast<size_t>(src) * vec_per_row + v);
+        }
+      }
+    }
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < kCombineMaxK; ++j)
+      if (j < k) acc_bf16x8(acc, val[j], wt[j]);
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    y[g] = o;
+  }
+}
+
+// Large batches: one warp per token, each lane sums 16-byte vectors of the k
+// rows (plenty of warps in flight hide the per-warp load chain).
+__global__ void __launch_bounds__(kRowsThreads) combine_rows_warp(
     const uint4* __restrict__ rows, int n_rows, const int* __restrict__ slot_src,
     const float* __restrict__ slot_w, const int* __restrict__ ids, int e_begin, int e_end, int T,
     int k, int vec_per_row, uint4* __restrict__ y, int* status) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int n = blockIdx.x * kRowsWarps + warp; n < T; n += gridDim.x * kRowsWarps) {
-    // Resolve the k source rows (lane j < k holds slot j).
     int src = -1;
     float w = 0.0f;
     if (lane < k) {
@@ -76,7 +127,8 @@ __global__ void __launch_bounds__(kRowsThreads) combine_rows(
       for (int j = 0; j < k; ++j) {
         const int sj = __shfl_sync(0xffffffffu, src, j);
         const float wj = __shfl_sync(0xffffffffu, w, j);
-        if (sj >= 0 && v < vec_per_row) acc_bf16x8(acc, __ldg(rows + static_cast<size_t>(sj) * vec_per_row + v), wj);
+        if (sj >= 0 && v < vec_per_row)
+          acc_bf16x8(acc, __ldg(rows + static_cast<size_t>(sj) * vec_per_row + v), wj);
       }
       if (v < vec_per_row) {
         uint4 o;
@@ -112,9 +164,18 @@ int launch_gather_rows(const void* src, int src_rows, const int* idx, int R, con
 int launch_combine(const void* rows, int n_rows, const int* slot_src, const float* slot_w,
                    const int* ids, int e_begin, int e_end, int T, int k, int H, void* y,
                    int* status, cudaStream_t stream) {
-  if (T < 0 || k <= 0 || k > 32 || H <= 0 || (H % 8) != 0) return kRcBadArgument;
+  if (T < 0 || k <= 0 || k > kCombineMaxK || H <= 0 || (H % 8) != 0) return kRcBadArgument;
   if (T == 0) return kRcOk;
-  combine_rows<<<rows_grid(T), kRowsThreads, 0, stream>>>(
+  if (T >= 1024) {
+    combine_rows_warp<<<rows_grid(T), kRowsThreads, 0, stream>>>(
+        static_cast<const uint4*>(rows), n_rows, slot_src, slot_w, ids, e_begin, e_end, T, k,
+        H / 8, static_cast<uint4*>(y), status);
+    return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+  }
+  const long long threads = static_cast<long long>(T) * (H / 8);
+  const long long blocks = (threads + kRowsThreads - 1) / kRowsThreads;
+  const int grid = static_cast<int>(blocks < 148LL * 16 ? blocks : 148LL * 16);
+  combine_rows<<<grid, kRowsThreads, 0, stream>>>(
       static_cast<const uint4*>(rows), n_rows, slot_src, slot_w, ids, e_begin, e_end, T, k, H / 8,
       static_cast<uint4*>(y), status);
   return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;

@@ -6,7 +6,8 @@
 // (C9/python/solution.py:142-159, which needs a host sync for its
 // repeat_interleave).
 //
-// Three launches over R = T*k routing records (flat slot index s = n*k + j):
+// Three launches over R = T*k routing records (flat slot index s = n*k + j;
+// one launch, sa_small, when R <= 4096 and E_local <= 256):
 //   1. sa_hist     per-CTA expert histograms of a contiguous record chunk
 //   2. sa_scan     one CTA: per-expert counts, offsets[E+1], the per-CTA base of
 //                  every expert, and the 128-row tile table
@@ -187,6 +188,76 @@ __global__ void __launch_bounds__(kSortThreads) sa_scatter(const int* __restrict
   }
 }
 
+// One-CTA variant for R <= kSortChunk and E_local <= kSortThreads (decode
+// batches): histogram, scan, tile table and the stable scatter in a single
+// launch.  Same outputs, same stable order as sa_hist + sa_scan + sa_scatter.
+__global__ void __launch_bounds__(kSortThreads) sa_small(
+    const int* __restrict__ ids, int R, int E, int e_begin, int E_local, int block_m,
+    int* __restrict__ counts, int* __restrict__ offsets, long long* __restrict__ offsets64,
+    int* __restrict__ perm, int* __restrict__ inv, int4* __restrict__ tiles, int max_tiles,
+    int* __restrict__ num_tiles, int* status) {
+  extern __shared__ int sm[];
+  int* base = sm;                 // [E_local]: counts, then next free position per expert
+  int* wcnt = sm + E_local;       // [8][E_local]
+  __shared__ int warp_sums[32];
+  __shared__ int total;
+  constexpr int kWarps = kSortThreads / 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int e = tid; e < E_local; e += blockDim.x) {
+    base[e] = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) wcnt[w * E_local + e] = 0;
+  }
+  __syncthreads();
+  for (int r = tid; r < R; r += blockDim.x) {
+    const int e = local_expert(ids, r, E, e_begin, E_local, status);
+    if (e >= 0) atomicAdd(&base[e], 1);
+  }
+  __syncthreads();
+  const int cnt = tid < E_local ? base[tid] : 0;
+  const int off = block_exclusive_scan(cnt, warp_sums, &total);
+  if (tid < E_local) {
+    counts[tid] = cnt;
+    offsets[tid] = off;
+    if (offsets64 != nullptr) offsets64[tid] = off;
+    base[tid] = off;
+  }
+  if (tid == 0) {
+    offsets[E_local] = total;
+    if (offsets64 != nullptr) offsets64[E_local] = total;
+  }
+  __syncthreads();
+  write_tiles(tid, E_local, cnt, off, block_m, tiles, max_tiles, num_tiles, warp_sums, &total);
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int r0 = 0; r0 < R; r0 += kSortThreads) {
+    const int r = r0 + tid;
+    const int e = r < R ? local_expert(ids, r, E, e_begin, E_local, status) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & lt_mask);
+    if (e >= 0 && rank == 0) wcnt[warp * E_local + e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int p = base[e] + rank;
+      for (int w = 0; w < warp; ++w) p += wcnt[w * E_local + e];
+      perm[p] = r;
+      if (inv != nullptr) inv[r] = p;
+    } else if (r < R && inv != nullptr) {
+      inv[r] = -1;
+    }
+    __syncthreads();
+    for (int x = tid; x < E_local; x += blockDim.x) {
+      int add = 0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        add += wcnt[w * E_local + x];
+        wcnt[w * E_local + x] = 0;
+      }
+      base[x] += add;
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void __launch_bounds__(1024) tiles_from_offsets(const long long* __restrict__ offsets,
                                                            int E, int block_m,
                                                            int4* __restrict__ tiles, int max_tiles,
@@ -216,6 +287,13 @@ int launch_sort_align(const int* ids, int R, int E, int e_begin, int E_local, in
       block_m <= 0)
     return kRcBadArgument;
   const int nblk = sort_num_blocks(R);
+  if (nblk <= 1 && E_local <= kSortThreads) {
+    const size_t sh = static_cast<size_t>(E_local) * (1 + kSortThreads / 32) * sizeof(int);
+    sa_small<<<1, kSortThreads, sh, stream>>>(ids, R, E, e_begin, E_local, block_m, counts,
+                                              offsets, offsets64, perm, inv, tiles, max_tiles,
+                                              num_tiles, status);
+    return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+  }
   int* hist = static_cast<int*>(workspace);
   const size_t sh_hist = static_cast<size_t>(E_local) * sizeof(int);
   const size_t sh_scatter = static_cast<size_t>(E_local) * (1 + kSortThreads / 32) * sizeof(int);

@@ -39,8 +39,14 @@ class CudaKernels:
     combine = staticmethod(ops.combine)
 
     @staticmethod
-    def expert_compute(xs, s, w_gate, w_up, w_down, row_map=None, slot_scale=None, out_rows=None):
-        h = ops.grouped_w13_swiglu(xs, s.tiles, s.num_tiles, s.max_tiles, w_gate, w_up)
+    def expert_compute(src, index, index_div, s, w_gate, w_up, w_down, row_map=None,
+                       slot_scale=None, out_rows=None):
+        """SwiGLU experts on rows src[index[p] // index_div] of the sorted order
+        (gather fused into the w13 GEMM), w2 output to row_map[p] scaled by
+        slot_scale[row_map[p]]."""
+        M = index.numel()
+        h = ops.grouped_w13_swiglu_gather(src, index, index_div, M, s.tiles, s.num_tiles,
+                                          s.max_tiles, w_gate, w_up)
         return ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, w_down, row_map=row_map,
                               slot_scale=slot_scale, out_rows=out_rows)
 
@@ -109,11 +115,10 @@ class EPSparseMoELean(_EPBase):
         ids, w = self._route(x_flat)                                   # full router (C6:127-133)
         s = K.sort_align(ids, self.num_experts, self.expert_start,     # local filter + stable sort
                          self.experts_per_rank)                        # (C6:141-160)
-        count = s.offsets[self.experts_per_rank:]
-        xs = K.gather_rows(x_flat, s.perm, k, count=count)             # (C6:156)
         wg, wu, wd = self.pack()
-        slots = K.expert_compute(xs, s, wg, wu, wd, row_map=s.perm,    # weighted, to slot rows
-                                 slot_scale=w.reshape(-1), out_rows=N * k)  # (C6:163-170)
+        slots = K.expert_compute(x_flat, s.perm, k, s, wg, wu, wd,     # gather (C6:156) fused;
+                                 row_map=s.perm, slot_scale=w.reshape(-1),  # weighted, to slot
+                                 out_rows=N * k)                       # rows (C6:163-170)
         partial = K.combine(slots, N, k, ids=ids.reshape(-1),          # (C6:175-176)
                             e_range=(self.expert_start, self.expert_end))
         dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)  # (C6:180)
@@ -140,9 +145,8 @@ def dispatch_combine(mod: _EPBase, local_x: torch.Tensor, group) -> torch.Tensor
     wg, wu, wd = mod.pack()
     if n_recv > 0:
         s2 = K.sort_align(recv_e, E, mod.expert_start, epr)           # local re-sort (C7:224-226)
-        xs2 = K.gather_rows(recv_x, s2.perm, 1)
-        y_t = K.expert_compute(xs2, s2, wg, wu, wd, row_map=s2.perm,  # back to received order
-                               out_rows=n_recv)                       # (C7:231-236)
+        y_t = K.expert_compute(recv_x, s2.perm, 1, s2, wg, wu, wd,    # back to received order
+                               row_map=s2.perm, out_rows=n_recv)      # (C7:227-236)
     else:
         y_t = recv_x.new_empty((0, local_x.shape[1]))
     y_ret = all_to_all_variable(y_t, recv_l, send_l, group)           # combine (C7:258)

@@ -222,6 +222,31 @@ def grouped_w13_swiglu(a: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Te
     return h
 
 
+def grouped_w13_swiglu_gather(src: torch.Tensor, index: torch.Tensor, index_div: int, M: int,
+                              tiles: torch.Tensor, num_tiles: torch.Tensor, max_tiles_: int,
+                              w_gate: torch.Tensor, w_up: torch.Tensor,
+                              out: torch.Tensor | None = None) -> torch.Tensor:
+    """``grouped_w13_swiglu`` whose A row r is ``src[index[r] // index_div]``: the
+    permutation gather (C5/python/solution.py:137) fused into the GEMM."""
+    _need(src, "src", torch.bfloat16, 2)
+    _need(index, "index", torch.int32)
+    _need(w_gate, "w_gate", torch.bfloat16, 3)
+    _need(w_up, "w_up", torch.bfloat16, 3)
+    H = src.shape[1]
+    E, I, H2 = w_gate.shape
+    if H2 != H or tuple(w_up.shape) != (E, I, H):
+        raise ValueError("w_gate / w_up must be [E, I, H] matching src [S, H]")
+    if index.numel() < M:
+        raise ValueError("index must hold at least M entries")
+    h = out if out is not None else torch.empty((M, I), dtype=torch.bfloat16, device=src.device)
+    lib = _native.load()
+    _rc(lib.moe_grouped_w13_swiglu_gather(_p(src), src.shape[0], _p(index), index_div, M,
+                                          _p(tiles), _p(num_tiles), max_tiles_, _p(w_gate),
+                                          _p(w_up), E, H, I, _p(h), _p(status_word(src.device)),
+                                          _stream(src.device)), "moe_grouped_w13_swiglu_gather")
+    return h
+
+
 def grouped_w2(h: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor, max_tiles_: int,
                w_down: torch.Tensor, row_map: torch.Tensor | None = None,
                slot_scale: torch.Tensor | None = None, out: torch.Tensor | None = None,

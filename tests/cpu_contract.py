@@ -53,8 +53,12 @@ class CpuContractKernels:
         return dst
 
     @staticmethod
-    def expert_compute(xs, s, w_gate, w_up, w_down, row_map=None, slot_scale=None, out_rows=None):
-        M = xs.shape[0]
+    def expert_compute(src, index, index_div, s, w_gate, w_up, w_down, row_map=None,
+                       slot_scale=None, out_rows=None):
+        M = index.numel()
+        n = int(s.offsets[-1])
+        xs = torch.zeros((M, src.shape[1]), dtype=src.dtype)
+        xs[:n] = src[index[:n].long() // index_div]
         out = torch.zeros((out_rows if out_rows is not None else M, w_down.shape[1]),
                           dtype=torch.bfloat16)
         off = s.offsets.tolist()

@@ -1,0 +1,66 @@
+"""The C ABI without a GPU: the library loads, exports exactly what
+include/moe_b200.h declares, the bindings match, the host-only queries answer,
+and the product path refuses CPU tensors (there is no CPU fallback)."""
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+import torch
+
+from moe_inference_verify_microbench_b200 import _native, ops
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "moe_b200.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^MOE_API [^(]*?\b(moe_\w+)\(", text, flags=re.M)))
+
+
+def test_library_loads_and_binds_every_declared_symbol():
+    lib = _native.load()
+    declared = header_functions()
+    assert len(declared) >= 14
+    assert sorted(_native.SIGNATURES) == declared
+    for name in declared:
+        assert isinstance(getattr(lib, name), ctypes._CFuncPtr)
+
+
+def test_exported_dynamic_symbols_match_header():
+    out = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = sorted({ln.split()[-1] for ln in out.splitlines() if " T moe_" in ln})
+    assert exported == header_functions()
+
+
+def test_host_queries():
+    lib = _native.load()
+    assert lib.moe_abi_version() == 1
+    assert lib.moe_max_tiles(131072, 128) == 1024 + 128
+    assert lib.moe_max_tiles(0, 16) == 16
+    assert lib.moe_sort_align_workspace_bytes(8192, 128) >= 2 * 128 * 4
+    ws = lib.moe_layer_workspace_bytes(16384, 2048, 768, 128, 8)
+    assert ws >= 16384 * 8 * (768 + 2048) * 2  # h + weighted slot rows
+    assert _native.error_string(-2) == "shape not supported by these kernels"
+    assert "expert id" in _native.error_string(0x201)
+
+
+def test_cpu_tensors_are_refused():
+    x = torch.zeros(4, 256, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="no CPU path"):
+        ops.router_topk(x, torch.zeros(16, 256, dtype=torch.bfloat16), 4)
+    with pytest.raises(ValueError, match="no CPU path"):
+        ops.sort_align(torch.zeros(8, dtype=torch.int32), 16)
+
+
+def test_null_arguments_rejected_without_launch():
+    lib = _native.load()
+    # No device pointer is touched: argument checks run first on the host.
+    assert lib.moe_layer_forward(None, None, None, None, None, None, 4, 256, 128, 16, 4, 1,
+                                 None, 0, None, None, None) == -1
+    assert lib.moe_sort_align(None, 8, 16, 0, 16, None, 0, None, None, None, None, None, None, 0,
+                              None, None, None) == -1

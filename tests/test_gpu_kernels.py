@@ -217,3 +217,45 @@ def test_w2_scatter(cuda, counts, H, I, mapped):
         if s < t:
             ref[rmap[s:t]] = (hf[s:t] @ fb["wd"][e].T) * scale[rmap[s:t]][:, None]
     assert mo.rel_err(to_f32(out), ref) <= 1e-2
+
+
+@pytest.mark.parametrize("T,k,H,I,E", [(300, 8, 256, 128, 16), (77, 4, 128, 64, 8), (2048, 8, 2048, 768, 128)])
+def test_w13_gather_fused_equals_gather_then_gemm(cuda, T, k, H, I, E):
+    """The fused-gather A operand (cp.async, swizzled by hand) must reproduce the
+    TMA-loaded pre-gathered operand bit for bit."""
+    g = torch.Generator(device=cuda)
+    g.manual_seed(T)
+    x = torch.randn(T, H, generator=g, device=cuda).to(torch.bfloat16)
+    ids = torch.randint(0, E, (T, k), generator=g, device=cuda, dtype=torch.int32)
+    wg = (torch.randn(E, I, H, generator=g, device=cuda) * 0.05).to(torch.bfloat16)
+    wu = (torch.randn(E, I, H, generator=g, device=cuda) * 0.05).to(torch.bfloat16)
+    s = ops.sort_align(ids, E)
+    xs = ops.gather_rows(x, s.perm, k)
+    h_ref = ops.grouped_w13_swiglu(xs, s.tiles, s.num_tiles, s.max_tiles, wg, wu)
+    h = ops.grouped_w13_swiglu_gather(x, s.perm, k, T * k, s.tiles, s.num_tiles, s.max_tiles, wg, wu)
+    ops.check_status(cuda)
+    assert torch.equal(h, h_ref)
+
+
+def test_layer_uses_fused_gather_consistently(cuda):
+    """moe_layer_forward (fused gather) equals the op-by-op pipeline with the
+    explicit gather, bit for bit."""
+    T, H, I, E, k = 700, 256, 128, 16, 4
+    g = torch.Generator(device=cuda)
+    g.manual_seed(1)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=g, device=cuda).to(bf)
+    wr = (torch.randn(E, H, generator=g, device=cuda) * 0.05).to(bf)
+    wg = (torch.randn(E, I, H, generator=g, device=cuda) * 0.05).to(bf)
+    wu = (torch.randn(E, I, H, generator=g, device=cuda) * 0.05).to(bf)
+    wd = (torch.randn(E, H, I, generator=g, device=cuda) * 0.05).to(bf)
+    y = ops.moe_layer(x, wr, wg, wu, wd, k)
+    ids, w, _ = ops.router_topk(x, wr, k)
+    s = ops.sort_align(ids, E)
+    xs = ops.gather_rows(x, s.perm, k)
+    h = ops.grouped_w13_swiglu(xs, s.tiles, s.num_tiles, s.max_tiles, wg, wu)
+    sl = ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, wd, row_map=s.perm,
+                        slot_scale=w.reshape(-1))
+    y2 = ops.combine(sl, T, k)
+    ops.check_status(cuda)
+    assert torch.equal(y, y2)

@@ -144,3 +144,31 @@ def test_fused_moe_forward_c9(cuda):
                                wd.float().numpy(), mode="fp32")
     assert mo.rel_err(to_f32(y), ref) <= REL_TOL
     assert torch.count_nonzero(y[int(offs[-1]):]) == 0
+
+
+@pytest.mark.parametrize("T", [1, 2, 5, 40])
+def test_layer_decode_sizes_full_shapes(cuda, T):
+    """Decode batch sizes at H=2048 I=768 E=128 k=8 (narrow N-tiles are picked
+    for these): routing bit-exact, every token within tolerance of the oracle."""
+    H, I, E, k = 2048, 768, 128, 8
+    g = torch.Generator(device=cuda)
+    g.manual_seed(100 + T)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=g, device=cuda).to(bf)
+    wr = (torch.randn(E, H, generator=g, device=cuda) * 0.02).to(bf)
+    wg = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wu = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wd = (torch.randn(E, H, I, generator=g, device=cuda) * 0.02).to(bf)
+    y = ops.moe_layer(x, wr, wg, wu, wd, k)
+    ids, w, lg = ops.router_topk(x, wr, k, return_logits=True)
+    ops.check_status(cuda)
+    ids_np = ids.cpu().numpy()
+    _, rid = mo.topk_ids(to_f32(lg), k)
+    assert np.array_equal(ids_np, rid)
+    used = np.unique(ids_np)
+    sel = torch.from_numpy(used).to(cuda)
+    f = lambda t: t.index_select(0, sel).float().cpu().numpy()  # noqa: E731
+    remap = {int(e): i for i, e in enumerate(used)}
+    lids = np.vectorize(remap.get)(ids_np)
+    ref = sample_token_outputs(to_f32(x), f(wg), f(wu), f(wd), lids, w.cpu().numpy(), np.arange(T))
+    assert mo.rel_err(to_f32(y), ref) <= REL_TOL
