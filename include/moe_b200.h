@@ -140,7 +140,7 @@ MOE_API int moe_gather_rows(const void* src, int src_rows, const int32_t* index,
  *   entries {e, row_begin, row_end}; A is [M, H], h is [M, I].
  * Replaces the gate/up grouped matmuls and silu*mul of
  * C9/python/solution.py:218-220 (and C5/python/solution.py:79-80 per expert).
- * Needs H % 64 == 0, I % 64 == 0.
+ * Needs H % 64 == 0, I % 32 == 0.
  */
 MOE_API int moe_grouped_w13_swiglu(const void* sorted_x, int M, const int32_t* tiles,
                            const int32_t* num_tiles, int max_tiles, const void* w_gate,
@@ -166,7 +166,7 @@ MOE_API int moe_grouped_w13_swiglu_gather(const void* src, int src_rows, const i
  *   NULL), s = slot_scale (1 when NULL).  With row_map = perm and slot_scale =
  *   the flat top-k weights, each slot's weighted expert output lands in row
  *   n*k + j.  Replaces C9/python/solution.py:221 and the weight scale of
- *   C5/python/solution.py:158.  Needs I % 64 == 0, H % 128 == 0.
+ *   C5/python/solution.py:158.  Needs I % 64 == 0, H % 64 == 0.
  */
 MOE_API int moe_grouped_w2(const void* h, int M, const int32_t* tiles, const int32_t* num_tiles,
                    int max_tiles, const void* w_down, int E, int H, int I,

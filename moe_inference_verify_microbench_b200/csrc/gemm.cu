@@ -164,9 +164,9 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
   if (a == nullptr || tiles == nullptr || num_tiles == nullptr || w_gate == nullptr ||
       w_up == nullptr || h_out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0)
     return kRcBadArgument;
-  if ((H % kBK) != 0 || (I % 64) != 0) return kRcUnsupported;
+  if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   if (M == 0 || max_tiles == 0) return kRcOk;
-  const int bn = (I % 128 == 0) ? 256 : 128;
+  const int bn = pick_bn(I, M, max_tiles, 7, [](int b) { return b / 2; });
   CUtensorMap ma, mg, mu;
   int rc = map_2d(&ma, a, M, H, kBM);
   if (rc == kRcOk) rc = map_3d(&mg, w_gate, E, I, H, bn / 2);
@@ -185,8 +185,9 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
   g.out_ld = I;
   g.out_rows = M;
   const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
-  return bn == 256 ? launch_gemm<256, kEpiSwiGLU, 4>(ma, mg, mu, g, units, stream)
-                   : launch_gemm<128, kEpiSwiGLU, 6>(ma, mg, mu, g, units, stream);
+  if (bn == 256) return launch_gemm<256, kEpiSwiGLU, 4>(ma, mg, mu, g, units, stream);
+  if (bn == 128) return launch_gemm<128, kEpiSwiGLU, 6>(ma, mg, mu, g, units, stream);
+  return launch_gemm<64, kEpiSwiGLU, 8>(ma, mg, mu, g, units, stream);
 }
 
 int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, int index_div,
@@ -200,6 +201,7 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
   if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0) return kRcBadArgument;
   if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   if (M == 0 || max_tiles == 0) return kRcOk;
+  if (src_rows == 0) return kRcBadArgument;  // rows to gather, but nothing to gather from
   const int bn = pick_bn(I, M, max_tiles, 7, [](int b) { return b / 2; });
   CUtensorMap mg, mu;
   int rc = map_3d(&mg, w_gate, E, I, H, bn / 2);
@@ -222,7 +224,7 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
   g.a_index = index;
   g.a_index_div = index_div;
   const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
-  // The A tensor map is unused when A is gathered; pass the gate map in its place.
+  // A is gathered by the loader warps; the gate map stands in for the unused A map.
   if (bn == 256) return launch_gemm<256, kEpiSwiGLU, 4, true>(mg, mg, mu, g, units, stream);
   if (bn == 128) return launch_gemm<128, kEpiSwiGLU, 6, true>(mg, mg, mu, g, units, stream);
   return launch_gemm<64, kEpiSwiGLU, 8, true>(mg, mg, mu, g, units, stream);

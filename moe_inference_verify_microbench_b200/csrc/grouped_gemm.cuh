@@ -20,14 +20,14 @@
 //
 // GATHER_A (384 threads): the A operand is not a pre-gathered matrix but rows
 // of a source matrix picked through an index (row p of the tile reads source
-// row index[p] / index_div: the token of routing record perm[p]).  Each thread
-// of warps 8..11 owns one tile row and loads it with 16-byte cp.async into the
-// same 128-byte-swizzled layout TMA would write; cp.async.mbarrier.arrive.noinc
-// makes the stage barrier count the thread's arrival once its copies land, so
-// the loaders run up to STAGES ahead without waiting.  The MMA thread fences
-// the generic->async proxy after the barrier wait, before its tcgen05.mma reads
-// the stage.  Warp 0 then only loads B.  This fuses the permutation gather
-// (C5/python/solution.py:137) into the GEMM.
+// row index[p] / index_div: the token of routing record perm[p]).  Warps 8..11
+// load them with 16-byte cp.async into the same 128-byte-swizzled layout TMA
+// would write; eight consecutive lanes cover one row's 128 bytes, so every
+// warp instruction moves four whole 128-byte lines.  A loader publishes stage i
+// two stages later: it waits for that stage's copies, fences the generic->async
+// proxy (the MMA reads shared memory through the async proxy), and its warp's
+// lane 0 arrives on the stage barrier.  Warp 0 then loads only B.  This fuses
+// the permutation gather (C5/python/solution.py:137) into the GEMM.
 #pragma once
 
 #include "ptx.cuh"
@@ -91,28 +91,46 @@ __device__ __forceinline__ int4 load_tile(const GemmArgs& a, int mt) {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-// Top-k insertion keeping (value desc, expert id asc): the reference's
-// torch.topk with ties broken toward the lower expert id.
-__device__ __forceinline__ void topk_insert(float (&v)[kRouterMaxK], int (&id)[kRouterMaxK],
-                                            float cv, int ci) {
+// Router top-k keys.  A bf16 logit and its expert id pack into one 32-bit key
+// whose unsigned order is "larger value first, lower expert id first among
+// equal values" -- the reference's torch.topk with ties broken toward the lower
+// id.  High half: the bf16 bits mapped to unsigned order (negative values
+// flipped, positive ones offset by the sign bit); low half: 0xFFFF - id.
+__device__ __forceinline__ uint32_t topk_key(float bf16_value, int id) {
+  uint32_t b = __float_as_uint(bf16_value) >> 16;
+  if (b == 0x8000u) b = 0u;  // -0 equals +0: let the id decide, as torch does
+  const uint32_t ord = (b & 0x8000u) ? (~b & 0xFFFFu) : (b | 0x8000u);
+  return (ord << 16) | (0xFFFFu - static_cast<uint32_t>(id));
+}
+
+__device__ __forceinline__ float topk_key_value(uint32_t key) {
+  const uint32_t ord = key >> 16;
+  const uint32_t b = (ord & 0x8000u) ? (ord & 0x7FFFu) : (~ord & 0xFFFFu);
+  return __uint_as_float(b << 16);
+}
+
+__device__ __forceinline__ int topk_key_id(uint32_t key) {
+  return static_cast<int>(0xFFFFu - (key & 0xFFFFu));
+}
+
+// Keep the kRouterMaxK largest keys in descending order: one max/min pair per
+// slot, no data-dependent branches.
+__device__ __forceinline__ void topk_insert(uint32_t (&top)[kRouterMaxK], uint32_t key) {
 #pragma unroll
   for (int i = 0; i < kRouterMaxK; ++i) {
-    const bool better = (cv > v[i]) || (cv == v[i] && ci < id[i]);
-    const float tv = better ? v[i] : cv;
-    const int ti = better ? id[i] : ci;
-    v[i] = better ? cv : v[i];
-    id[i] = better ? ci : id[i];
-    cv = tv;
-    ci = ti;
+    const uint32_t hi = max(top[i], key);
+    key = min(top[i], key);
+    top[i] = hi;
   }
 }
 
-constexpr int kGatherWarp0 = 8;   // first of the four A-gather warps
-constexpr int kGatherThreads = 128;
+constexpr int kGatherWarp0 = 8;    // first of the four A-loader warps
+constexpr int kGatherWarps = 4;
+constexpr int kGatherLag = 2;      // a stage is published this many stages after its copies
 
 template <bool GATHER_A>
 constexpr int gemm_threads() {
-  return GATHER_A ? 384 : 256;
+  return GATHER_A ? 256 + 32 * kGatherWarps : 256;
 }
 
 template <int BN, int EPI, int STAGES, bool GATHER_A = false>
@@ -143,7 +161,7 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], GATHER_A ? 1 + kGatherThreads : 1);  // TMA (+ each gather thread)
+      mbar_init(&full[s], GATHER_A ? 1 + kGatherWarps : 1);  // TMA (+ each loader warp)
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -243,7 +261,6 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
             ok = false;
             break;
           }
-          if (GATHER_A) fence_proxy_async_smem();  // cp.async (generic) writes -> MMA reads
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * L::kABytes);
           const uint32_t b0 = smem_u32(sB + s * L::kBBytes);
@@ -268,25 +285,35 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
       }
     }
   } else if (GATHER_A && warp >= kGatherWarp0) {
-    // ---------------------------------------------------------- A-row gather
-    const int r = (warp - kGatherWarp0) * 32 + lane;  // row of the 128-row tile
-    const uint32_t swz = static_cast<uint32_t>(r & 7);
+    // ---------------------------------------------------------- A-row loaders
+    // Thread g = 0..127 copies 16-byte chunk (g % 8) of tile rows (g / 8) + 16 j,
+    // j = 0..7: lanes 8m..8m+7 of a warp read one row's 128 contiguous bytes.
+    const int g = threadIdx.x - kGatherWarp0 * 32;
+    const uint32_t chunk = static_cast<uint32_t>(g & 7);
+    const int row0 = g >> 3;  // 0..15
+    const int K = args.num_kb * kBK;
+    static_assert(kGatherLag < STAGES - 1, "a loader must publish before it needs the stage back");
     int s = 0;
     uint32_t ph = 0;
+    uint32_t it = 0;  // stages issued by this loader
     bool ok = true;
     for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
       const int mt = w / args.n_tiles;
       const int4 t = load_tile(args, mt);
-      const int p = t.y + r;
-      const __nv_bfloat16* src = args.a_src;  // any valid address when the row is absent
-      uint32_t nbytes = 0;
-      if (p < t.z) {
-        const int i = args.a_index != nullptr ? args.a_index[p] / args.a_index_div : p;
-        if (i >= 0 && i < args.a_src_rows) {
-          src = args.a_src + static_cast<size_t>(i) * (args.num_kb * kBK);
-          nbytes = 16;
-        } else {
-          record_status(args.status, kErrBadRow);
+      const __nv_bfloat16* src[8];
+      uint32_t nbytes = 0;  // bit j set: row j present
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int p = t.y + row0 + 16 * j;
+        src[j] = args.a_src;  // any valid address when the row is absent (zero-filled)
+        if (p < t.z) {
+          const int i = args.a_index != nullptr ? args.a_index[p] / args.a_index_div : p;
+          if (i >= 0 && i < args.a_src_rows) {
+            src[j] = args.a_src + static_cast<size_t>(i) * K + chunk * 8;
+            nbytes |= 1u << j;
+          } else {
+            record_status(args.status, kErrBadRow);
+          }
         }
       }
       for (int kb = 0; kb < args.num_kb; ++kb) {
@@ -296,19 +323,36 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
           ok = false;
           break;
         }
-        const uint32_t dst = smem_u32(sA + s * L::kABytes) + static_cast<uint32_t>(r) * 128u;
-        const __nv_bfloat16* g = src + (nbytes ? kb * kBK : 0);
+        const uint32_t base = smem_u32(sA + s * L::kABytes);
 #pragma unroll
-        for (uint32_t c = 0; c < 8; ++c) cp_async_16(dst + ((c ^ swz) << 4), g + c * 8, nbytes);
-        cp_async_arrive_noinc(&full[s]);
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t r = static_cast<uint32_t>(row0 + 16 * j);
+          const uint32_t dst = base + r * 128u + ((chunk ^ (r & 7u)) << 4);
+          const bool have = (nbytes >> j) & 1u;
+          cp_async_16(dst, have ? src[j] + kb * kBK : src[j], have ? 16u : 0u);
+        }
+        cp_async_commit();
+        if (it >= static_cast<uint32_t>(kGatherLag)) {
+          cp_async_wait_group<kGatherLag>();
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[(it - kGatherLag) % STAGES]);
+        }
+        ++it;
         if (++s == STAGES) {
           s = 0;
           ph ^= 1u;
         }
       }
     }
-    // Every copy must have landed before the CTA may exit (also on abort).
+    // Publish the stages still in flight (also on abort), then let every copy land.
     cp_async_wait_all();
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t first = it > static_cast<uint32_t>(kGatherLag) ? it - kGatherLag : 0u;
+      for (uint32_t i = first; i < it; ++i) mbar_arrive(&full[i % STAGES]);
+    }
   } else if (warp >= 4 && warp < 8) {
     // -------------------------------------------------------------- epilogue
     const int q = warp - 4;  // TMEM lane quarter owned by this warp
@@ -388,13 +432,9 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
       } else {
         // Router: the row's E logits -> bf16 -> top-k (value desc, id asc) -> softmax.
         const int E = args.b_rows;
-        float tv[kRouterMaxK];
-        int ti[kRouterMaxK];
+        uint32_t top[kRouterMaxK];
 #pragma unroll
-        for (int i = 0; i < kRouterMaxK; ++i) {
-          tv[i] = -INFINITY;
-          ti[i] = 0x7fffffff;
-        }
+        for (int i = 0; i < kRouterMaxK; ++i) top[i] = 0u;  // below every real key
         float run_max = -INFINITY, run_sum = 0.0f;  // softmax over all E (norm_topk_prob=False)
 #pragma unroll 1
         for (int c0 = 0; c0 < E; c0 += 16) {
@@ -417,7 +457,7 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
           }
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            topk_insert(tv, ti, lv[j], c0 + j);
+            topk_insert(top, topk_key(lv[j], c0 + j));
             if (!args.norm_topk_prob) {
               const float m = fmaxf(run_max, lv[j]);
               run_sum = run_sum * expf(run_max - m) + expf(lv[j] - m);
@@ -427,6 +467,13 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
         }
         if (valid) {
           const int k = args.top_k;
+          float tv[kRouterMaxK];
+          int ti[kRouterMaxK];
+#pragma unroll
+          for (int i = 0; i < kRouterMaxK; ++i) {
+            tv[i] = topk_key_value(top[i]);
+            ti[i] = topk_key_id(top[i]);
+          }
           float den = 0.0f, ref = tv[0];
           if (args.norm_topk_prob) {
 #pragma unroll

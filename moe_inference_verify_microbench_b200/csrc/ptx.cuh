@@ -131,7 +131,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uin
 // ---------------------------------------------------------------- cp.async (row gathers)
 
 // 16-byte global -> shared copy through L2 only; bytes past `src_bytes`
-// (0 or 16) are zero-filled, so a row that does not exist costs no traffic.
+// (0 or 16) are zero-filled.
 __device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst_smem), "l"(src),
                "r"(src_bytes)
@@ -143,6 +143,16 @@ __device__ __forceinline__ void cp_async_16(uint32_t dst_smem, const void* src, 
 __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// Wait until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // Wait until every cp.async this thread issued has completed.
