@@ -128,9 +128,17 @@ constexpr int kGatherWarp0 = 8;    // first of the four A-loader warps
 constexpr int kGatherWarps = 4;
 constexpr int kGatherLag = 2;      // a stage is published this many stages after its copies
 
+// Epilogue warps: 4..7 read TMEM lane quarters 0..3; without GATHER_A, warps
+// 8..11 take the second half of the accumulator columns (two warps per lane
+// quarter), so the epilogue keeps pace with short main loops (w2's K = I).
+template <bool GATHER_A>
+constexpr int epi_warps() {
+  return GATHER_A ? 4 : 8;
+}
+
 template <bool GATHER_A>
 constexpr int gemm_threads() {
-  return GATHER_A ? 256 + 32 * kGatherWarps : 256;
+  return 384;
 }
 
 template <int BN, int EPI, int STAGES, bool GATHER_A = false>
@@ -166,7 +174,7 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 128);
+      mbar_init(&acc_empty[a], 32 * epi_warps<GATHER_A>());
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -353,9 +361,11 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
       const uint32_t first = it > static_cast<uint32_t>(kGatherLag) ? it - kGatherLag : 0u;
       for (uint32_t i = first; i < it; ++i) mbar_arrive(&full[i % STAGES]);
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 4 && warp < 4 + epi_warps<GATHER_A>()) {
     // -------------------------------------------------------------- epilogue
-    const int q = warp - 4;  // TMEM lane quarter owned by this warp
+    const int q = warp & 3;                 // TMEM lane quarter owned by this warp
+    constexpr int kHalves = epi_warps<GATHER_A>() / 4;
+    const int half = (warp - 4) >> 2;       // which share of the columns (0 or 0/1)
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     int it = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++it) {
@@ -375,8 +385,13 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
       if constexpr (EPI == kEpiSwiGLU) {
         __nv_bfloat16* orow = args.out + static_cast<size_t>(row) * args.out_ld + nt * (BN / 2);
         const bool st = valid && row < args.out_rows;
+        // Output columns are shared between the warps of one lane quarter when
+        // each share is at least one 32-column chunk; otherwise one warp does all.
+        constexpr int kSplit = (BN / 2 / kHalves >= 32) ? kHalves : 1;
+        constexpr int kCols = BN / 2 / kSplit;
+        static_assert(kCols % 32 == 0, "SwiGLU epilogue works in 32-column chunks");
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+        for (int c0 = half * kCols; half < kSplit && c0 < (half + 1) * kCols; c0 += 32) {
           uint32_t g[32], u[32];
           tmem_ld32(tb + c0, g);
           tmem_ld32(tb + BN / 2 + c0, u);
@@ -409,86 +424,112 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
           }
         }
         __nv_bfloat16* orow = args.out + static_cast<size_t>(st ? orow_idx : 0) * args.out_ld + nt * BN;
+        constexpr int kSplit = (BN / kHalves >= 32) ? kHalves : 1;
+        constexpr int kCols = BN / kSplit;  // accumulator columns of this warp's share
+        static_assert(kCols % 32 == 0, "store epilogue works in 32-column chunks");
+        if constexpr (kCols % 64 == 0) {
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 64) {
-          uint32_t r0[32], r1[32];
-          tmem_ld32(tb + c0, r0);
-          tmem_ld32(tb + c0 + 32, r1);
-          tc_wait_ld();
-          uint32_t pk[32];
+          for (int c0 = half * kCols; half < kSplit && c0 < (half + 1) * kCols; c0 += 64) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(tb + c0, r0);
+            tmem_ld32(tb + c0 + 32, r1);
+            tc_wait_ld();
+            uint32_t pk[32];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            pk[j] = pack_bf16x2(__uint_as_float(r0[2 * j]) * scale, __uint_as_float(r0[2 * j + 1]) * scale);
-            pk[16 + j] =
-                pack_bf16x2(__uint_as_float(r1[2 * j]) * scale, __uint_as_float(r1[2 * j + 1]) * scale);
+            for (int j = 0; j < 16; ++j) {
+              pk[j] = pack_bf16x2(__uint_as_float(r0[2 * j]) * scale,
+                                  __uint_as_float(r0[2 * j + 1]) * scale);
+              pk[16 + j] = pack_bf16x2(__uint_as_float(r1[2 * j]) * scale,
+                                       __uint_as_float(r1[2 * j + 1]) * scale);
+            }
+            if (st) {
+              uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            }
           }
-          if (st) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-          }
-        }
-      } else {
-        // Router: the row's E logits -> bf16 -> top-k (value desc, id asc) -> softmax.
-        const int E = args.b_rows;
-        uint32_t top[kRouterMaxK];
-#pragma unroll
-        for (int i = 0; i < kRouterMaxK; ++i) top[i] = 0u;  // below every real key
-        float run_max = -INFINITY, run_sum = 0.0f;  // softmax over all E (norm_topk_prob=False)
+        } else {
 #pragma unroll 1
-        for (int c0 = 0; c0 < E; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(tb + c0, r);
-          tc_wait_ld();
-          float lv[16];
+          for (int c0 = half * kCols; half < kSplit && c0 < (half + 1) * kCols; c0 += 32) {
+            uint32_t r0[32];
+            tmem_ld32(tb + c0, r0);
+            tc_wait_ld();
+            uint32_t pk[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float v = __uint_as_float(r[j]);
-            if (args.bias != nullptr) v += args.bias[c0 + j];
-            lv[j] = bf16_round_f(v);
-          }
-          if (valid && args.logits_out != nullptr) {
-            uint4* dst = reinterpret_cast<uint4*>(args.logits_out + static_cast<size_t>(row) * E + c0);
-            dst[0] = make_uint4(pack_bf16x2(lv[0], lv[1]), pack_bf16x2(lv[2], lv[3]),
-                                pack_bf16x2(lv[4], lv[5]), pack_bf16x2(lv[6], lv[7]));
-            dst[1] = make_uint4(pack_bf16x2(lv[8], lv[9]), pack_bf16x2(lv[10], lv[11]),
-                                pack_bf16x2(lv[12], lv[13]), pack_bf16x2(lv[14], lv[15]));
-          }
+            for (int j = 0; j < 16; ++j)
+              pk[j] = pack_bf16x2(__uint_as_float(r0[2 * j]) * scale,
+                                  __uint_as_float(r0[2 * j + 1]) * scale);
+            if (st) {
+              uint4* dst = reinterpret_cast<uint4*>(orow + c0);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            topk_insert(top, topk_key(lv[j], c0 + j));
-            if (!args.norm_topk_prob) {
-              const float m = fmaxf(run_max, lv[j]);
-              run_sum = run_sum * expf(run_max - m) + expf(lv[j] - m);
-              run_max = m;
+              for (int j = 0; j < 4; ++j)
+                dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
             }
           }
         }
-        if (valid) {
-          const int k = args.top_k;
-          float tv[kRouterMaxK];
-          int ti[kRouterMaxK];
-#pragma unroll
-          for (int i = 0; i < kRouterMaxK; ++i) {
-            tv[i] = topk_key_value(top[i]);
-            ti[i] = topk_key_id(top[i]);
+      } else {
+        if (half == 0) {  // one warp per lane quarter: rows are not split by columns
+          // Router: the row's E logits -> bf16 -> top-k (value desc, id asc) -> softmax.
+          const int E = args.b_rows;
+          uint32_t top[kRouterMaxK];
+  #pragma unroll
+          for (int i = 0; i < kRouterMaxK; ++i) top[i] = 0u;  // below every real key
+          float run_max = -INFINITY, run_sum = 0.0f;  // softmax over all E (norm_topk_prob=False)
+  #pragma unroll 1
+          for (int c0 = 0; c0 < E; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(tb + c0, r);
+            tc_wait_ld();
+            float lv[16];
+  #pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float v = __uint_as_float(r[j]);
+              if (args.bias != nullptr) v += args.bias[c0 + j];
+              lv[j] = bf16_round_f(v);
+            }
+            if (valid && args.logits_out != nullptr) {
+              uint4* dst = reinterpret_cast<uint4*>(args.logits_out + static_cast<size_t>(row) * E + c0);
+              dst[0] = make_uint4(pack_bf16x2(lv[0], lv[1]), pack_bf16x2(lv[2], lv[3]),
+                                  pack_bf16x2(lv[4], lv[5]), pack_bf16x2(lv[6], lv[7]));
+              dst[1] = make_uint4(pack_bf16x2(lv[8], lv[9]), pack_bf16x2(lv[10], lv[11]),
+                                  pack_bf16x2(lv[12], lv[13]), pack_bf16x2(lv[14], lv[15]));
+            }
+  #pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              topk_insert(top, topk_key(lv[j], c0 + j));
+              if (!args.norm_topk_prob) {
+                const float m = fmaxf(run_max, lv[j]);
+                run_sum = run_sum * expf(run_max - m) + expf(lv[j] - m);
+                run_max = m;
+              }
+            }
           }
-          float den = 0.0f, ref = tv[0];
-          if (args.norm_topk_prob) {
-#pragma unroll
-            for (int i = 0; i < kRouterMaxK; ++i)
-              if (i < k) den += expf(tv[i] - ref);
-          } else {
-            den = run_sum;
-            ref = run_max;
-          }
-          const float inv = 1.0f / den;
-#pragma unroll
-          for (int i = 0; i < kRouterMaxK; ++i) {
-            if (i < k) {
-              args.ids_out[static_cast<size_t>(row) * k + i] = ti[i];
-              args.w_out[static_cast<size_t>(row) * k + i] = expf(tv[i] - ref) * inv;
+          if (valid) {
+            const int k = args.top_k;
+            float tv[kRouterMaxK];
+            int ti[kRouterMaxK];
+  #pragma unroll
+            for (int i = 0; i < kRouterMaxK; ++i) {
+              tv[i] = topk_key_value(top[i]);
+              ti[i] = topk_key_id(top[i]);
+            }
+            float den = 0.0f, ref = tv[0];
+            if (args.norm_topk_prob) {
+  #pragma unroll
+              for (int i = 0; i < kRouterMaxK; ++i)
+                if (i < k) den += expf(tv[i] - ref);
+            } else {
+              den = run_sum;
+              ref = run_max;
+            }
+            const float inv = 1.0f / den;
+  #pragma unroll
+            for (int i = 0; i < kRouterMaxK; ++i) {
+              if (i < k) {
+                args.ids_out[static_cast<size_t>(row) * k + i] = ti[i];
+                args.w_out[static_cast<size_t>(row) * k + i] = expf(tv[i] - ref) * inv;
+              }
             }
           }
         }
