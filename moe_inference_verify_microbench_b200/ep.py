@@ -42,11 +42,11 @@ class CudaKernels:
     def expert_compute(src, index, index_div, s, w_gate, w_up, w_down, row_map=None,
                        slot_scale=None, out_rows=None):
         """SwiGLU experts on rows src[index[p] // index_div] of the sorted order
-        (gather fused into the w13 GEMM), w2 output to row_map[p] scaled by
-        slot_scale[row_map[p]]."""
-        M = index.numel()
-        h = ops.grouped_w13_swiglu_gather(src, index, index_div, M, s.tiles, s.num_tiles,
-                                          s.max_tiles, w_gate, w_up)
+        (rows past the sort's valid count are neither gathered nor computed), w2
+        output to row_map[p] scaled by slot_scale[row_map[p]]."""
+        e_local = s.counts.numel()
+        xs = ops.gather_rows(src, index, index_div, count=s.offsets[e_local:])
+        h = ops.grouped_w13_swiglu(xs, s.tiles, s.num_tiles, s.max_tiles, w_gate, w_up)
         return ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, w_down, row_map=row_map,
                               slot_scale=slot_scale, out_rows=out_rows)
 
@@ -127,31 +127,57 @@ class EPSparseMoELean(_EPBase):
 
 def dispatch_combine(mod: _EPBase, local_x: torch.Tensor, group) -> torch.Tensor:
     """The all_to_all EP core shared by C7 (C7/python/solution.py:120-269) and
-    C8's MoE (C8/python/solution.py:171-224), on this rank's tokens."""
+    C8's MoE (C8/python/solution.py:171-224), on this rank's tokens.
+
+    The reference dispatches k copies of every token (one per routing record,
+    C7:167,201).  Here a token travels once to each rank that owns at least
+    one of its experts, with its (local expert, weight) list; the owner runs
+    every record of the row through the grouped GEMMs, sums them with their
+    weights, and returns one partial row per (token, rank), which the sender
+    sums.  Same collectives in the same order (counts, dispatch, combine) and
+    the same result; the rows on the wire drop from k per token to the number
+    of distinct owner ranks per token.
+    """
     K = mod._kernels
-    N, k, E, epr = local_x.shape[0], mod.top_k, mod.num_experts, mod.experts_per_rank
+    N, k, E, epr, ep = local_x.shape[0], mod.top_k, mod.num_experts, mod.experts_per_rank, mod.ep_size
+    dev = local_x.device
     ids, w = mod._route(local_x)                                       # local router (C7:141-146)
-    s = K.sort_align(ids, E, want_inv=True)                           # sort by global id (C7:162)
-    xs = K.gather_rows(local_x, s.perm, k)                            # (C7:167)
-    sorted_eids = ids.reshape(-1).index_select(0, s.perm.long())
-    bounds = s.offsets[0::epr].to(torch.int64)                        # per-destination splits
-    send = bounds[1:] - bounds[:-1]                                   # (C7:186-187)
+    # Send plan: key each (token n, rank r) pair with r if one of n's experts lives
+    # on r, else the sentinel ep; a stable sort by key gives the per-rank counts,
+    # the send order (rank-major, token order inside) and each pair's position.
+    dest = ids.long() // epr                                           # owner of each record
+    sent = torch.zeros((N, ep), dtype=torch.bool, device=dev)
+    sent.scatter_(1, dest, True)
+    ranks = torch.arange(ep, dtype=torch.int32, device=dev)
+    keys = torch.where(sent, ranks, torch.full_like(ranks, ep))
+    plan = K.sort_align(keys, ep + 1, 0, ep, want_inv=True)
+    send = plan.counts.to(torch.int64)                                 # rows per destination
     recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send, group=group)                   # count exchange (C7:190)
     send_l, recv_l = send.tolist(), recv.tolist()                     # host sync (C7:199-200)
+    total = int(sum(send_l))
+    pair = plan.perm[:total].long()                                    # n * ep + r per send row
+    tok = pair // ep
+    rank_of = pair - tok * ep
+    own = dest.index_select(0, tok) == rank_of[:, None]
+    meta_e = torch.where(own, ids.index_select(0, tok) - (rank_of * epr)[:, None].to(torch.int32),
+                         torch.full_like(ids[:1], epr)).to(torch.int32)
+    meta_w = w.index_select(0, tok) * own
+    xs = K.gather_rows(local_x, plan.perm, ep, count=plan.offsets[ep:])[:total]
     recv_x = all_to_all_variable(xs, send_l, recv_l, group)           # dispatch (C7:201)
-    recv_e = all_to_all_variable(sorted_eids, send_l, recv_l, group)  # (C7:203)
+    recv_e = all_to_all_variable(meta_e, send_l, recv_l, group)       # (C7:203)
+    recv_w = all_to_all_variable(meta_w, send_l, recv_l, group)
     n_recv = recv_x.shape[0]
     wg, wu, wd = mod.pack()
     if n_recv > 0:
-        s2 = K.sort_align(recv_e, E, mod.expert_start, epr)           # local re-sort (C7:224-226)
-        y_t = K.expert_compute(recv_x, s2.perm, 1, s2, wg, wu, wd,    # back to received order
-                               row_map=s2.perm, out_rows=n_recv)      # (C7:227-236)
+        s2 = K.sort_align(recv_e, epr + 1, 0, epr, want_inv=True)    # local re-sort (C7:224-226);
+        out = K.expert_compute(recv_x, s2.perm, k, s2, wg, wu, wd)    # id epr marks "not mine"
+        partial = K.combine(out, n_recv, k, slot_src=s2.inv,          # weighted sum of the row's
+                            slot_w=recv_w.reshape(-1))                # records (C7:259-261)
     else:
-        y_t = recv_x.new_empty((0, local_x.shape[1]))
-    y_ret = all_to_all_variable(y_t, recv_l, send_l, group)           # combine (C7:258)
-    return K.combine(y_ret, N, k, slot_src=s.inv, slot_w=w.reshape(-1))  # weight + index_add_
-    # (C7:259-261)
+        partial = recv_x.new_empty((0, local_x.shape[1]))
+    back = all_to_all_variable(partial, recv_l, send_l, group)        # combine (C7:258)
+    return K.combine(back, N, ep, slot_src=plan.inv)                  # sum over owner ranks (ep <= 8)
 
 
 class EPSparseMoEPure(_EPBase):

@@ -12,6 +12,7 @@ from __future__ import annotations
 import datetime
 import json
 import os
+import sys
 import time
 
 import torch
@@ -45,7 +46,19 @@ def run_ep(args, metric, config_block, clock_sampler_cls, _make_inputs) -> None:
     local = int(os.environ.get("LOCAL_RANK", str(rank)))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    # NCCL prints its version on stdout while communicators come up; keep stdout
+    # for the one JSON line by pointing file descriptor 1 at stderr meanwhile.
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.barrier()
+        torch.cuda.synchronize()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
     try:
         _run(args, metric, config_block, clock_sampler_cls, rank, world, dev)
         dist.barrier()
