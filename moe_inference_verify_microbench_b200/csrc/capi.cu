@@ -183,18 +183,31 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                    int* offsets, int* perm, int4* tiles, int* num_tiles, void* sorted_x, void* h,
                    void* slots) {
                  const int R = static_cast<int>(p.R);
-                 rc = launch_router(x, router_weight, router_bias, T, H, E, top_k, norm_topk_prob,
-                                    ids, w, nullptr, status, stream);
-                 if (rc == kRcOk)
-                   rc = launch_sort_align(ids, R, E, 0, E, MOE_BLOCK_M, sort_ws, counts, offsets,
-                                          nullptr, perm, nullptr, tiles, p.max_tiles, num_tiles,
-                                          status, stream);
-                 if (rc == kRcOk)
+                 const bool small = use_gemv_w13(R);  // decode: weight-streaming kernels
+                 if (small && use_router_small(T, H, E, top_k)) {
+                   rc = launch_router_sort_small(x, router_weight, router_bias, T, H, E, top_k,
+                                                 norm_topk_prob, ids, w, nullptr, counts, offsets,
+                                                 perm, tiles, p.max_tiles, num_tiles, status,
+                                                 stream);
+                 } else {
+                   rc = launch_router(x, router_weight, router_bias, T, H, E, top_k,
+                                      norm_topk_prob, ids, w, nullptr, status, stream);
+                   if (rc == kRcOk)
+                     rc = launch_sort_align(ids, R, E, 0, E, MOE_BLOCK_M, sort_ws, counts,
+                                            offsets, nullptr, perm, nullptr, tiles, p.max_tiles,
+                                            num_tiles, status, stream);
+                 }
+                 if (rc == kRcOk && small) {
+                   rc = launch_w13_swiglu_gather(x, T, perm, top_k, R, tiles, num_tiles,
+                                                 p.max_tiles, w_gate, w_up, E, H, I, h, status,
+                                                 stream);
+                 } else if (rc == kRcOk) {
                    rc = launch_gather_rows(x, T, perm, R, nullptr, top_k, H, sorted_x, status,
                                            stream);
-                 if (rc == kRcOk)
-                   rc = launch_w13_swiglu(sorted_x, R, tiles, num_tiles, p.max_tiles, w_gate, w_up,
-                                          E, H, I, h, status, stream);
+                   if (rc == kRcOk)
+                     rc = launch_w13_swiglu(sorted_x, R, tiles, num_tiles, p.max_tiles, w_gate,
+                                            w_up, E, H, I, h, status, stream);
+                 }
                  if (rc == kRcOk)
                    rc = launch_w2(h, R, tiles, num_tiles, p.max_tiles, w_down, E, H, I, perm, w,
                                   slots, R, status, stream);

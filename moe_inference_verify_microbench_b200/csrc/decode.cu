@@ -1,0 +1,658 @@
+// Small-batch (decode) kernels of the MoE layer.  At a few routing records per
+// expert the layer is a stream of the routed experts' weights; a 128-row
+// tensor-core tile would idle there, so these kernels stream weight rows
+// through shared memory with the bulk-copy engine and apply each row to all
+// records of its expert on the CUDA cores.
+//
+//   router_sort_small  one 8-CTA cluster.  Each CTA stages the T tokens in shared
+//                      memory; each warp holds one expert's router row in
+//                      registers and dots it with every token; the logits meet in
+//                      CTA 0's shared memory over distributed shared memory; CTA 0
+//                      takes the top-k per token (one warp per token, same key
+//                      order as the tensor-core router: value descending, lower
+//                      expert id first) and, when asked, runs the one-CTA sort of
+//                      sort_block.cuh on the fresh ids, so router + sort_align is
+//                      one launch (C5/python/solution.py:124-136).
+//   gemv_stream<true>  h[p] = silu(A[p] . Wg[e]) * (A[p] . Wu[e]), A[p] =
+//                      src[index[p] / index_div] (C5/python/solution.py:79-80)
+//   gemv_stream<false> out[row_map[p]] = row_scale[row_map[p]] * (h[p] . Wd[e])
+//                      (C5/python/solution.py:80,158)
+//
+// gemv_stream is persistent, one CTA per SM.  Work item = (tile of the sort's
+// tile table, block of output rows); every CTA takes a contiguous
+// range of items, computed on the device from the tile count, so the host never
+// synchronises.  One producer thread copies each item's weight rows (contiguous
+// in memory: rows rb*B..rb*B+B-1 of expert e) into a ring of shared-memory
+// stages; eight consumer warps own one output row each and dot it with the
+// item's records (A rows read through L1).
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <atomic>
+
+#include "grouped_gemm.cuh"
+#include "internal.h"
+#include "sort_block.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace moe {
+
+constexpr int kRouterCluster = 8;
+constexpr int kRouterThreads = kSortThreads;  // CTA 0 also runs the one-CTA sort
+constexpr int kRouterWarps = kRouterThreads / 32;
+constexpr int kRouterSmallMaxT = 16;
+constexpr int kRouterMaxVecPerLane = 16;      // H <= 32 * 16 * 8 = 4096
+constexpr int kGemvConsumerWarps = 8;
+constexpr int kGemvThreads = 32 * (kGemvConsumerWarps + 1);  // + one producer warp
+// Output rows per work item: one per consumer warp for the gate/up pair, four
+// for the down projection (whose rows are short).
+template <bool SWIGLU>
+constexpr int gemv_rows_per_warp() {
+  return SWIGLU ? 1 : 4;
+}
+template <bool SWIGLU>
+constexpr int gemv_row_block() {
+  return kGemvConsumerWarps * gemv_rows_per_warp<SWIGLU>();
+}
+constexpr int kGemvMaxRecs = 8;     // records sharing one pass over a weight row
+constexpr int kGemvRingBytes = 192 * 1024;
+constexpr int kGemvMaxStages = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Mixed-precision FMA: fma.rn.f32.bf16 multiplies two bf16 values exactly and
+// adds them to an fp32 accumulator with one rounding, so weights and
+// activations are used as stored, without conversion instructions.
+__device__ __forceinline__ void fma_bf16x2(float& lo, float& hi, uint32_t w, uint32_t x) {
+  asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\t"
+      "mov.b32 {wl, wh}, %2;\n\t"
+      "mov.b32 {xl, xh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, wl, xl, %0;\n\t"
+      "fma.rn.f32.bf16 %1, wh, xh, %1;\n\t}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(w), "r"(x));
+}
+
+// acc[0..3] += the 8-element dot product of w and x, over four dependency chains.
+__device__ __forceinline__ void dot8_acc(const uint4& w, const uint4& x, float* acc) {
+  fma_bf16x2(acc[0], acc[1], w.x, x.x);
+  fma_bf16x2(acc[2], acc[3], w.y, x.y);
+  fma_bf16x2(acc[0], acc[1], w.z, x.z);
+  fma_bf16x2(acc[2], acc[3], w.w, x.w);
+}
+
+__device__ __forceinline__ float acc_sum(const float* acc) {
+  return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
+// ------------------------------------------------------------------ router
+
+__global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouterThreads, 1)
+    router_sort_small(const uint4* __restrict__ x, const uint4* __restrict__ wr,
+                      const float* __restrict__ bias, int T, int vec_per_row, int E, int k,
+                      int norm_topk_prob, int* __restrict__ ids_out, float* __restrict__ w_out,
+                      __nv_bfloat16* __restrict__ logits_out, int* counts, int* offsets,
+                      int* perm, int4* tiles, int max_tiles, int* num_tiles, int* status) {
+  __shared__ float logits[kRouterSmallMaxT * kSortThreads];  // [expert][token], rank 0 only
+  __shared__ int sid[kRouterSmallMaxT * kRouterMaxK];
+  extern __shared__ __align__(16) uint4 dyn[];
+  uint4* xs = dyn;                                            // [T][vec_per_row]
+  int* sort_sm = reinterpret_cast<int*>(dyn + static_cast<size_t>(T) * vec_per_row);
+  cg::cluster_group cluster = cg::this_cluster();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    const int n = T * vec_per_row;
+    int i = threadIdx.x;
+    for (; i + 3 * kRouterThreads < n; i += 4 * kRouterThreads) {  // four loads in flight
+      const uint4 v0 = __ldg(x + i), v1 = __ldg(x + i + kRouterThreads);
+      const uint4 v2 = __ldg(x + i + 2 * kRouterThreads), v3 = __ldg(x + i + 3 * kRouterThreads);
+      xs[i] = v0;
+      xs[i + kRouterThreads] = v1;
+      xs[i + 2 * kRouterThreads] = v2;
+      xs[i + 3 * kRouterThreads] = v3;
+    }
+    for (; i < n; i += kRouterThreads) xs[i] = __ldg(x + i);
+  }
+  __syncthreads();
+
+  // Warp = one expert row held in registers; tokens one by one.
+  const int per_cta = E / kRouterCluster;
+  float* dst = cluster.map_shared_rank(logits, 0);
+  for (int el = warp; el < per_cta; el += kRouterWarps) {
+    const int e = static_cast<int>(cluster.block_rank()) * per_cta + el;
+    const uint4* row = wr + static_cast<size_t>(e) * vec_per_row;
+    uint4 wv[kRouterMaxVecPerLane];
+#pragma unroll
+    for (int j = 0; j < kRouterMaxVecPerLane; ++j) {
+      const int v = lane + 32 * j;
+      wv[j] = v < vec_per_row ? __ldg(row + v) : make_uint4(0, 0, 0, 0);
+    }
+    const float be = bias != nullptr ? bias[e] : 0.0f;
+#pragma unroll 1
+    for (int t = 0; t < T; ++t) {
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const uint4* xr = xs + t * vec_per_row;
+#pragma unroll
+      for (int j = 0; j < kRouterMaxVecPerLane; ++j) {
+        const int v = lane + 32 * j;
+        if (v < vec_per_row) dot8_acc(wv[j], xr[v], acc);
+      }
+      const float sum = warp_sum(acc_sum(acc));
+      if (lane == 0) {
+        const float b = bf16_round_f(sum + be);
+        dst[e * T + t] = b;
+        if (logits_out != nullptr) logits_out[static_cast<size_t>(t) * E + e] = __float2bfloat16_rn(b);
+      }
+    }
+  }
+  cluster.sync();  // every CTA's logits are in CTA 0's shared memory
+  if (cluster.block_rank() != 0) return;
+
+  for (int t = warp; t < T; t += kRouterWarps) {
+    uint32_t top[kRouterMaxK];
+#pragma unroll
+    for (int i = 0; i < kRouterMaxK; ++i) top[i] = 0u;  // below every real key
+    for (int c = lane; c < E; c += 32) topk_insert(top, topk_key(logits[c * T + t], c));
+    uint32_t sel[kRouterMaxK];
+#pragma unroll
+    for (int i = 0; i < kRouterMaxK; ++i) {
+      // Keys are unique (the id is part of the key): exactly one lane holds the max.
+      const uint32_t m = __reduce_max_sync(0xffffffffu, top[0]);
+      sel[i] = m;
+      if (top[0] == m) {
+#pragma unroll
+        for (int j = 0; j + 1 < kRouterMaxK; ++j) top[j] = top[j + 1];
+        top[kRouterMaxK - 1] = 0u;
+      }
+    }
+    const float ref = topk_key_value(sel[0]);
+    float den = 0.0f;
+    if (norm_topk_prob) {
+#pragma unroll
+      for (int i = 0; i < kRouterMaxK; ++i)
+        if (i < k) den += expf(topk_key_value(sel[i]) - ref);
+    } else {
+      for (int c = lane; c < E; c += 32) den += expf(logits[c * T + t] - ref);
+      den = warp_sum(den);
+    }
+    const float inv = 1.0f / den;
+#pragma unroll
+    for (int i = 0; i < kRouterMaxK; ++i) {
+      if (i < k && lane == i) {
+        const int id = topk_key_id(sel[i]);
+        ids_out[t * k + i] = id;
+        w_out[t * k + i] = expf(topk_key_value(sel[i]) - ref) * inv;
+        sid[t * k + i] = id;
+      }
+    }
+  }
+  if (perm == nullptr) return;  // block-uniform: router only
+  __syncthreads();
+  sort_small_block(sid, T * k, E, 0, E, kBM, counts, offsets, nullptr, perm, nullptr, tiles,
+                   max_tiles, num_tiles, status, sort_sm);
+}
+
+// ------------------------------------------------------------------ streamed GEMV
+
+struct StreamArgs {
+  const uint4* act;      // A operand rows [act_rows][K]
+  int act_rows;
+  const int* index;      // A row of record p = act[index[p] / index_div] (null = p)
+  int index_div;
+  int M;                 // records
+  const int4* tiles;
+  const int* num_tiles;
+  int max_tiles;
+  const __nv_bfloat16* w0;  // [E][N][K]: gate (SwiGLU) or down weight
+  const __nv_bfloat16* w1;  // [E][N][K]: up (SwiGLU only)
+  int E, K, N;
+  __nv_bfloat16* out;
+  const int* row_map;       // down: out row of record p (null = p)
+  const float* row_scale;   // down: scale indexed by the out row (null = 1)
+  int out_rows;
+  int stages;
+  int* status;
+};
+
+// One warp's pass over ROWS weight rows of a stage (row j at w + j * rstride,
+// in uint4 units) for n <= NR records whose A rows are act[rows[r]], over CH
+// dependency chains per (row, record).
+template <int ROWS, int NR, int CH>
+__device__ __forceinline__ void stage_dots(const uint4* w, int rstride,
+                                           const uint4* __restrict__ act, const int* rows, int n,
+                                           int vec, int lane, float (&acc)[ROWS][NR][CH]) {
+  static_assert(CH == 2 || CH == 4, "two or four chains");
+#pragma unroll
+  for (int j = 0; j < ROWS; ++j)
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+      for (int c = 0; c < CH; ++c) acc[j][r][c] = 0.0f;
+#pragma unroll 2
+  for (int v = lane; v < vec; v += 32) {
+    uint4 wv[ROWS];
+#pragma unroll
+    for (int j = 0; j < ROWS; ++j) wv[j] = w[j * rstride + v];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      if (r < n) {
+        const uint4 xv = __ldg(act + static_cast<size_t>(rows[r]) * vec + v);
+#pragma unroll
+        for (int j = 0; j < ROWS; ++j) {
+          float* c = acc[j][r];
+          fma_bf16x2(c[0], c[1], wv[j].x, xv.x);
+          fma_bf16x2(c[CH - 2], c[CH - 1], wv[j].y, xv.y);
+          fma_bf16x2(c[0], c[1], wv[j].z, xv.z);
+          fma_bf16x2(c[CH - 2], c[CH - 1], wv[j].w, xv.w);
+        }
+      }
+    }
+  }
+}
+
+// Warp reduction of v[j][r] over the 32 lanes, scattered over records: after
+// it, v[j][0] of lane L holds the full sum for record reduced_record<NR>(L),
+// for every row j.  Halving steps exchange half of the remaining records with
+// the lane `o` apart (ROWS * (NR - 1) shuffles in all), then plain butterfly
+// steps finish the sums.
+template <int NR>
+__device__ __forceinline__ int reduced_record(int lane) {
+  int r = 0;
+#pragma unroll
+  for (int k = 0; (NR >> k) > 1; ++k)
+    if (lane & (16 >> k)) r += NR >> (k + 1);
+  return r;
+}
+
+template <int ROWS, int NR>
+__device__ __forceinline__ void reduce_records(float (&v)[ROWS][NR], int lane) {
+#pragma unroll
+  for (int k = 0; (NR >> k) > 1; ++k) {
+    const int h = NR >> (k + 1);
+    const int o = 16 >> k;
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int j = 0; j < ROWS; ++j)
+#pragma unroll
+      for (int i = 0; i < NR / 2; ++i) {
+        if (i < h) {
+          const float keep = upper ? v[j][i + h] : v[j][i];
+          const float send = upper ? v[j][i] : v[j][i + h];
+          v[j][i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+  }
+#pragma unroll
+  for (int o = 16 / NR; o >= 1; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < ROWS; ++j) v[j][0] += __shfl_xor_sync(0xffffffffu, v[j][0], o);
+}
+
+// Gate/up: rows 0 and 1 are the gate and up rows of output row `row`; down:
+// rows j = 0..ROWS-1 are output rows row + j * kGemvConsumerWarps.  Both sit
+// kGemvConsumerWarps rows apart in the stage.
+template <bool SWIGLU, int NR>
+__device__ __forceinline__ void gemv_pass(const StreamArgs& a, const uint4* w, int p0, int n,
+                                          int row, const int* rows, int my_out, float my_scale,
+                                          int bad, int vec, int lane) {
+  constexpr int ROWS = SWIGLU ? 2 : gemv_rows_per_warp<false>();
+  constexpr int CH = ROWS * NR >= 16 ? 2 : 4;
+  float acc[ROWS][NR][CH];
+  stage_dots<ROWS, NR, CH>(w, kGemvConsumerWarps * vec, a.act, rows, n, vec, lane, acc);
+  float v[ROWS][NR];
+#pragma unroll
+  for (int j = 0; j < ROWS; ++j)
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      float t = acc[j][r][0] + acc[j][r][1];
+      if (CH == 4) t += acc[j][r][CH - 2] + acc[j][r][CH - 1];
+      v[j][r] = t;
+    }
+  reduce_records<ROWS, NR>(v, lane);
+  const int r = reduced_record<NR>(lane);
+  const int o = __shfl_sync(0xffffffffu, my_out, r);
+  const float sc = __shfl_sync(0xffffffffu, my_scale, r);
+  const int rbad = __shfl_sync(0xffffffffu, bad, r);
+  const bool writer = (lane & (32 / NR - 1)) == 0 && r < n && !rbad;
+  if (writer) {
+    if (SWIGLU) {
+      a.out[static_cast<size_t>(p0 + r) * a.N + row] = __float2bfloat16_rn(silu_f(v[0][0]) * v[1][0]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < ROWS; ++j)
+        a.out[static_cast<size_t>(o) * a.N + row + j * kGemvConsumerWarps] =
+            __float2bfloat16_rn(v[j][0] * sc);
+    }
+  }
+}
+
+// Cost of one work item of a tile, in units of one record's dot products: the
+// weight rows stream at a fixed cost, each record of the tile adds one unit.
+constexpr long long kItemCost0 = 4;
+
+__device__ __forceinline__ long long item_cost(const StreamArgs& a, int i) {
+  const int4 t = a.tiles[i];
+  const int n = (t.z > t.y && t.y >= 0) ? min(t.z - t.y, a.M) : 0;  // bad tiles are reported later
+  return kItemCost0 + n;
+}
+
+// Inclusive scan of v over the block (every thread calls it); *total gets the
+// block's sum.
+__device__ __forceinline__ long long block_scan_ll(long long v, long long* sh, long long* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long y = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += y;
+  }
+  if (lane == 31) sh[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    long long w = lane < nw ? sh[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < nw) sh[lane] = w;
+  }
+  __syncthreads();
+  const long long res = v + (warp > 0 ? sh[warp - 1] : 0);
+  *total = sh[nw - 1];
+  __syncthreads();
+  return res;
+}
+
+// This CTA's contiguous item range [*lo, *hi): items are ordered (tile, row
+// block) and the ranges split the summed item cost evenly over the grid, so a
+// CTA that meets tiles with many records gets fewer items.
+__device__ void balanced_range(const StreamArgs& a, int nt, int blocks, long long* lo,
+                               long long* hi) {
+  __shared__ long long sh_scan[32];
+  __shared__ long long sh_range[2];
+  const long long total_items = static_cast<long long>(nt) * blocks;
+  if (threadIdx.x == 0) sh_range[0] = sh_range[1] = total_items;
+  const int nthr = blockDim.x;
+  long long C = 0;
+  long long my_cost = 0;  // item cost of this thread's tile when nt <= nthr
+  if (nt <= nthr) {
+    my_cost = static_cast<int>(threadIdx.x) < nt ? item_cost(a, threadIdx.x) : 0;
+  } else {
+    long long mine = 0;
+    for (int i = threadIdx.x; i < nt; i += nthr) mine += item_cost(a, i) * blocks;
+    block_scan_ll(mine, sh_scan, &C);
+  }
+  long long carry = 0;
+  for (int base = 0; base < nt; base += nthr) {
+    const int i = base + static_cast<int>(threadIdx.x);
+    const long long ci = nt <= nthr ? my_cost : (i < nt ? item_cost(a, i) : 0);
+    long long chunk = 0;
+    const long long incl = block_scan_ll(ci * blocks, sh_scan, &chunk) + carry;
+    if (nt <= nthr) C = chunk;  // one chunk: its total is the grand total
+    const long long excl = incl - ci * blocks;
+    const long long lo_c = C * blockIdx.x / gridDim.x;
+    const long long hi_c = C * (blockIdx.x + 1) / gridDim.x;
+    if (i < nt) {
+      if (excl <= lo_c && lo_c < incl) sh_range[0] = static_cast<long long>(i) * blocks + (lo_c - excl + ci - 1) / ci;
+      if (excl <= hi_c && hi_c < incl) sh_range[1] = static_cast<long long>(i) * blocks + (hi_c - excl + ci - 1) / ci;
+    }
+    carry += chunk;
+  }
+  __syncthreads();
+  *lo = sh_range[0];
+  *hi = sh_range[1];
+}
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int vec = a.K / 8;
+  constexpr int kRB = gemv_row_block<SWIGLU>();
+  const uint32_t mat_bytes = static_cast<uint32_t>(kRB) * a.K * 2;  // one matrix's rows
+  const uint32_t stage_bytes = (SWIGLU ? 2u : 1u) * mat_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + a.stages * stage_bytes);
+  uint64_t* empty = full + kGemvMaxStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kGemvMaxStages);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGemvConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int nt = max(0, min(*a.num_tiles, a.max_tiles));
+  const int blocks = a.N / kRB;
+  long long lo, hi;
+  balanced_range(a, nt, blocks, &lo, &hi);
+
+  if (warp == kGemvConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, issued = 0;
+      for (long long w = lo; w < hi; ++w) {
+        const int ti = static_cast<int>(w / blocks);
+        const int rb = static_cast<int>(w - static_cast<long long>(ti) * blocks);
+        const int4 t = a.tiles[ti];
+        if (t.x < 0 || t.x >= a.E || t.y < 0 || t.y > t.z || t.z > a.M) break;  // consumers report
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.status, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        const size_t row0 = (static_cast<size_t>(t.x) * a.N + static_cast<size_t>(rb) * kRB) * a.K;
+        uint8_t* dst = smem_raw + s * stage_bytes;
+        bulk_load(dst, a.w0 + row0, mat_bytes, &full[s]);
+        if (SWIGLU) bulk_load(dst + mat_bytes, a.w1 + row0, mat_bytes, &full[s]);
+        ++issued;
+        if (++s == a.stages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      if (*abort_flag) {
+        // Let every copy still in flight land before the CTA exits.
+        const uint32_t first = issued > static_cast<uint32_t>(a.stages) ? issued - a.stages : 0u;
+        for (uint32_t i = first; i < issued; ++i) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[i % a.stages], (i / a.stages) & 1u)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  // Lane r < n holds record p0 + r's A row, out row and scale; a tile of at
+  // most kGemvMaxRecs records keeps them across its items.
+  int cached_ti = -1;
+  int my_row = 0, my_out = 0, bad = 0;
+  float my_scale = 1.0f;
+  auto fetch = [&](int p0, int n) {
+    my_row = my_out = bad = 0;
+    my_scale = 1.0f;
+    if (lane < n) {
+      const int p = p0 + lane;
+      if (SWIGLU) {
+        my_row = a.index != nullptr ? a.index[p] / a.index_div : p;
+        bad = my_row < 0 || my_row >= a.act_rows;
+        if (bad) my_row = 0;
+      } else {
+        my_row = p;
+        my_out = a.row_map != nullptr ? a.row_map[p] : p;
+        bad = my_out < 0 || my_out >= a.out_rows;
+        if (!bad && a.row_scale != nullptr) my_scale = a.row_scale[my_out];
+      }
+    }
+    if (__any_sync(0xffffffffu, bad) && lane == 0) record_status(a.status, kErrBadRow);
+  };
+  int s = 0;
+  uint32_t ph = 0;
+  for (long long w = lo; w < hi; ++w) {
+    const int ti = static_cast<int>(w / blocks);
+    const int rb = static_cast<int>(w - static_cast<long long>(ti) * blocks);
+    const int4 t = a.tiles[ti];
+    if (t.x < 0 || t.x >= a.E || t.y < 0 || t.y > t.z || t.z > a.M) {
+      if (threadIdx.x == 0) record_status(a.status, t.x < 0 || t.x >= a.E ? kErrBadExpert : kErrBadRow);
+      break;
+    }
+    const bool single = t.z - t.y <= kGemvMaxRecs;
+    if (!single || ti != cached_ti) {
+      fetch(t.y, min(kGemvMaxRecs, t.z - t.y));
+      cached_ti = single ? ti : -1;
+    }
+    if (!mbar_wait(&full[s], ph, abort_flag, a.status, kErrTimeoutFull)) return;
+    const uint4* w0 = reinterpret_cast<const uint4*>(smem_raw + s * stage_bytes) + warp * vec;
+    const int row = rb * kRB + warp;  // this warp's (first) output row
+    for (int p0 = t.y; p0 < t.z; p0 += kGemvMaxRecs) {
+      const int n = min(kGemvMaxRecs, t.z - p0);
+      if (p0 != t.y) fetch(p0, n);
+      int rows[kGemvMaxRecs];
+#pragma unroll
+      for (int r = 0; r < kGemvMaxRecs; ++r) rows[r] = __shfl_sync(0xffffffffu, my_row, r);
+      if (n == 1) gemv_pass<SWIGLU, 1>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
+      else if (n == 2) gemv_pass<SWIGLU, 2>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
+      else if (n <= 4) gemv_pass<SWIGLU, 4>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
+      else gemv_pass<SWIGLU, 8>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (++s == a.stages) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ launchers
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kRouterMaxDynSmem = 160 * 1024;
+constexpr int kGemvMaxDynSmem = kGemvRingBytes + 2 * kGemvMaxStages * 8 + 16;
+
+// Raise a kernel's dynamic shared memory limit to `bytes`, once per device.
+template <class Kernel>
+static bool allow_smem(Kernel* fn, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((done.load(std::memory_order_acquire) & bit) != 0) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return false;
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return true;
+}
+
+static size_t router_dyn_smem(int T, int H, int E) {
+  return static_cast<size_t>(T) * H * 2 + static_cast<size_t>(E) * (1 + kSortThreads / 32) * sizeof(int);
+}
+
+bool router_small_ok(int T, int H, int E, int k) {
+  return T >= 1 && T <= kRouterSmallMaxT && (H % 8) == 0 && H <= 32 * 8 * kRouterMaxVecPerLane &&
+         (E % kRouterCluster) == 0 && E <= kSortThreads && k >= 1 && k <= kRouterMaxK && k <= E &&
+         router_dyn_smem(T, H, E) <= kRouterMaxDynSmem;
+}
+
+int launch_router_sort_small(const void* x, const void* wr, const float* bias, int T, int H, int E,
+                             int k, int norm_topk_prob, int* ids_out, float* w_out,
+                             void* logits_out, int* counts, int* offsets, int* perm, int4* tiles,
+                             int max_tiles, int* num_tiles, int* status, cudaStream_t stream) {
+  if (!router_small_ok(T, H, E, k) || !aligned16(x) || !aligned16(wr)) return kRcUnsupported;
+  const size_t sh = router_dyn_smem(T, H, E);
+  static std::atomic<uint64_t> attr{0};
+  if (!allow_smem(router_sort_small, kRouterMaxDynSmem, attr)) return kRcCudaError;
+  router_sort_small<<<kRouterCluster, kRouterThreads, sh, stream>>>(
+      static_cast<const uint4*>(x), static_cast<const uint4*>(wr), bias, T, H / 8, E, k,
+      norm_topk_prob, ids_out, w_out, static_cast<__nv_bfloat16*>(logits_out), counts, offsets,
+      perm, tiles, max_tiles, num_tiles, status);
+  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+static int gemv_stages(int K, bool swiglu) {
+  const long long rb = swiglu ? gemv_row_block<true>() : gemv_row_block<false>();
+  const long long stage = (swiglu ? 2LL : 1LL) * rb * K * 2;
+  return static_cast<int>(std::min<long long>(kGemvMaxStages, kGemvRingBytes / stage));
+}
+
+bool gemv_ok(int n_out, int K, bool swiglu) {
+  const int rb = swiglu ? gemv_row_block<true>() : gemv_row_block<false>();
+  return n_out > 0 && (n_out % rb) == 0 && K > 0 && (K % 8) == 0 &&
+         gemv_stages(K, swiglu) >= 2;
+}
+
+template <bool SWIGLU>
+static int launch_stream(StreamArgs a, cudaStream_t stream) {
+  a.stages = gemv_stages(a.K, SWIGLU);
+  const size_t stage = (SWIGLU ? 2u : 1u) * static_cast<size_t>(gemv_row_block<SWIGLU>()) * a.K * 2;
+  const size_t sh = a.stages * stage + 2 * kGemvMaxStages * sizeof(uint64_t) + 16;
+  static std::atomic<uint64_t> attr{0};
+  if (!allow_smem(gemv_stream<SWIGLU>, kGemvMaxDynSmem, attr)) return kRcCudaError;
+  const long long work = static_cast<long long>(a.max_tiles) * (a.N / gemv_row_block<SWIGLU>());
+  const int grid = static_cast<int>(std::min<long long>(work, device_sm_count()));
+  gemv_stream<SWIGLU><<<grid, kGemvThreads, sh, stream>>>(a);
+  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+int launch_w13_gemv(const void* src, int src_rows, const int* index, int index_div, int M,
+                    const int4* tiles, const int* num_tiles, int max_tiles, const void* w_gate,
+                    const void* w_up, int E, int H, int I, void* h_out, int* status,
+                    cudaStream_t stream) {
+  if (!gemv_ok(I, H, true) || !aligned16(src) || !aligned16(w_gate) || !aligned16(w_up))
+    return kRcUnsupported;
+  if (M == 0 || max_tiles == 0) return kRcOk;
+  StreamArgs a{};
+  a.act = static_cast<const uint4*>(src);
+  a.act_rows = src_rows;
+  a.index = index;
+  a.index_div = index_div;
+  a.M = M;
+  a.tiles = tiles;
+  a.num_tiles = num_tiles;
+  a.max_tiles = max_tiles;
+  a.w0 = static_cast<const __nv_bfloat16*>(w_gate);
+  a.w1 = static_cast<const __nv_bfloat16*>(w_up);
+  a.E = E;
+  a.K = H;
+  a.N = I;
+  a.out = static_cast<__nv_bfloat16*>(h_out);
+  a.out_rows = M;
+  a.status = status;
+  return launch_stream<true>(a, stream);
+}
+
+int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
+                   const void* w_down, int E, int H, int I, const int* row_map,
+                   const float* row_scale, void* out, int out_rows, int* status,
+                   cudaStream_t stream) {
+  if (!gemv_ok(H, I, false) || !aligned16(h) || !aligned16(w_down)) return kRcUnsupported;
+  if (M == 0 || max_tiles == 0) return kRcOk;
+  StreamArgs a{};
+  a.act = static_cast<const uint4*>(h);
+  a.act_rows = M;
+  a.index_div = 1;
+  a.M = M;
+  a.tiles = tiles;
+  a.num_tiles = num_tiles;
+  a.max_tiles = max_tiles;
+  a.w0 = static_cast<const __nv_bfloat16*>(w_down);
+  a.E = E;
+  a.K = I;
+  a.N = H;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.row_map = row_map;
+  a.row_scale = row_scale;
+  a.out_rows = out_rows;
+  a.status = status;
+  return launch_stream<false>(a, stream);
+}
+
+}  // namespace moe

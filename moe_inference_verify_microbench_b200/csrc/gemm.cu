@@ -130,6 +130,8 @@ GemmArgs blank_args(int* status) {
 
 }  // namespace
 
+int device_sm_count() { return device_sms(); }
+
 int launch_router(const void* x, const void* wr, const float* bias, int T, int H, int E, int k,
                   int norm_topk_prob, int* ids_out, float* w_out, void* logits_out, int* status,
                   cudaStream_t stream) {
@@ -138,6 +140,10 @@ int launch_router(const void* x, const void* wr, const float* bias, int T, int H
   if ((H % kBK) != 0 || (E % 16) != 0 || E < 16 || E > 256 || k < 1 || k > kRouterMaxK || k > E)
     return kRcUnsupported;
   if (T == 0) return kRcOk;
+  if (use_router_small(T, H, E, k))
+    return launch_router_sort_small(x, wr, bias, T, H, E, k, norm_topk_prob, ids_out, w_out,
+                                    logits_out, nullptr, nullptr, nullptr, nullptr, 0, nullptr,
+                                    status, stream);
   CUtensorMap ma, mb;
   int rc = map_2d(&ma, x, T, H, kBM);
   if (rc == kRcOk) rc = map_3d(&mb, wr, 1, E, H, E);
@@ -164,8 +170,11 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
   if (a == nullptr || tiles == nullptr || num_tiles == nullptr || w_gate == nullptr ||
       w_up == nullptr || h_out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0)
     return kRcBadArgument;
-  if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   if (M == 0 || max_tiles == 0) return kRcOk;
+  if (use_gemv_w13(M) && gemv_ok(I, H, true))
+    return launch_w13_gemv(a, M, nullptr, 1, M, tiles, num_tiles, max_tiles, w_gate, w_up, E, H,
+                           I, h_out, status, stream);
+  if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   const int bn = pick_bn(I, M, max_tiles, 7, [](int b) { return b / 2; });
   CUtensorMap ma, mg, mu;
   int rc = map_2d(&ma, a, M, H, kBM);
@@ -199,9 +208,12 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
       max_tiles < 0 || src_rows < 0 || index_div <= 0)
     return kRcBadArgument;
   if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0) return kRcBadArgument;
-  if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   if (M == 0 || max_tiles == 0) return kRcOk;
   if (src_rows == 0) return kRcBadArgument;  // rows to gather, but nothing to gather from
+  if (use_gemv_w13(M) && gemv_ok(I, H, true))
+    return launch_w13_gemv(src, src_rows, index, index_div, M, tiles, num_tiles, max_tiles,
+                           w_gate, w_up, E, H, I, h_out, status, stream);
+  if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   const int bn = pick_bn(I, M, max_tiles, 7, [](int b) { return b / 2; });
   CUtensorMap mg, mu;
   int rc = map_3d(&mg, w_gate, E, I, H, bn / 2);
@@ -236,8 +248,11 @@ int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int
   if (h == nullptr || tiles == nullptr || num_tiles == nullptr || w_down == nullptr ||
       out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0 || out_rows < 0)
     return kRcBadArgument;
-  if ((I % kBK) != 0 || (H % 64) != 0) return kRcUnsupported;
   if (M == 0 || max_tiles == 0) return kRcOk;
+  if (use_gemv_w2(M) && gemv_ok(H, I, false))
+    return launch_w2_gemv(h, M, tiles, num_tiles, max_tiles, w_down, E, H, I, row_map, row_scale,
+                          out, out_rows, status, stream);
+  if ((I % kBK) != 0 || (H % 64) != 0) return kRcUnsupported;
   const int bn = pick_bn(H, M, max_tiles, 7, [](int b) { return b; });
   CUtensorMap ma, md;
   int rc = map_2d(&ma, h, M, I, kBM);

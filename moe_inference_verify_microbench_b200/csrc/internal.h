@@ -48,6 +48,35 @@ int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
               void* out, int out_rows, int* status, cudaStream_t stream);
 
+int device_sm_count();
+
+// Small-batch kernels (decode.cu).  Below these sizes the layer streams the
+// routed experts' weights through the CUDA cores instead of 128-row
+// tensor-core tiles: the router for up to 16 tokens (router_small_ok), the
+// gate/up GEMM for M <= kGemvW13MaxRows routing records and the down GEMM for
+// M <= kGemvW2MaxRows (measured crossovers on B200, H=2048, I=768, E=128).
+constexpr int kGemvW13MaxRows = 128;
+constexpr int kGemvW2MaxRows = 32;
+
+bool router_small_ok(int T, int H, int E, int k);
+bool gemv_ok(int n_out, int K, bool swiglu);
+inline bool use_router_small(int T, int H, int E, int k) { return router_small_ok(T, H, E, k); }
+inline bool use_gemv_w13(long long M) { return M > 0 && M <= kGemvW13MaxRows; }
+inline bool use_gemv_w2(long long M) { return M > 0 && M <= kGemvW2MaxRows; }
+
+int launch_router_sort_small(const void* x, const void* wr, const float* bias, int T, int H, int E,
+                             int k, int norm_topk_prob, int* ids_out, float* w_out,
+                             void* logits_out, int* counts, int* offsets, int* perm, int4* tiles,
+                             int max_tiles, int* num_tiles, int* status, cudaStream_t stream);
+int launch_w13_gemv(const void* src, int src_rows, const int* index, int index_div, int M,
+                    const int4* tiles, const int* num_tiles, int max_tiles, const void* w_gate,
+                    const void* w_up, int E, int H, int I, void* h_out, int* status,
+                    cudaStream_t stream);
+int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
+                   const void* w_down, int E, int H, int I, const int* row_map,
+                   const float* row_scale, void* out, int out_rows, int* status,
+                   cudaStream_t stream);
+
 inline int max_tiles_bound(long long R, int E, int block_m) {
   return static_cast<int>((R + block_m - 1) / block_m + E);
 }

@@ -259,3 +259,73 @@ def test_layer_uses_fused_gather_consistently(cuda):
     y2 = ops.combine(sl, T, k)
     ops.check_status(cuda)
     assert torch.equal(y, y2)
+
+
+# ----------------------------------------------------------------------------- decode (GEMV) path
+
+
+@pytest.mark.parametrize("counts,H,I", [
+    ([1, 0, 3, 8, 0, 2, 1, 1], 2048, 768),        # decode shapes, a few records per expert
+    ([20, 1, 0, 9, 2], 256, 128),                 # > 8 records per expert: several passes
+    ([128], 512, 64),                             # largest gate/up batch on the streaming path
+])
+def test_gemv_w13_w2_small_batches(cuda, counts, H, I):
+    """Small batches run the expert GEMMs as weight-streaming GEMVs (gate/up up
+    to 128 records, down up to 32); same contract (tile table, row map, slot
+    scale, fused gather) as the tensor-core kernels."""
+    offs, M, tb, fb, tiles, nt, mt = _grouped_setup(cuda, counts, H, I, 3 + sum(counts))
+    assert M <= 128
+    h = ops.grouped_w13_swiglu(tb["a"].to(cuda), tiles, nt, mt, tb["wg"].to(cuda), tb["wu"].to(cuda))
+    # Fused gather through an index with a divisor: A row p = src[index[p] // 2].
+    src = torch.zeros(2 * M, H, dtype=torch.bfloat16)
+    perm = torch.randperm(M, generator=torch.Generator().manual_seed(M)).to(torch.int32)
+    src[perm.long()] = tb["a"]
+    index = 2 * perm + torch.arange(M, dtype=torch.int32) % 2
+    h_g = ops.grouped_w13_swiglu_gather(src.to(cuda), index.to(cuda), 2, M, tiles, nt, mt,
+                                        tb["wg"].to(cuda), tb["wu"].to(cuda))
+    rng = np.random.default_rng(5)
+    rmap = rng.permutation(M).astype(np.int32)
+    scale = rng.random(M).astype(np.float32)
+    out = ops.grouped_w2(h, tiles, nt, mt, tb["wd"].to(cuda), row_map=torch.from_numpy(rmap).to(cuda),
+                         slot_scale=torch.from_numpy(scale).to(cuda))
+    ops.check_status(cuda)
+    assert torch.equal(h_g, h)
+    hf = to_f32(h)
+    ref_h = np.zeros((M, I), dtype=np.float32)
+    ref_o = np.zeros((M, H), dtype=np.float32)
+    for e in range(len(counts)):
+        s, t = offs[e], offs[e + 1]
+        if s == t:
+            continue
+        g = fb["a"][s:t] @ fb["wg"][e].T
+        u = fb["a"][s:t] @ fb["wu"][e].T
+        ref_h[s:t] = mo.silu_f32(g) * u
+        ref_o[rmap[s:t]] = (hf[s:t] @ fb["wd"][e].T) * scale[rmap[s:t]][:, None]
+    assert mo.rel_err(hf, ref_h) <= 1e-2
+    assert mo.rel_err(to_f32(out), ref_o) <= 1e-2
+
+
+@pytest.mark.parametrize("T,k,E", [(1, 4, 16), (3, 8, 64), (16, 8, 128), (17, 4, 32)])
+def test_layer_decode_equals_op_by_op(cuda, T, k, E):
+    """moe_layer_forward at decode sizes (fused router + sort, GEMV experts)
+    equals the op-by-op pipeline through the separate C-ABI entry points, bit
+    for bit."""
+    H, I = 256, 128
+    g = torch.Generator(device=cuda)
+    g.manual_seed(T * 100 + E)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=g, device=cuda).to(bf)
+    wr = (torch.randn(E, H, generator=g, device=cuda) * 0.05).to(bf)
+    wg = (torch.randn(E, I, H, generator=g, device=cuda) * 0.05).to(bf)
+    wu = (torch.randn(E, I, H, generator=g, device=cuda) * 0.05).to(bf)
+    wd = (torch.randn(E, H, I, generator=g, device=cuda) * 0.05).to(bf)
+    y = ops.moe_layer(x, wr, wg, wu, wd, k)
+    ids, w, _ = ops.router_topk(x, wr, k)
+    s = ops.sort_align(ids, E)
+    xs = ops.gather_rows(x, s.perm, k)
+    h = ops.grouped_w13_swiglu(xs, s.tiles, s.num_tiles, s.max_tiles, wg, wu)
+    sl = ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, wd, row_map=s.perm,
+                        slot_scale=w.reshape(-1))
+    y2 = ops.combine(sl, T, k)
+    ops.check_status(cuda)
+    assert torch.equal(y, y2)
