@@ -105,6 +105,8 @@ __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouter
   int* sort_sm = reinterpret_cast<int*>(dyn + static_cast<size_t>(T) * vec_per_row);
   cg::cluster_group cluster = cg::this_cluster();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
   {
     const int n = T * vec_per_row;
     int i = threadIdx.x;
@@ -428,6 +430,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_wait();
+  pdl_trigger();
 
   const int nt = max(0, min(*a.num_tiles, a.max_tiles));
   const int blocks = a.N / kRB;
@@ -570,11 +574,12 @@ int launch_router_sort_small(const void* x, const void* wr, const float* bias, i
   const size_t sh = router_dyn_smem(T, H, E);
   static std::atomic<uint64_t> attr{0};
   if (!allow_smem(router_sort_small, kRouterMaxDynSmem, attr)) return kRcCudaError;
-  router_sort_small<<<kRouterCluster, kRouterThreads, sh, stream>>>(
+  const cudaError_t e = launch_pdl(
+      router_sort_small, dim3(kRouterCluster), dim3(kRouterThreads), sh, stream,
       static_cast<const uint4*>(x), static_cast<const uint4*>(wr), bias, T, H / 8, E, k,
       norm_topk_prob, ids_out, w_out, static_cast<__nv_bfloat16*>(logits_out), counts, offsets,
       perm, tiles, max_tiles, num_tiles, status);
-  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+  return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 
 static int gemv_stages(int K, bool swiglu) {
@@ -598,8 +603,9 @@ static int launch_stream(StreamArgs a, cudaStream_t stream) {
   if (!allow_smem(gemv_stream<SWIGLU>, kGemvMaxDynSmem, attr)) return kRcCudaError;
   const long long work = static_cast<long long>(a.max_tiles) * (a.N / gemv_row_block<SWIGLU>());
   const int grid = static_cast<int>(std::min<long long>(work, device_sm_count()));
-  gemv_stream<SWIGLU><<<grid, kGemvThreads, sh, stream>>>(a);
-  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+  const cudaError_t e =
+      launch_pdl(gemv_stream<SWIGLU>, dim3(grid), dim3(kGemvThreads), sh, stream, a);
+  return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 
 int launch_w13_gemv(const void* src, int src_rows, const int* index, int index_div, int M,

@@ -96,9 +96,10 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
   const long long sms = device_sms();
   const int grid = static_cast<int>(work_units < sms ? work_units : sms);
   if (grid <= 0) return kRcOk;
-  grouped_gemm_kernel<BN, EPI, STAGES, GATHER_A>
-      <<<grid, gemm_threads<GATHER_A>(), L::kTotal, stream>>>(a, b0, b1, args);
-  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+  const cudaError_t e = launch_pdl(grouped_gemm_kernel<BN, EPI, STAGES, GATHER_A>, dim3(grid),
+                                   dim3(gemm_threads<GATHER_A>()), L::kTotal, stream, a, b0, b1,
+                                   args);
+  return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 
 // Widest N-tile (of those the shape allows) that still gives every SM a work

@@ -194,6 +194,8 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
 
   int num_tiles = args.num_tiles != nullptr ? *args.num_tiles : args.max_tiles;
   num_tiles = max(0, min(num_tiles, args.max_tiles));

@@ -4,6 +4,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <utility>
 
 #include "ptx.cuh"
 
@@ -18,6 +19,24 @@ enum ReturnCode : int {
   kRcTensorMap = -4,      // cuTensorMapEncodeTiled rejected a tensor map
   kRcWorkspace = -5,      // caller workspace smaller than required
 };
+
+// Launch with programmatic stream serialisation, so the kernel may be
+// scheduled while its predecessor in the stream is finishing (see pdl_wait).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 int sort_num_blocks(int R);
 size_t sort_workspace_bytes(int R, int E_local);

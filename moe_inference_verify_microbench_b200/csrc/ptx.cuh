@@ -37,6 +37,19 @@ __device__ __forceinline__ void record_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
 
+// Programmatic dependent launch.  pdl_wait() returns once the kernels this
+// one depends on in the stream have completed and their writes are visible
+// (at once for a kernel launched without the attribute); pdl_trigger() lets
+// the next kernel in the stream be scheduled and run its prologue.  Every
+// kernel of this library waits before its first access to global data other
+// than weights and triggers right after, so a kernel that starts early only
+// overlaps its set-up (barrier init, TMEM allocation, descriptor prefetch)
+// with the tail of its predecessor.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(kRowsThreads) gather_rows(const uint4* __restr
                                                             const int* __restrict__ count,
                                                             int idx_div, int vec_per_row,
                                                             uint4* __restrict__ dst, int* status) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows = count != nullptr ? min(R, *count) : R;
   for (int p = blockIdx.x * kRowsWarps + warp; p < rows; p += gridDim.x * kRowsWarps) {
@@ -57,6 +59,8 @@ __global__ void __launch_bounds__(kRowsThreads) combine_rows(
     const uint4* __restrict__ rows, int n_rows, const int* __restrict__ slot_src,
     const float* __restrict__ slot_w, const int* __restrict__ ids, int e_begin, int e_end, int T,
     int k, int vec_per_row, uint4* __restrict__ y, int* status) {
+  pdl_wait();
+  pdl_trigger();
   const long long total = static_cast<long long>(T) * vec_per_row;
   for (long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; g < total;
        g += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -104,6 +108,8 @@ __global__ void __launch_bounds__(kRowsThreads) combine_rows_warp(
     const uint4* __restrict__ rows, int n_rows, const int* __restrict__ slot_src,
     const float* __restrict__ slot_w, const int* __restrict__ ids, int e_begin, int e_end, int T,
     int k, int vec_per_row, uint4* __restrict__ y, int* status) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int n = blockIdx.x * kRowsWarps + warp; n < T; n += gridDim.x * kRowsWarps) {
     int src = -1;
@@ -155,10 +161,10 @@ int launch_gather_rows(const void* src, int src_rows, const int* idx, int R, con
                        int idx_div, int H, void* dst, int* status, cudaStream_t stream) {
   if (R < 0 || H <= 0 || idx_div <= 0 || (H % 8) != 0) return kRcBadArgument;
   if (R == 0) return kRcOk;
-  gather_rows<<<rows_grid(R), kRowsThreads, 0, stream>>>(static_cast<const uint4*>(src), src_rows,
-                                                         idx, R, count, idx_div, H / 8,
-                                                         static_cast<uint4*>(dst), status);
-  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+  const cudaError_t e = launch_pdl(gather_rows, dim3(rows_grid(R)), dim3(kRowsThreads), 0, stream,
+                                   static_cast<const uint4*>(src), src_rows, idx, R, count,
+                                   idx_div, H / 8, static_cast<uint4*>(dst), status);
+  return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 
 int launch_combine(const void* rows, int n_rows, const int* slot_src, const float* slot_w,
@@ -167,18 +173,19 @@ int launch_combine(const void* rows, int n_rows, const int* slot_src, const floa
   if (T < 0 || k <= 0 || k > kCombineMaxK || H <= 0 || (H % 8) != 0) return kRcBadArgument;
   if (T == 0) return kRcOk;
   if (T >= 1024) {
-    combine_rows_warp<<<rows_grid(T), kRowsThreads, 0, stream>>>(
-        static_cast<const uint4*>(rows), n_rows, slot_src, slot_w, ids, e_begin, e_end, T, k,
-        H / 8, static_cast<uint4*>(y), status);
-    return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+    const cudaError_t e = launch_pdl(combine_rows_warp, dim3(rows_grid(T)), dim3(kRowsThreads), 0,
+                                     stream, static_cast<const uint4*>(rows), n_rows, slot_src,
+                                     slot_w, ids, e_begin, e_end, T, k, H / 8,
+                                     static_cast<uint4*>(y), status);
+    return e == cudaSuccess ? kRcOk : kRcCudaError;
   }
   const long long threads = static_cast<long long>(T) * (H / 8);
   const long long blocks = (threads + kRowsThreads - 1) / kRowsThreads;
   const int grid = static_cast<int>(blocks < 148LL * 16 ? blocks : 148LL * 16);
-  combine_rows<<<grid, kRowsThreads, 0, stream>>>(
-      static_cast<const uint4*>(rows), n_rows, slot_src, slot_w, ids, e_begin, e_end, T, k, H / 8,
-      static_cast<uint4*>(y), status);
-  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+  const cudaError_t e = launch_pdl(combine_rows, dim3(grid), dim3(kRowsThreads), 0, stream,
+                                   static_cast<const uint4*>(rows), n_rows, slot_src, slot_w, ids,
+                                   e_begin, e_end, T, k, H / 8, static_cast<uint4*>(y), status);
+  return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 
 }  // namespace moe

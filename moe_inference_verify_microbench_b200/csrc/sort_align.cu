@@ -33,6 +33,8 @@ size_t sort_workspace_bytes(int R, int E_local) {
 __global__ void __launch_bounds__(kSortThreads) sa_hist(const int* __restrict__ ids, int R, int E,
                                                         int e_begin, int E_local,
                                                         int* __restrict__ hist, int* status) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sh[];
   for (int e = threadIdx.x; e < E_local; e += blockDim.x) sh[e] = 0;
   __syncthreads();
@@ -53,6 +55,8 @@ __global__ void __launch_bounds__(1024) sa_scan(int* __restrict__ hist, int nblk
                                                 long long* __restrict__ offsets64,
                                                 int4* __restrict__ tiles, int max_tiles,
                                                 int* __restrict__ num_tiles) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int warp_sums[32];
   __shared__ int total;
   const int e = threadIdx.x;
@@ -85,6 +89,8 @@ __global__ void __launch_bounds__(kSortThreads) sa_scatter(const int* __restrict
                                                            const int* __restrict__ hist,
                                                            int* __restrict__ perm,
                                                            int* __restrict__ inv, int* status) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sm[];
   int* base = sm;                       // [E_local] next free position per expert
   int* wcnt = sm + E_local;             // [8][E_local] per-warp counts of this round
@@ -133,6 +139,8 @@ __global__ void __launch_bounds__(kSortThreads) sa_small(
     int* __restrict__ counts, int* __restrict__ offsets, long long* __restrict__ offsets64,
     int* __restrict__ perm, int* __restrict__ inv, int4* __restrict__ tiles, int max_tiles,
     int* __restrict__ num_tiles, int* status) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ int sm[];
   sort_small_block(ids, R, E, e_begin, E_local, block_m, counts, offsets, offsets64, perm, inv,
                    tiles, max_tiles, num_tiles, status, sm);
@@ -143,6 +151,8 @@ __global__ void __launch_bounds__(1024) tiles_from_offsets(const long long* __re
                                                            int4* __restrict__ tiles, int max_tiles,
                                                            int* __restrict__ num_tiles,
                                                            int* status) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int warp_sums[32];
   __shared__ int total;
   const int e = threadIdx.x;
@@ -169,35 +179,40 @@ int launch_sort_align(const int* ids, int R, int E, int e_begin, int E_local, in
   const int nblk = sort_num_blocks(R);
   if (nblk <= 1 && E_local <= kSortThreads) {
     const size_t sh = static_cast<size_t>(E_local) * (1 + kSortThreads / 32) * sizeof(int);
-    sa_small<<<1, kSortThreads, sh, stream>>>(ids, R, E, e_begin, E_local, block_m, counts,
-                                              offsets, offsets64, perm, inv, tiles, max_tiles,
-                                              num_tiles, status);
-    return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+    const cudaError_t e = launch_pdl(sa_small, dim3(1), dim3(kSortThreads), sh, stream, ids, R, E,
+                                     e_begin, E_local, block_m, counts, offsets, offsets64, perm,
+                                     inv, tiles, max_tiles, num_tiles, status);
+    return e == cudaSuccess ? kRcOk : kRcCudaError;
   }
   int* hist = static_cast<int*>(workspace);
   const size_t sh_hist = static_cast<size_t>(E_local) * sizeof(int);
   const size_t sh_scatter = static_cast<size_t>(E_local) * (1 + kSortThreads / 32) * sizeof(int);
   // E_local <= 1024 keeps sh_scatter <= 36 KB, inside the default 48 KB limit.
   if (nblk > 0) {
-    sa_hist<<<nblk, kSortThreads, sh_hist, stream>>>(ids, R, E, e_begin, E_local, hist, status);
+    if (launch_pdl(sa_hist, dim3(nblk), dim3(kSortThreads), sh_hist, stream, ids, R, E, e_begin,
+                   E_local, hist, status) != cudaSuccess)
+      return kRcCudaError;
   }
   const int scan_threads = ((E_local + 31) / 32) * 32;
-  sa_scan<<<1, scan_threads, 0, stream>>>(hist, nblk, E_local, block_m, counts, offsets, offsets64,
-                                          tiles, max_tiles, num_tiles);
+  if (launch_pdl(sa_scan, dim3(1), dim3(scan_threads), 0, stream, hist, nblk, E_local, block_m,
+                 counts, offsets, offsets64, tiles, max_tiles, num_tiles) != cudaSuccess)
+    return kRcCudaError;
   if (nblk > 0) {
-    sa_scatter<<<nblk, kSortThreads, sh_scatter, stream>>>(ids, R, E, e_begin, E_local, hist, perm,
-                                                           inv, status);
+    if (launch_pdl(sa_scatter, dim3(nblk), dim3(kSortThreads), sh_scatter, stream, ids, R, E,
+                   e_begin, E_local, static_cast<const int*>(hist), perm, inv,
+                   status) != cudaSuccess)
+      return kRcCudaError;
   }
-  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+  return kRcOk;
 }
 
 int launch_tiles_from_offsets(const long long* offsets, int E, int block_m, int4* tiles,
                               int max_tiles, int* num_tiles, int* status, cudaStream_t stream) {
   if (E <= 0 || E > 1024 || block_m <= 0) return kRcBadArgument;
   const int threads = ((E + 31) / 32) * 32;
-  tiles_from_offsets<<<1, threads, 0, stream>>>(offsets, E, block_m, tiles, max_tiles, num_tiles,
-                                                status);
-  return cudaGetLastError() == cudaSuccess ? kRcOk : kRcCudaError;
+  const cudaError_t e = launch_pdl(tiles_from_offsets, dim3(1), dim3(threads), 0, stream, offsets,
+                                   E, block_m, tiles, max_tiles, num_tiles, status);
+  return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 
 }  // namespace moe
