@@ -184,6 +184,10 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                    void* slots) {
                  const int R = static_cast<int>(p.R);
                  const bool small = use_gemv_w13(R);  // decode: weight-streaming kernels
+                 // Large batches: 256-row tiles for the CTA-pair GEMMs.
+                 const int tile_rows = !small && use_pair_gemm(R, E, H, I) ? kPairTileRows
+                                                                           : MOE_BLOCK_M;
+                 const int max_tiles = max_tiles_bound(R, E, tile_rows);
                  if (small && use_router_small(T, H, E, top_k)) {
                    rc = launch_router_sort_small(x, router_weight, router_bias, T, H, E, top_k,
                                                  norm_topk_prob, ids, w, nullptr, counts, offsets,
@@ -193,9 +197,9 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                    rc = launch_router(x, router_weight, router_bias, T, H, E, top_k,
                                       norm_topk_prob, ids, w, nullptr, status, stream);
                    if (rc == kRcOk)
-                     rc = launch_sort_align(ids, R, E, 0, E, MOE_BLOCK_M, sort_ws, counts,
-                                            offsets, nullptr, perm, nullptr, tiles, p.max_tiles,
-                                            num_tiles, status, stream);
+                     rc = launch_sort_align(ids, R, E, 0, E, tile_rows, sort_ws, counts, offsets,
+                                            nullptr, perm, nullptr, tiles, max_tiles, num_tiles,
+                                            status, stream);
                  }
                  if (rc == kRcOk && small) {
                    rc = launch_w13_swiglu_gather(x, T, perm, top_k, R, tiles, num_tiles,
@@ -205,12 +209,12 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                    rc = launch_gather_rows(x, T, perm, R, nullptr, top_k, H, sorted_x, status,
                                            stream);
                    if (rc == kRcOk)
-                     rc = launch_w13_swiglu(sorted_x, R, tiles, num_tiles, p.max_tiles, w_gate,
-                                            w_up, E, H, I, h, status, stream);
+                     rc = launch_w13_swiglu(sorted_x, R, tiles, num_tiles, max_tiles, w_gate,
+                                            w_up, E, H, I, h, status, stream, tile_rows);
                  }
                  if (rc == kRcOk)
-                   rc = launch_w2(h, R, tiles, num_tiles, p.max_tiles, w_down, E, H, I, perm, w,
-                                  slots, R, status, stream);
+                   rc = launch_w2(h, R, tiles, num_tiles, max_tiles, w_down, E, H, I, perm, w,
+                                  slots, R, status, stream, tile_rows);
                  if (rc == kRcOk)
                    rc = launch_combine(slots, R, nullptr, nullptr, nullptr, 0, E, T, top_k, H, y,
                                        status, stream);

@@ -4,6 +4,7 @@
 #include <mutex>
 
 #include "grouped_gemm.cuh"
+#include "grouped_gemm_pair.cuh"
 #include "internal.h"
 
 namespace moe {
@@ -65,6 +66,7 @@ int map_3d(CUtensorMap* m, const void* base, int E, int rows, int cols, int box_
 }
 
 constexpr int kMaxDevices = 64;
+constexpr int kMaxSmemPerBlock = 232448;  // sm_100 opt-in dynamic shared memory per block
 
 int device_sms() {
   static std::atomic<int> cache[kMaxDevices];
@@ -82,7 +84,8 @@ int device_sms() {
 template <int BN, int EPI, int STAGES, bool GATHER_A = false>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                 const GemmArgs& args, long long work_units, cudaStream_t stream) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, gemm_out_bytes<EPI, GATHER_A>()>;
+  static_assert(L::kTotal <= kMaxSmemPerBlock, "shared memory budget");
   static std::atomic<uint64_t> attr_done{0};  // one bit per device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return kRcCudaError;
@@ -101,6 +104,31 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
                                    args);
   return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
+
+template <int EPI, int STAGES>
+int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
+                     const GemmArgs& args, long long work_units, cudaStream_t stream) {
+  using L = PairSmem<STAGES>;
+  static_assert(L::kTotal <= kMaxSmemPerBlock, "shared memory budget");
+  static std::atomic<uint64_t> attr_done{0};  // one bit per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return kRcCudaError;
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((attr_done.load(std::memory_order_acquire) & bit) == 0) {
+    if (cudaFuncSetAttribute(grouped_gemm_pair_kernel<EPI, STAGES>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) != cudaSuccess)
+      return kRcCudaError;
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const long long pairs = device_sms() / 2;
+  const int grid = 2 * static_cast<int>(work_units < pairs ? work_units : pairs);
+  if (grid <= 0) return kRcOk;
+  const cudaError_t e = launch_pdl_cluster(grouped_gemm_pair_kernel<EPI, STAGES>, dim3(grid),
+                                           dim3(384), L::kTotal, stream, 2u, a, b0, b1, args);
+  return e == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+constexpr int kPairStages = 6;
 
 // Widest N-tile (of those the shape allows) that still gives every SM a work
 // unit; narrow tiles only pay off for small batches (decode), where the
@@ -167,7 +195,7 @@ int launch_router(const void* x, const void* wr, const float* bias, int T, int H
 
 int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_tiles, int max_tiles,
                       const void* w_gate, const void* w_up, int E, int H, int I, void* h_out,
-                      int* status, cudaStream_t stream) {
+                      int* status, cudaStream_t stream, int tile_rows) {
   if (a == nullptr || tiles == nullptr || num_tiles == nullptr || w_gate == nullptr ||
       w_up == nullptr || h_out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0)
     return kRcBadArgument;
@@ -176,6 +204,29 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
     return launch_w13_gemv(a, M, nullptr, 1, M, tiles, num_tiles, max_tiles, w_gate, w_up, E, H,
                            I, h_out, status, stream);
   if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
+  if (tile_rows == kPairTileRows) {
+    if ((I % (kPairBN / 2)) != 0) return kRcUnsupported;
+    CUtensorMap ma, mg, mu;
+    int rc = map_2d(&ma, a, M, H, kBM);
+    if (rc == kRcOk) rc = map_3d(&mg, w_gate, E, I, H, kPairBN / 2);
+    if (rc == kRcOk) rc = map_3d(&mu, w_up, E, I, H, kPairBN / 2);
+    if (rc != kRcOk) return rc;
+    GemmArgs g = blank_args(status);
+    g.tiles = tiles;
+    g.num_tiles = num_tiles;
+    g.max_tiles = max_tiles;
+    g.n_tiles = I / (kPairBN / 2);
+    g.num_kb = H / kBK;
+    g.b_rows = kPairBN;
+    g.a_rows = M;
+    g.num_experts = E;
+    g.out = static_cast<__nv_bfloat16*>(h_out);
+    g.out_ld = I;
+    g.out_rows = M;
+    return launch_gemm_pair<kEpiSwiGLU, kPairStages>(
+        ma, mg, mu, g, static_cast<long long>(max_tiles) * g.n_tiles, stream);
+  }
+  if (tile_rows != kBM) return kRcBadArgument;
   const int bn = pick_bn(I, M, max_tiles, 7, [](int b) { return b / 2; });
   CUtensorMap ma, mg, mu;
   int rc = map_2d(&ma, a, M, H, kBM);
@@ -245,7 +296,7 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
 
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
-              void* out, int out_rows, int* status, cudaStream_t stream) {
+              void* out, int out_rows, int* status, cudaStream_t stream, int tile_rows) {
   if (h == nullptr || tiles == nullptr || num_tiles == nullptr || w_down == nullptr ||
       out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0 || out_rows < 0)
     return kRcBadArgument;
@@ -254,6 +305,30 @@ int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int
     return launch_w2_gemv(h, M, tiles, num_tiles, max_tiles, w_down, E, H, I, row_map, row_scale,
                           out, out_rows, status, stream);
   if ((I % kBK) != 0 || (H % 64) != 0) return kRcUnsupported;
+  if (tile_rows == kPairTileRows) {
+    if ((H % kPairBN) != 0) return kRcUnsupported;
+    CUtensorMap ma, md;
+    int rc = map_2d(&ma, h, M, I, kBM);
+    if (rc == kRcOk) rc = map_3d(&md, w_down, E, H, I, kPairBN / 2);
+    if (rc != kRcOk) return rc;
+    GemmArgs g = blank_args(status);
+    g.tiles = tiles;
+    g.num_tiles = num_tiles;
+    g.max_tiles = max_tiles;
+    g.n_tiles = H / kPairBN;
+    g.num_kb = I / kBK;
+    g.b_rows = kPairBN;
+    g.a_rows = M;
+    g.num_experts = E;
+    g.out = static_cast<__nv_bfloat16*>(out);
+    g.out_ld = H;
+    g.out_rows = out_rows;
+    g.row_map = row_map;
+    g.row_scale = row_scale;
+    return launch_gemm_pair<kEpiStore, kPairStages>(
+        ma, md, md, g, static_cast<long long>(max_tiles) * g.n_tiles, stream);
+  }
+  if (tile_rows != kBM) return kRcBadArgument;
   const int bn = pick_bn(H, M, max_tiles, 7, [](int b) { return b; });
   CUtensorMap ma, md;
   int rc = map_2d(&ma, h, M, I, kBM);

@@ -74,13 +74,18 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kRouterMaxK = 8;
 
-template <int BN, int STAGES>
+// Output staging: each epilogue warp owns 32 rows x 128 bytes of shared memory
+// through which it turns its row-per-lane results into whole-line stores.
+constexpr int kEpiStageBytes = 32 * 128;
+
+template <int BN, int STAGES, int OUT_BYTES = 0>
 struct GemmSmem {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kOutBytes = OUT_BYTES;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kTotal = 1024 + STAGES * kStageBytes + kBarrierBytes;
+  static constexpr int kTotal = 1024 + STAGES * kStageBytes + kOutBytes + kBarrierBytes;
 };
 
 __device__ __forceinline__ int4 load_tile(const GemmArgs& a, int mt) {
@@ -89,7 +94,9 @@ __device__ __forceinline__ int4 load_tile(const GemmArgs& a, int mt) {
   return make_int4(0, r0, min(a.a_rows, r0 + kBM), 0);
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+// silu(g) = g * sigmoid(g) with the fast exponential and division
+// intrinsics; the result is rounded to bf16, far above their error.
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // Router top-k keys.  A bf16 logit and its expert id pack into one 32-bit key
 // whose unsigned order is "larger value first, lower expert id first among
@@ -124,6 +131,95 @@ __device__ __forceinline__ void topk_insert(uint32_t (&top)[kRouterMaxK], uint32
   }
 }
 
+// 16-byte slot of row r's chunk j in a warp's staging rows of `row_bytes`:
+// XOR-swizzled so that both the row-per-lane writes and the line-per-8-lanes
+// reads are free of bank conflicts.
+template <int ROW_BYTES>
+__device__ __forceinline__ uint32_t stage_slot(int r, int j) {
+  if constexpr (ROW_BYTES == 128) return static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4));
+  else return static_cast<uint32_t>(r * 64 + ((j ^ ((r >> 1) & 3)) << 4));
+}
+
+// Epilogue of one accumulator tile for this thread's row: TMEM columns ->
+// bf16 -> this warp's staging rows -> global.  SwiGLU: out[row, nt*BN/2 + c] =
+// silu(acc[c]) * acc[BN/2 + c]; store: out[orow, nt*BN + c] = scale * acc[c].
+// `half` selects this warp's share of the columns when kHalves warps serve one
+// TMEM lane quarter.  Output is written in chunks of CW columns: every lane
+// stages its row, then each store instruction writes CW*2-byte row segments of
+// 256/CW rows (whole 128-byte lines for CW = 64), with the row's destination
+// and store flag taken from the lane that owns it.
+template <int BN, int EPI, int kHalves>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tb, int row,
+                                              bool valid, bool st, int orow_idx, float scale,
+                                              int nt, int half, uint8_t* stage, int lane) {
+  constexpr int kOut = EPI == kEpiSwiGLU ? BN / 2 : BN;  // output columns of the tile
+  constexpr int kSplit = (kOut / kHalves >= 32) ? kHalves : 1;
+  constexpr int kCols = kOut / kSplit;                   // this warp's output columns
+  constexpr int CW = (kCols % 64 == 0) ? 64 : 32;
+  static_assert(kCols % 32 == 0, "epilogue works in 32-column chunks");
+  constexpr int kRowBytes = 2 * CW;
+  constexpr int kLanesPerRow = CW / 8;
+  constexpr int kRowsPerStore = 32 / kLanesPerRow;
+  if (half >= kSplit) return;
+  if constexpr (EPI == kEpiSwiGLU) {
+    orow_idx = row;
+    st = valid && row < args.out_rows;
+  }
+  const uint32_t my_stage = smem_u32(stage);
+  const int j = lane % kLanesPerRow;
+  const int rsub = lane / kLanesPerRow;
+  __nv_bfloat16* const out_base = args.out + static_cast<size_t>(nt) * kOut;
+#pragma unroll 1
+  for (int c0 = half * kCols; c0 < (half + 1) * kCols; c0 += CW) {
+    uint32_t pk[CW / 2];
+#pragma unroll
+    for (int sub = 0; sub < CW / 32; ++sub) {
+      if constexpr (EPI == kEpiSwiGLU) {
+        uint32_t g[32], u[32];
+        tmem_ld32(tb + c0 + 32 * sub, g);
+        tmem_ld32(tb + BN / 2 + c0 + 32 * sub, u);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+          const float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
+          pk[16 * sub + i] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
+        }
+      } else {
+        uint32_t r[32];
+        tmem_ld32(tb + c0 + 32 * sub, r);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          pk[16 * sub + i] = pack_bf16x2(__uint_as_float(r[2 * i]) * scale,
+                                         __uint_as_float(r[2 * i + 1]) * scale);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < CW / 8; ++q) {
+      const uint32_t a = my_stage + stage_slot<kRowBytes>(lane, q);
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(pk[4 * q]),
+                   "r"(pk[4 * q + 1]), "r"(pk[4 * q + 2]), "r"(pk[4 * q + 3])
+                   : "memory");
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 32 / kRowsPerStore; ++i) {
+      const int r = i * kRowsPerStore + rsub;
+      const int o = __shfl_sync(0xffffffffu, orow_idx, r);
+      const bool ok = __shfl_sync(0xffffffffu, st ? 1 : 0, r) != 0;
+      uint4 v;
+      asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                   : "r"(my_stage + stage_slot<kRowBytes>(r, j))
+                   : "memory");
+      if (ok)
+        *reinterpret_cast<uint4*>(out_base + static_cast<size_t>(o) * args.out_ld + c0 + j * 8) = v;
+    }
+    __syncwarp();
+  }
+}
+
 constexpr int kGatherWarp0 = 8;    // first of the four A-loader warps
 constexpr int kGatherWarps = 4;
 constexpr int kGatherLag = 2;      // a stage is published this many stages after its copies
@@ -136,6 +232,11 @@ constexpr int epi_warps() {
   return GATHER_A ? 4 : 8;
 }
 
+template <int EPI, bool GATHER_A>
+constexpr int gemm_out_bytes() {
+  return EPI == kEpiRouter ? 0 : epi_warps<GATHER_A>() * kEpiStageBytes;
+}
+
 template <bool GATHER_A>
 constexpr int gemm_threads() {
   return 384;
@@ -146,7 +247,7 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB0,
                         const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, gemm_out_bytes<EPI, GATHER_A>()>;
   constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
   static_assert(kTmemCols == 128 || kTmemCols == 256 || kTmemCols == 512,
                 "TMEM allocation must be a power of 2 of at least 32 columns");
@@ -156,7 +257,8 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * L::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * L::kBBytes);
+  uint8_t* sOut = sB + STAGES * L::kBBytes;  // epilogue staging, kEpiStageBytes per warp
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + L::kOutBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -174,7 +276,7 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 32 * epi_warps<GATHER_A>());
+      mbar_init(&acc_empty[a], epi_warps<GATHER_A>());  // one arrival per epilogue warp
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -214,7 +316,8 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
         const int mt = w / args.n_tiles;
         const int nt = w - mt * args.n_tiles;
         const int4 t = load_tile(args, mt);
-        if (t.x < 0 || t.x >= args.num_experts || t.y < 0 || t.z > args.a_rows || t.y >= t.z) {
+        if (t.x < 0 || t.x >= args.num_experts || t.y < 0 || t.z > args.a_rows || t.y >= t.z ||
+            t.z - t.y > kBM) {
           record_status(args.status, t.x < 0 || t.x >= args.num_experts ? kErrBadExpert : kErrBadRow);
           *abort_flag = 1;
           break;
@@ -376,46 +479,14 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
       const int mt = w / args.n_tiles;
       const int nt = w - mt * args.n_tiles;
       const int4 t = load_tile(args, mt);
-      bool ok = mbar_wait(&acc_full[acc], acc_ph, abort_flag, args.status, kErrTimeoutAccFull);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
       const int row = t.y + q * 32 + lane;
       const bool valid = row < t.z;
-      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
-
-      if constexpr (EPI == kEpiSwiGLU) {
-        __nv_bfloat16* orow = args.out + static_cast<size_t>(row) * args.out_ld + nt * (BN / 2);
-        const bool st = valid && row < args.out_rows;
-        // Output columns are shared between the warps of one lane quarter when
-        // each share is at least one 32-column chunk; otherwise one warp does all.
-        constexpr int kSplit = (BN / 2 / kHalves >= 32) ? kHalves : 1;
-        constexpr int kCols = BN / 2 / kSplit;
-        static_assert(kCols % 32 == 0, "SwiGLU epilogue works in 32-column chunks");
-#pragma unroll 1
-        for (int c0 = half * kCols; half < kSplit && c0 < (half + 1) * kCols; c0 += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(tb + c0, g);
-          tmem_ld32(tb + BN / 2 + c0, u);
-          tc_wait_ld();
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float g0 = __uint_as_float(g[2 * j]), g1 = __uint_as_float(g[2 * j + 1]);
-            const float u0 = __uint_as_float(u[2 * j]), u1 = __uint_as_float(u[2 * j + 1]);
-            pk[j] = pack_bf16x2(silu_f(g0) * u0, silu_f(g1) * u1);
-          }
-          if (st) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-          }
-        }
-      } else if constexpr (EPI == kEpiStore) {
-        int orow_idx = row;
-        float scale = 1.0f;
-        bool st = valid;
+      // Store epilogue: the output row and its scale do not depend on the
+      // accumulator, so their loads overlap the wait for it.
+      int orow_idx = row;
+      float scale = 1.0f;
+      bool st = valid;
+      if constexpr (EPI == kEpiStore) {
         if (st) {
           if (args.row_map != nullptr) orow_idx = args.row_map[row];
           if (orow_idx < 0 || orow_idx >= args.out_rows) {
@@ -425,51 +496,16 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
             scale = args.row_scale[orow_idx];
           }
         }
-        __nv_bfloat16* orow = args.out + static_cast<size_t>(st ? orow_idx : 0) * args.out_ld + nt * BN;
-        constexpr int kSplit = (BN / kHalves >= 32) ? kHalves : 1;
-        constexpr int kCols = BN / kSplit;  // accumulator columns of this warp's share
-        static_assert(kCols % 32 == 0, "store epilogue works in 32-column chunks");
-        if constexpr (kCols % 64 == 0) {
-#pragma unroll 1
-          for (int c0 = half * kCols; half < kSplit && c0 < (half + 1) * kCols; c0 += 64) {
-            uint32_t r0[32], r1[32];
-            tmem_ld32(tb + c0, r0);
-            tmem_ld32(tb + c0 + 32, r1);
-            tc_wait_ld();
-            uint32_t pk[32];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              pk[j] = pack_bf16x2(__uint_as_float(r0[2 * j]) * scale,
-                                  __uint_as_float(r0[2 * j + 1]) * scale);
-              pk[16 + j] = pack_bf16x2(__uint_as_float(r1[2 * j]) * scale,
-                                       __uint_as_float(r1[2 * j + 1]) * scale);
-            }
-            if (st) {
-              uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-            }
-          }
-        } else {
-#pragma unroll 1
-          for (int c0 = half * kCols; half < kSplit && c0 < (half + 1) * kCols; c0 += 32) {
-            uint32_t r0[32];
-            tmem_ld32(tb + c0, r0);
-            tc_wait_ld();
-            uint32_t pk[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-              pk[j] = pack_bf16x2(__uint_as_float(r0[2 * j]) * scale,
-                                  __uint_as_float(r0[2 * j + 1]) * scale);
-            if (st) {
-              uint4* dst = reinterpret_cast<uint4*>(orow + c0);
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-            }
-          }
-        }
+      }
+      bool ok = mbar_wait(&acc_full[acc], acc_ph, abort_flag, args.status, kErrTimeoutAccFull);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
+
+      if constexpr (EPI == kEpiSwiGLU || EPI == kEpiStore) {
+        epilogue_tile<BN, EPI, kHalves>(args, tb, row, valid, st, orow_idx, scale, nt, half,
+                                        sOut + (warp - 4) * kEpiStageBytes, lane);
       } else {
         if (half == 0) {  // one warp per lane quarter: rows are not split by columns
           // Router: the row's E logits -> bf16 -> top-k (value desc, id asc) -> softmax.
@@ -537,7 +573,8 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
   }
 

@@ -1,0 +1,260 @@
+// CTA-pair variant of the grouped GEMM for large batches: one
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16) per K-step, issued by the
+// even CTA of a (2,1,1) cluster.
+//
+// Work unit: one (pair tile, N-tile).  A pair tile is up to 256 consecutive
+// rows of one expert (tile table built with 256-row blocks); CTA r of the pair
+// owns rows row_begin + 128 r .. +127 of it and loads those A rows plus half of
+// the B tile (gate rows for r = 0 and up rows for r = 1 in the SwiGLU GEMM;
+// B rows n*256 + 128 r .. +127 for the store GEMM).  Each CTA's tensor memory
+// receives the 128 x 256 accumulator of its own rows, so the epilogue is the
+// one of the single-CTA kernel.  Per CTA and K-block the operands are 32 KB
+// for 4.2 MFLOP, against 48 KB for the single-CTA 128 x 256 tile: the pair
+// halves the B traffic from L2 and leaves room for six stages.
+//
+// Roles per CTA (384 threads): warp 0 TMA producer (both CTAs; the copies of
+// both count on the even CTA's stage barrier), warp 1 MMA issuer (even CTA
+// only; its commits arrive on the stage and accumulator barriers of both
+// CTAs), warp 2 tensor-memory allocator (.cta_group::2, both CTAs), warps
+// 4..11 epilogue (both CTAs; they release an accumulator by arriving on the
+// even CTA's barrier).  Every wait is bounded; a CTA leaves only after the
+// final cluster barrier, so no copy, MMA or remote arrival can target a CTA
+// that has exited.
+#pragma once
+
+#include "grouped_gemm.cuh"
+
+namespace moe {
+
+constexpr int kPairBM = 2 * kBM;  // rows of a pair tile (M of the pair MMA)
+constexpr int kPairBN = 256;
+
+template <int STAGES>
+struct PairSmem {
+  static constexpr int kABytes = kBM * kBK * 2;                // this CTA's 128 A rows
+  static constexpr int kBBytes = (kPairBN / 2) * kBK * 2;      // this CTA's half of the B rows
+  static constexpr int kStageBytes = kABytes + kBBytes;        // 32 KB
+  static constexpr int kOutBytes = 8 * kEpiStageBytes;         // epilogue staging
+  static constexpr int kTotal = 1024 + STAGES * kStageBytes + kOutBytes + 256;
+};
+
+template <int EPI, int STAGES>
+__global__ void __launch_bounds__(384, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                             const __grid_constant__ CUtensorMap tmB0,
+                             const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
+  static_assert(EPI == kEpiSwiGLU || EPI == kEpiStore, "pair kernel: SwiGLU or store epilogue");
+  using L = PairSmem<STAGES>;
+  constexpr int BN = kPairBN;
+  constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
+  constexpr int kEpiWarps = 8;
+  constexpr int kHalves = kEpiWarps / 4;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * L::kABytes;
+  uint8_t* sOut = sB + STAGES * L::kBBytes;  // epilogue staging, kEpiStageBytes per warp
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + L::kOutBytes);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();  // 0: issues the pair's MMAs
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);   // the even CTA's producer (+ the bytes of both CTAs)
+      mbar_init(&empty[s], 1);  // one MMA commit
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * kEpiWarps);  // the epilogue warps of both CTAs
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB0);
+    if (EPI == kEpiSwiGLU) tma_prefetch_desc(&tmB1);
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
+
+  int num_tiles = args.num_tiles != nullptr ? *args.num_tiles : args.max_tiles;
+  num_tiles = max(0, min(num_tiles, args.max_tiles));
+  const int total = num_tiles * args.n_tiles;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int npairs = static_cast<int>(gridDim.x >> 1);
+  const uint32_t stage_tx = static_cast<uint32_t>(L::kStageBytes);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int w = pair; ok && w < total; w += npairs) {
+        const int mt = w / args.n_tiles;
+        const int nt = w - mt * args.n_tiles;
+        const int4 t = load_tile(args, mt);
+        if (t.x < 0 || t.x >= args.num_experts || t.y < 0 || t.z > args.a_rows || t.y >= t.z ||
+            t.z - t.y > kPairBM) {
+          record_status(args.status, t.x < 0 || t.x >= args.num_experts ? kErrBadExpert : kErrBadRow);
+          *abort_flag = 1;
+          break;
+        }
+        const int arow = t.y + kBM * static_cast<int>(rank);
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, args.status, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * stage_tx);
+          const uint32_t fb = cluster_addr(&full[s], 0);
+          tma_load_2d_pair(sA + s * L::kABytes, &tmA, fb, kb * kBK, arow);
+          uint8_t* b = sB + s * L::kBBytes;
+          if (EPI == kEpiSwiGLU) {
+            tma_load_3d_pair(b, leader ? &tmB0 : &tmB1, fb, kb * kBK, nt * (BN / 2), t.x);
+          } else {
+            tma_load_3d_pair(b, &tmB0, fb, kb * kBK, nt * BN + (BN / 2) * static_cast<int>(rank),
+                             t.x);
+          }
+          ++issued;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag && leader) {
+        // Let every copy counted on this CTA's stage barriers land.
+        const uint32_t first = issued > STAGES ? issued - STAGES : 0u;
+        for (uint32_t i = first; i < issued; ++i) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1u)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------------------ MMA issuer
+      const uint32_t idesc = idesc_bf16_f32(kPairBM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int it = 0;
+      bool ok = true;
+      for (int w = pair; ok && w < total; w += npairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_ph = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag, args.status,
+                               kErrTimeoutAccEmpty))
+          break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, args.status, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * L::kABytes);
+          const uint32_t b0 = smem_u32(sB + s * L::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            tc_mma_bf16_pair(d, sw128_kmajor_desc(a0 + kk * 32), sw128_kmajor_desc(b0 + kk * 32),
+                             idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit_pair(cluster_addr(&empty[s], 0));
+          tc_commit_pair(cluster_addr(&empty[s], 1));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) {
+          tc_commit_pair(cluster_addr(&acc_full[acc], 0));
+          tc_commit_pair(cluster_addr(&acc_full[acc], 1));
+        }
+      }
+      // Every MMA issued by this thread has finished once `drain` completes.
+      tc_commit_pair(cluster_addr(drain, 0));
+      const unsigned long long t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+      }
+    }
+  } else if (warp >= 4 && warp < 4 + kEpiWarps) {
+    // -------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t release0 = cluster_addr(&acc_empty[0], 0);
+    const uint32_t release1 = cluster_addr(&acc_empty[1], 0);
+    int it = 0;
+    for (int w = pair; w < total; w += npairs, ++it) {
+      const int acc = it & 1;
+      const uint32_t acc_ph = (it >> 1) & 1;
+      const int mt = w / args.n_tiles;
+      const int nt = w - mt * args.n_tiles;
+      const int4 t = load_tile(args, mt);
+      const int row = t.y + kBM * static_cast<int>(rank) + q * 32 + lane;
+      const bool valid = row < t.z;
+      int orow_idx = row;
+      float scale = 1.0f;
+      bool st = valid;
+      if constexpr (EPI == kEpiStore) {
+        if (st) {
+          if (args.row_map != nullptr) orow_idx = args.row_map[row];
+          if (orow_idx < 0 || orow_idx >= args.out_rows) {
+            record_status(args.status, kErrBadRow);
+            st = false;
+          } else if (args.row_scale != nullptr) {
+            scale = args.row_scale[orow_idx];
+          }
+        }
+      }
+      bool ok = mbar_wait(&acc_full[acc], acc_ph, abort_flag, args.status,
+                                  kErrTimeoutAccFull);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
+      epilogue_tile<BN, EPI, kHalves>(args, tb, row, valid, st, orow_idx, scale, nt, half,
+                                      sOut + (warp - 4) * kEpiStageBytes, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc ? release1 : release0);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // nothing targets either CTA after this point
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace moe

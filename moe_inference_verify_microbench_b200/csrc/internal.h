@@ -21,21 +21,35 @@ enum ReturnCode : int {
 };
 
 // Launch with programmatic stream serialisation, so the kernel may be
-// scheduled while its predecessor in the stream is finishing (see pdl_wait).
+// scheduled while its predecessor in the stream is finishing (see pdl_wait);
+// `cluster_x` > 1 groups consecutive CTAs into clusters of that size.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                       cudaStream_t stream, Args&&... args) {
+cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, unsigned cluster_x, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (cluster_x > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+  }
+  cfg.attrs = attr;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  return launch_pdl_cluster(kernel, grid, block, smem, stream, 1u, std::forward<Args>(args)...);
 }
 
 int sort_num_blocks(int R);
@@ -56,16 +70,25 @@ int launch_combine(const void* rows, int n_rows, const int* slot_src, const floa
 int launch_router(const void* x, const void* wr, const float* bias, int T, int H, int E, int k,
                   int norm_topk_prob, int* ids_out, float* w_out, void* logits_out, int* status,
                   cudaStream_t stream);
+// tile_rows: the height of the tile table's row blocks, 128 (MOE_BLOCK_M) or
+// kPairTileRows (CTA-pair kernels, large batches).
+constexpr int kPairTileRows = 256;
 int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_tiles, int max_tiles,
                       const void* w_gate, const void* w_up, int E, int H, int I, void* h_out,
-                      int* status, cudaStream_t stream);
+                      int* status, cudaStream_t stream, int tile_rows = 128);
 int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, int index_div,
                              int M, const int4* tiles, const int* num_tiles, int max_tiles,
                              const void* w_gate, const void* w_up, int E, int H, int I,
                              void* h_out, int* status, cudaStream_t stream);
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
-              void* out, int out_rows, int* status, cudaStream_t stream);
+              void* out, int out_rows, int* status, cudaStream_t stream, int tile_rows = 128);
+
+// CTA-pair GEMMs pay off once the average expert has a full pair tile of rows.
+inline bool use_pair_gemm(long long R, int E, int H, int I) {
+  return R >= static_cast<long long>(kPairTileRows) * E && (I % 128) == 0 && (H % 256) == 0 &&
+         (H % 64) == 0 && (I % 64) == 0;
+}
 
 int device_sm_count();
 

@@ -81,6 +81,32 @@ def test_layer_zipf_bias(cuda):
     assert mo.rel_err(y, o["y"]) <= REL_TOL
 
 
+@pytest.mark.parametrize("T,k,E", [(2048, 4, 16), (1500, 8, 32)])
+def test_layer_pair_gemm_path(cuda, T, k, E):
+    """Batches with >= 256 routing records per expert run 256-row tiles on the
+    CTA-pair GEMMs (ragged experts, partial pair tiles): oracle parity, and
+    agreement with the op-by-op pipeline on 128-row tiles and single-CTA GEMMs."""
+    H, I = 256, 128
+    d = mo.make_inputs(T, H, I, E, seed=T + E)
+    assert T * k >= 256 * E
+    y, ids, w, lg = _layer(cuda, d, k)
+    f = {n: mo.f32_from_bf16_bits(d[n]) for n in ("x", "wr", "w_gate", "w_up", "w_down")}
+    o = mo.permuted_moe(f["x"], f["wr"], f["w_gate"], f["w_up"], f["w_down"], k, True, mode="fp32",
+                        logits=lg)
+    assert np.array_equal(ids, o["ids"])
+    assert mo.rel_err(y, o["y"]) <= REL_TOL
+    args = [to_t(d[n], cuda) for n in ("x", "wr", "w_gate", "w_up", "w_down")]
+    it, wt, _ = ops.router_topk(args[0], args[1], k)
+    s = ops.sort_align(it, E)
+    xs = ops.gather_rows(args[0], s.perm, k)
+    h = ops.grouped_w13_swiglu(xs, s.tiles, s.num_tiles, s.max_tiles, args[2], args[3])
+    sl = ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, args[4], row_map=s.perm,
+                        slot_scale=wt.reshape(-1))
+    y2 = to_f32(ops.combine(sl, T, k))
+    ops.check_status(cuda)
+    assert mo.rel_err(y, y2) <= 1e-2
+
+
 def test_layer_t16384_properties(cuda):
     """Full benchmark size: routing metadata bit-exact, sampled outputs in tolerance,
     and two runs bitwise identical."""
