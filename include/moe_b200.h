@@ -98,8 +98,8 @@ MOE_API int moe_sort_align(const int32_t* topk_ids, int R, int E, int e_begin, i
  * device allocation, or a serving process that forbids allocation, and the
  * device synchronisation cudaMalloc may bring, once it is running).  It calls
  * no allocator.
- * Limit: ceil(R / 4096) * E_local <= MOE_SORT_STATIC_SCRATCH_INTS (for
- * E_local = 128, R <= 2,097,152 records); larger requests return
+ * Limit: ceil(R / 2048) * E_local <= MOE_SORT_STATIC_SCRATCH_INTS (for
+ * E_local = 128, R <= 1,048,576 records); larger requests return
  * MOE_RC_WORKSPACE and launch nothing.
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call

@@ -190,6 +190,8 @@ int launch_router(const void* x, const void* wr, const float* bias, int T, int H
   g.ids_out = ids_out;
   g.w_out = w_out;
   g.logits_out = static_cast<__nv_bfloat16*>(logits_out);
+  // E <= 128 fills a 128-column accumulator: half the B stage, six stages deep.
+  if (E <= 128) return launch_gemm<128, kEpiRouter, 6>(ma, mb, mb, g, g.max_tiles, stream);
   return launch_gemm<256, kEpiRouter, 4>(ma, mb, mb, g, g.max_tiles, stream);
 }
 

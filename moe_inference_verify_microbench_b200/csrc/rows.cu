@@ -36,7 +36,22 @@ __global__ void __launch_bounds__(kRowsThreads) gather_rows(const uint4* __restr
     }
     const uint4* a = src + static_cast<size_t>(s) * vec_per_row;
     uint4* b = dst + static_cast<size_t>(p) * vec_per_row;
-    for (int v = lane; v < vec_per_row; v += 32) b[v] = __ldg(a + v);
+    // Eight loads in flight per lane before the stores; the gathered rows are
+    // written with the streaming hint so the source rows (each read k times)
+    // keep their place in L2.
+    for (int v0 = 0; v0 < vec_per_row; v0 += 8 * 32) {
+      uint4 buf[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int v = v0 + u * 32 + lane;
+        if (v < vec_per_row) buf[u] = __ldg(a + v);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int v = v0 + u * 32 + lane;
+        if (v < vec_per_row) __stcs(b + v, buf[u]);
+      }
+    }
   }
 }
 

@@ -7,7 +7,7 @@
 // repeat_interleave).
 //
 // Three launches over R = T*k routing records (flat slot index s = n*k + j;
-// one launch, sa_small, when R <= 4096 and E_local <= 256):
+// one launch, sa_small, when R <= 2048 and E_local <= 256):
 //   1. sa_hist     per-CTA expert histograms of a contiguous record chunk
 //   2. sa_scan     one CTA: per-expert counts, offsets[E+1], the per-CTA base of
 //                  every expert, and the 128-row tile table
@@ -62,19 +62,31 @@ __global__ void __launch_bounds__(1024) sa_scan(int* __restrict__ hist, int nblk
   const int e = threadIdx.x;
   int run = 0;
   if (e < E_local) {
-    for (int b = 0; b < nblk; ++b) {
+    // hist[b][e] becomes the records of expert e in chunks before b; eight
+    // independent loads are in flight per batch.
+    int b = 0;
+    for (; b + 8 <= nblk; b += 8) {
+      int c[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) c[u] = hist[static_cast<size_t>(b + u) * E_local + e];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        hist[static_cast<size_t>(b + u) * E_local + e] = run;
+        run += c[u];
+      }
+    }
+    for (; b < nblk; ++b) {
       int* h = hist + static_cast<size_t>(b) * E_local + e;
       const int c = *h;
-      *h = run;  // records of expert e in earlier chunks
+      *h = run;
       run += c;
     }
   }
   const int off = block_exclusive_scan(e < E_local ? run : 0, warp_sums, &total);
   if (e < E_local) {
     counts[e] = run;
-    offsets[e] = off;
+    offsets[e] = off;  // sa_scatter adds it to its chunk's base
     if (offsets64 != nullptr) offsets64[e] = off;
-    for (int b = 0; b < nblk; ++b) hist[static_cast<size_t>(b) * E_local + e] += off;
   }
   if (e == 0) {
     offsets[E_local] = total;
@@ -87,6 +99,7 @@ __global__ void __launch_bounds__(1024) sa_scan(int* __restrict__ hist, int nblk
 __global__ void __launch_bounds__(kSortThreads) sa_scatter(const int* __restrict__ ids, int R, int E,
                                                            int e_begin, int E_local,
                                                            const int* __restrict__ hist,
+                                                           const int* __restrict__ offsets,
                                                            int* __restrict__ perm,
                                                            int* __restrict__ inv, int* status) {
   pdl_wait();
@@ -97,7 +110,7 @@ __global__ void __launch_bounds__(kSortThreads) sa_scatter(const int* __restrict
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kWarps = kSortThreads / 32;
   for (int e = threadIdx.x; e < E_local; e += blockDim.x) {
-    base[e] = hist[static_cast<size_t>(blockIdx.x) * E_local + e];
+    base[e] = hist[static_cast<size_t>(blockIdx.x) * E_local + e] + offsets[e];
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) wcnt[w * E_local + e] = 0;
   }
@@ -199,8 +212,8 @@ int launch_sort_align(const int* ids, int R, int E, int e_begin, int E_local, in
     return kRcCudaError;
   if (nblk > 0) {
     if (launch_pdl(sa_scatter, dim3(nblk), dim3(kSortThreads), sh_scatter, stream, ids, R, E,
-                   e_begin, E_local, static_cast<const int*>(hist), perm, inv,
-                   status) != cudaSuccess)
+                   e_begin, E_local, static_cast<const int*>(hist),
+                   static_cast<const int*>(offsets), perm, inv, status) != cudaSuccess)
       return kRcCudaError;
   }
   return kRcOk;

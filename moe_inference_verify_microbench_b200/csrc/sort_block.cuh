@@ -7,7 +7,7 @@
 namespace moe {
 
 constexpr int kSortThreads = 256;
-constexpr int kSortItems = 16;  // records per thread per CTA chunk
+constexpr int kSortItems = 8;  // records per thread per CTA chunk
 constexpr int kSortChunk = kSortThreads * kSortItems;
 
 __device__ __forceinline__ int local_expert(const int* ids, int r, int E, int e_begin, int E_local,

@@ -76,7 +76,7 @@ def test_static_scratch_matches_workspace_entry_point(cuda, R, E, e_begin, e_loc
 
 def test_static_scratch_refuses_oversize(cuda):
     lib = _native.load()
-    R, E = 4096 * 600, 128  # 600 CTAs x 128 experts > 65536 ints
+    R, E = 4096 * 600, 128  # 1200 chunks of 2048 records x 128 experts > 65536 ints
     ids = torch.zeros(R, dtype=torch.int32, device=cuda)  # full size: in bounds either way
     o, mt = _outputs(cuda, R, E)
     rc = lib.moe_sort_align_static_scratch(_p(ids), R, E, 0, E, _p(o["counts"]), _p(o["offsets"]),
