@@ -209,7 +209,8 @@ def config_block(T: int, n: int) -> dict:
         par = f"ep{n}"
     return {"workload": wl, "tokens_per_rank": T, "hidden": H, "intermediate": I, "experts": E,
             "top_k": K_TOP, "routing": "uniform (router N(0,0.02), no bias)", "parallelism": par,
-            "l2": "inputs larger than L2: 1.21 GB of expert weights streamed per step"}
+            "l2": "inputs larger than L2: 1.21 GB of expert weights streamed per step; "
+                  "sweep: L2 flushed (512 MB write) before each timed replay"}
 
 
 class Timer:
@@ -227,6 +228,26 @@ class Timer:
 
     def ms(self):
         return self.a.elapsed_time(self.b)
+
+
+# DRAM bytes (read + write) of one launch of the gate/up GEMM at the bench
+# workload, from the one-pass ncu capture summarised in
+# profiles/w13_pair_gather_t16384.md.
+W13_TRAFFIC = {(16384, 256): 1210507520 + 192126208}
+
+
+def w13_kernel_name(tile_rows):
+    if tile_rows == 256:
+        return "grouped_gemm_pair_kernel<SwiGLU,6,gather> (w13, 2-CTA cluster)"
+    return "grouped_gemm_kernel<BN,SwiGLU,stages,gather> (w13)"
+
+
+def layer_launches(T, tile_rows):
+    """Kernels moe_layer_forward launches for T tokens (large-batch path):
+    router, sort (one kernel up to 2048 records, else three), gate/up with the
+    gather fused, down, combine."""
+    R = T * K_TOP
+    return 1 + (1 if R <= 2048 else 3) + 1 + 1 + 1
 
 
 def run_ours_single(args):
@@ -262,7 +283,8 @@ def run_ours_single(args):
 
     # --- per-kernel breakdown: the launches of moe_layer_forward, issued one C-ABI
     # call at a time into preallocated buffers, CUDA events between them.
-    ev, n_active = kernel_breakdown(dev, x, wr, wg, wu, wd, T, max(3, min(args.steps, 50)))
+    ev, n_active, tile_rows = kernel_breakdown(dev, x, wr, wg, wu, wd, T,
+                                               max(3, min(args.steps, 50)))
     avg = {n: statistics.mean(v) for n, v in ev.items()}
 
     # --- e2e: PermutedSparseMoE.forward with host copies inside the timed region
@@ -302,9 +324,9 @@ def run_ours_single(args):
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded x~N(0,1), weights~N(0,0.02), random-init Qwen3-30B-A3B MoE shapes)",
         "config": config_block(T, 1),
-        "roofline": {"bound": "tensor", "kernel": "grouped_gemm_kernel<256,SwiGLU> (w13)",
+        "roofline": {"bound": "tensor", "kernel": w13_kernel_name(tile_rows),
                      "achieved": w13_tflops, "peak": peak_tc, "unit": "TFLOP/s",
-                     "frac": w13_tflops / peak_tc, "traffic": None,
+                     "frac": w13_tflops / peak_tc, "traffic": W13_TRAFFIC.get((T, tile_rows)),
                      "peak_source": f"{peak_kind} bf16_tflops_sustained",
                      "algorithmic_per_launch": f"2*T*k*(2I)*H = {w13_flop:.4g} FLOP"},
         "layer_roofline": {"t_roof_ms": t_roof * 1e3, "frac": t_roof * 1e3 / ms_step,
@@ -314,7 +336,7 @@ def run_ours_single(args):
         "e2e": {"value": T * n_e2e / (te.ms() * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
                 "api": "PermutedSparseMoE.forward", "steps": n_e2e},
-        "gpu_launches": 8 * args.steps,
+        "gpu_launches": layer_launches(T, tile_rows) * args.steps,
         "clocks": clk,
     }
     if args.cpu_baseline:
@@ -332,20 +354,23 @@ def run_ours_single(args):
 
 
 def kernel_breakdown(dev, x, wr, wg, wu, wd, T, n_steps):
-    """Per-kernel device time of the layer's launch sequence (router, sort,
-    gather, w13, w2, combine) through the C ABI, buffers preallocated so the
-    host enqueues fast; a sleep kernel first lets the host fill the queue, so
-    the events bracket GPU work only."""
+    """Per-kernel device time of the layer's own launch sequence at this size
+    (router, sort into the layer's tile height, gate/up GEMM with the row
+    gather fused, down GEMM, combine) through the C ABI, buffers preallocated
+    so the host enqueues fast; a sleep kernel first lets the host fill the
+    queue, so the events bracket GPU work only.  Returns (times, active
+    experts, tile height)."""
     import ctypes
 
     from moe_inference_verify_microbench_b200 import _native, ops
     lib = _native.load()
     P = lambda t: None if t is None else ctypes.c_void_p(t.data_ptr())  # noqa: E731
     R = T * K_TOP
+    rows = lib.moe_layer_tile_rows(T, H, I, E, K_TOP)
     i32, bf = torch.int32, torch.bfloat16
     ids = torch.empty(T, K_TOP, dtype=i32, device=dev)
     w = torch.empty(T, K_TOP, dtype=torch.float32, device=dev)
-    mt = lib.moe_max_tiles(R, E)
+    mt = lib.moe_max_tiles_rows(R, E, rows)
     wsb = lib.moe_sort_align_workspace_bytes(R, E)
     ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
     counts = torch.empty(E, dtype=i32, device=dev)
@@ -353,22 +378,21 @@ def kernel_breakdown(dev, x, wr, wg, wu, wd, T, n_steps):
     perm = torch.empty(R, dtype=i32, device=dev)
     tiles = torch.empty(mt, 4, dtype=i32, device=dev)
     nt = torch.empty(1, dtype=i32, device=dev)
-    sx = torch.empty(R, H, dtype=bf, device=dev)
     h = torch.empty(R, I, dtype=bf, device=dev)
     sl = torch.empty(R, H, dtype=bf, device=dev)
     y = torch.empty(T, H, dtype=bf, device=dev)
     st = ops.status_word(dev)
     S = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-    names = ["router", "sort", "gather", "w13", "w2", "combine"]
+    names = ["router", "sort", "w13", "w2", "combine"]
     calls = [
         lambda: lib.moe_router_topk(P(x), P(wr), None, T, H, E, K_TOP, 1, P(ids), P(w), None, P(st), S),
-        lambda: lib.moe_sort_align(P(ids), R, E, 0, E, P(ws), wsb, P(counts), P(offs), None,
-                                   P(perm), None, P(tiles), mt, P(nt), P(st), S),
-        lambda: lib.moe_gather_rows(P(x), T, P(perm), R, None, K_TOP, H, P(sx), P(st), S),
-        lambda: lib.moe_grouped_w13_swiglu(P(sx), R, P(tiles), P(nt), mt, P(wg), P(wu), E, H, I,
-                                           P(h), P(st), S),
-        lambda: lib.moe_grouped_w2(P(h), R, P(tiles), P(nt), mt, P(wd), E, H, I, P(perm), P(w),
-                                   P(sl), R, P(st), S),
+        lambda: lib.moe_sort_align_rows(P(ids), R, E, 0, E, P(ws), wsb, P(counts), P(offs), None,
+                                        P(perm), None, P(tiles), mt, P(nt), rows, P(st), S),
+        lambda: lib.moe_grouped_w13_swiglu_gather_rows(P(x), T, P(perm), K_TOP, R, P(tiles), P(nt),
+                                                       mt, P(wg), P(wu), E, H, I, P(h), rows,
+                                                       P(st), S),
+        lambda: lib.moe_grouped_w2_rows(P(h), R, P(tiles), P(nt), mt, P(wd), E, H, I, P(perm), P(w),
+                                        P(sl), R, rows, P(st), S),
         lambda: lib.moe_combine(P(sl), R, None, None, None, 0, E, T, K_TOP, H, P(y), P(st), S),
     ]
 
@@ -395,14 +419,17 @@ def kernel_breakdown(dev, x, wr, wg, wu, wd, T, n_steps):
     ops.check_status(dev)
     ev = {n: [m[i].elapsed_time(m[i + 1]) for m in all_marks] for i, n in enumerate(names)}
     n_active = int((counts > 0).sum().item())
-    return ev, n_active
+    return ev, n_active, rows
 
 
 def sweep(dev, token_counts, wr, wg, wu, wd, peaks):
-    """Decode / prefill sweep: CUDA-graph-captured layer, inputs resident."""
+    """Decode / prefill sweep: CUDA-graph-captured layer, inputs resident.  A
+    512 MB buffer is written before every replay (outside the timed events), so
+    each layer call finds the weights in HBM, not in the 126 MB L2."""
     from moe_inference_verify_microbench_b200 import ops
     out = {}
     stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
     for T in token_counts:
         g = torch.Generator(device=dev)
         g.manual_seed(T)
@@ -415,22 +442,30 @@ def sweep(dev, token_counts, wr, wg, wu, wd, peaks):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             ops.moe_layer(x, wr, wg, wu, wd, K_TOP, out=y, workspace=ws)
-        n = 200 if T <= 1024 else 40
+        n = 50 if T <= 1024 else 20
         for _ in range(3):
             graph.replay()
         torch.cuda.synchronize()
-        with Timer(stream) as t:
-            for _ in range(n):
-                graph.replay()
+        evs = []
+        for _ in range(n):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            graph.replay()
+            b.record(stream)
+            evs.append((a, b))
         torch.cuda.synchronize()
-        ms = t.ms() / n
+        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
         ids, _, _ = ops.router_topk(x, wr, K_TOP)
         n_act = int(torch.bincount(ids.reshape(-1).long(), minlength=E).gt(0).sum())
         peak_tc = peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]
         t_roof = max(layer_flops(T) / (peak_tc * 1e12), layer_bytes(n_act, T) / (peaks["hbm_gbs"] * 1e9))
         out[str(T)] = {"tokens_per_s": T / (ms * 1e-3), "us_per_layer": ms * 1e3,
-                       "roofline_frac": t_roof * 1e3 / ms, "active_experts": n_act}
+                       "roofline_frac": t_roof * 1e3 / ms, "active_experts": n_act,
+                       "hbm_gbs": layer_bytes(n_act, T) / (ms * 1e-3) / 1e9}
         del graph
+    del flush
     return out
 
 

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define MOE_B200_ABI_VERSION 1
+#define MOE_B200_ABI_VERSION 2
 
 #define MOE_RC_OK 0
 #define MOE_RC_BAD_ARGUMENT (-1)
@@ -44,8 +44,10 @@ extern "C" {
 #define MOE_RC_TENSOR_MAP (-4)
 #define MOE_RC_WORKSPACE (-5)
 
-/* Rows per M-tile of the grouped GEMMs (the C9 BLOCK_M, fixed at 128 here). */
+/* Rows per M-tile of the grouped GEMMs (the C9 BLOCK_M), and the taller
+ * tile of the 2-CTA cluster-pair GEMMs that large batches use (ABI 2). */
 #define MOE_BLOCK_M 128
+#define MOE_PAIR_TILE_ROWS 256
 
 MOE_API int moe_abi_version(void);
 
@@ -196,6 +198,41 @@ MOE_API int moe_layer_forward(const void* x, const void* router_weight, const fl
                       const void* w_gate, const void* w_up, const void* w_down, int T, int H,
                       int I, int E, int top_k, int norm_topk_prob, void* workspace,
                       size_t workspace_bytes, void* y, int32_t* status, cudaStream_t stream);
+
+/*
+ * ABI 2: tile tables of either height.  moe_layer_forward sorts into
+ * MOE_PAIR_TILE_ROWS-row tiles once the average expert has >= 1024 routing
+ * records and then runs its grouped GEMMs as 2-CTA cluster pairs
+ * (tcgen05.mma.cta_group::2, M = 256), gathering the token rows inside the
+ * gate/up GEMM.  The *_rows entry points are the entry points above with the
+ * height of the tile table they build or read (MOE_BLOCK_M or
+ * MOE_PAIR_TILE_ROWS) as an extra argument; with MOE_BLOCK_M they are
+ * identical to them.  moe_layer_tile_rows returns the height the layer picks
+ * for a shape, so a caller can run the layer's own kernels one by one.
+ */
+MOE_API int moe_layer_tile_rows(int T, int H, int I, int E, int top_k);
+MOE_API int moe_max_tiles_rows(int R, int E_local, int tile_rows);
+MOE_API int moe_sort_align_rows(const int32_t* topk_ids, int R, int E, int e_begin, int E_local,
+                                void* workspace, size_t workspace_bytes, int32_t* counts,
+                                int32_t* offsets, int64_t* offsets64, int32_t* perm, int32_t* inv,
+                                int32_t* tiles, int max_tiles, int32_t* num_tiles, int tile_rows,
+                                int32_t* status, cudaStream_t stream);
+MOE_API int moe_grouped_w13_swiglu_rows(const void* sorted_x, int M, const int32_t* tiles,
+                                        const int32_t* num_tiles, int max_tiles,
+                                        const void* w_gate, const void* w_up, int E, int H, int I,
+                                        void* h, int tile_rows, int32_t* status,
+                                        cudaStream_t stream);
+MOE_API int moe_grouped_w13_swiglu_gather_rows(const void* src, int src_rows,
+                                               const int32_t* index, int index_div, int M,
+                                               const int32_t* tiles, const int32_t* num_tiles,
+                                               int max_tiles, const void* w_gate, const void* w_up,
+                                               int E, int H, int I, void* h, int tile_rows,
+                                               int32_t* status, cudaStream_t stream);
+MOE_API int moe_grouped_w2_rows(const void* h, int M, const int32_t* tiles,
+                                const int32_t* num_tiles, int max_tiles, const void* w_down, int E,
+                                int H, int I, const int32_t* row_map, const float* slot_scale,
+                                void* out, int out_rows, int tile_rows, int32_t* status,
+                                cudaStream_t stream);
 
 #ifdef __cplusplus
 }

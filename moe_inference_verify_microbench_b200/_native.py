@@ -43,9 +43,22 @@ SIGNATURES: dict[str, tuple] = {
     "moe_layer_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "moe_layer_forward": (_c_int, [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _c_int, _c_int, _c_int,
                                    _c_int, _c_int, _c_int, _ptr, _c_size, _ptr, _ptr, _ptr]),
+    # ABI 2: tile tables of either height (128 or 256 rows)
+    "moe_layer_tile_rows": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "moe_max_tiles_rows": (_c_int, [_c_int, _c_int, _c_int]),
+    "moe_sort_align_rows": (_c_int, [_ptr, _c_int, _c_int, _c_int, _c_int, _ptr, _c_size, _ptr,
+                                     _ptr, _ptr, _ptr, _ptr, _ptr, _c_int, _ptr, _c_int, _ptr,
+                                     _ptr]),
+    "moe_grouped_w13_swiglu_rows": (_c_int, [_ptr, _c_int, _ptr, _ptr, _c_int, _ptr, _ptr, _c_int,
+                                             _c_int, _c_int, _ptr, _c_int, _ptr, _ptr]),
+    "moe_grouped_w13_swiglu_gather_rows": (_c_int, [_ptr, _c_int, _ptr, _c_int, _c_int, _ptr,
+                                                    _ptr, _c_int, _ptr, _ptr, _c_int, _c_int,
+                                                    _c_int, _ptr, _c_int, _ptr, _ptr]),
+    "moe_grouped_w2_rows": (_c_int, [_ptr, _c_int, _ptr, _ptr, _c_int, _ptr, _c_int, _c_int,
+                                     _c_int, _ptr, _ptr, _ptr, _c_int, _c_int, _ptr, _ptr]),
 }
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

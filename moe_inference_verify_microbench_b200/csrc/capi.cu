@@ -37,9 +37,27 @@ LayerPlan plan_layer(int T, int E, int k) {
   return p;
 }
 
+// How one layer call runs: decode kernels, tile height, whether the gate/up
+// GEMM gathers its rows itself (then no gathered copy is allocated).
+struct LayerPath {
+  bool small;
+  int tile_rows;
+  bool fuse_gather;
+};
+
+LayerPath layer_path(long long R, int H, int I, int E) {
+  LayerPath lp;
+  lp.small = use_gemv_w13(R);
+  lp.tile_rows = !lp.small && use_pair_gemm(R, E, H, I) ? kPairTileRows : MOE_BLOCK_M;
+  lp.fuse_gather =
+      lp.small || (lp.tile_rows == kPairTileRows ? kFuseGatherPair : kFuseGatherSingle);
+  return lp;
+}
+
 template <class Body>
 size_t layer_layout(int T, int H, int I, int E, int k, void* ws, Body&& body) {
   const LayerPlan p = plan_layer(T, E, k);
+  const LayerPath lp = layer_path(p.R, H, I, E);
   Carver c(ws);
   int* ids = c.take<int>(p.R);
   float* w = c.take<float>(p.R);
@@ -49,7 +67,7 @@ size_t layer_layout(int T, int H, int I, int E, int k, void* ws, Body&& body) {
   int* perm = c.take<int>(p.R);
   int4* tiles = c.take<int4>(p.max_tiles);
   int* num_tiles = c.take<int>(1);
-  void* sorted_x = c.take<__nv_bfloat16>(p.R * H);
+  void* sorted_x = lp.fuse_gather ? nullptr : c.take<__nv_bfloat16>(p.R * H);
   void* h = c.take<__nv_bfloat16>(p.R * I);
   void* slots = c.take<__nv_bfloat16>(p.R * H);
   body(p, ids, w, sort_ws, counts, offsets, perm, tiles, num_tiles, sorted_x, h, slots);
@@ -92,21 +110,36 @@ size_t moe_sort_align_workspace_bytes(int R, int E_local) {
   return sort_workspace_bytes(R, E_local);
 }
 
-int moe_max_tiles(int R, int E_local) {
-  if (R < 0 || E_local <= 0) return 0;
-  return max_tiles_bound(R, E_local, MOE_BLOCK_M);
+int moe_max_tiles(int R, int E_local) { return moe_max_tiles_rows(R, E_local, MOE_BLOCK_M); }
+
+int moe_max_tiles_rows(int R, int E_local, int tile_rows) {
+  if (R < 0 || E_local <= 0 || (tile_rows != MOE_BLOCK_M && tile_rows != MOE_PAIR_TILE_ROWS))
+    return 0;
+  return max_tiles_bound(R, E_local, tile_rows);
 }
 
 int moe_sort_align(const int32_t* topk_ids, int R, int E, int e_begin, int E_local,
                    void* workspace, size_t workspace_bytes, int32_t* counts, int32_t* offsets,
                    int64_t* offsets64, int32_t* perm, int32_t* inv, int32_t* tiles,
                    int max_tiles, int32_t* num_tiles, int32_t* status, cudaStream_t stream) {
+  return moe_sort_align_rows(topk_ids, R, E, e_begin, E_local, workspace, workspace_bytes, counts,
+                             offsets, offsets64, perm, inv, tiles, max_tiles, num_tiles,
+                             MOE_BLOCK_M, status, stream);
+}
+
+int moe_sort_align_rows(const int32_t* topk_ids, int R, int E, int e_begin, int E_local,
+                        void* workspace, size_t workspace_bytes, int32_t* counts,
+                        int32_t* offsets, int64_t* offsets64, int32_t* perm, int32_t* inv,
+                        int32_t* tiles, int max_tiles, int32_t* num_tiles, int tile_rows,
+                        int32_t* status, cudaStream_t stream) {
   if ((R > 0 && (topk_ids == nullptr || perm == nullptr)) || counts == nullptr ||
       offsets == nullptr || workspace == nullptr || tiles == nullptr || num_tiles == nullptr)
     return kRcBadArgument;
-  if (R < 0 || E_local <= 0 || max_tiles < moe_max_tiles(R, E_local)) return kRcBadArgument;
+  if (tile_rows != MOE_BLOCK_M && tile_rows != MOE_PAIR_TILE_ROWS) return kRcBadArgument;
+  if (R < 0 || E_local <= 0 || max_tiles < moe_max_tiles_rows(R, E_local, tile_rows))
+    return kRcBadArgument;
   if (workspace_bytes < sort_workspace_bytes(R, E_local)) return kRcWorkspace;
-  return launch_sort_align(topk_ids, R, E, e_begin, E_local, MOE_BLOCK_M, workspace, counts,
+  return launch_sort_align(topk_ids, R, E, e_begin, E_local, tile_rows, workspace, counts,
                            offsets, reinterpret_cast<long long*>(offsets64), perm, inv,
                            reinterpret_cast<int4*>(tiles), max_tiles, num_tiles, status, stream);
 }
@@ -131,8 +164,17 @@ int moe_grouped_w13_swiglu(const void* sorted_x, int M, const int32_t* tiles,
                            const int32_t* num_tiles, int max_tiles, const void* w_gate,
                            const void* w_up, int E, int H, int I, void* h, int32_t* status,
                            cudaStream_t stream) {
+  return moe_grouped_w13_swiglu_rows(sorted_x, M, tiles, num_tiles, max_tiles, w_gate, w_up, E, H,
+                                     I, h, MOE_BLOCK_M, status, stream);
+}
+
+int moe_grouped_w13_swiglu_rows(const void* sorted_x, int M, const int32_t* tiles,
+                                const int32_t* num_tiles, int max_tiles, const void* w_gate,
+                                const void* w_up, int E, int H, int I, void* h, int tile_rows,
+                                int32_t* status, cudaStream_t stream) {
+  if (tile_rows != MOE_BLOCK_M && tile_rows != MOE_PAIR_TILE_ROWS) return kRcBadArgument;
   return launch_w13_swiglu(sorted_x, M, reinterpret_cast<const int4*>(tiles), num_tiles, max_tiles,
-                           w_gate, w_up, E, H, I, h, status, stream);
+                           w_gate, w_up, E, H, I, h, status, stream, tile_rows);
 }
 
 int moe_grouped_w13_swiglu_gather(const void* src, int src_rows, const int32_t* index,
@@ -140,17 +182,38 @@ int moe_grouped_w13_swiglu_gather(const void* src, int src_rows, const int32_t* 
                                   const int32_t* num_tiles, int max_tiles, const void* w_gate,
                                   const void* w_up, int E, int H, int I, void* h,
                                   int32_t* status, cudaStream_t stream) {
+  return moe_grouped_w13_swiglu_gather_rows(src, src_rows, index, index_div, M, tiles, num_tiles,
+                                            max_tiles, w_gate, w_up, E, H, I, h, MOE_BLOCK_M,
+                                            status, stream);
+}
+
+int moe_grouped_w13_swiglu_gather_rows(const void* src, int src_rows, const int32_t* index,
+                                       int index_div, int M, const int32_t* tiles,
+                                       const int32_t* num_tiles, int max_tiles,
+                                       const void* w_gate, const void* w_up, int E, int H, int I,
+                                       void* h, int tile_rows, int32_t* status,
+                                       cudaStream_t stream) {
+  if (tile_rows != MOE_BLOCK_M && tile_rows != MOE_PAIR_TILE_ROWS) return kRcBadArgument;
   return launch_w13_swiglu_gather(src, src_rows, index, index_div, M,
                                   reinterpret_cast<const int4*>(tiles), num_tiles, max_tiles,
-                                  w_gate, w_up, E, H, I, h, status, stream);
+                                  w_gate, w_up, E, H, I, h, status, stream, tile_rows);
 }
 
 int moe_grouped_w2(const void* h, int M, const int32_t* tiles, const int32_t* num_tiles,
                    int max_tiles, const void* w_down, int E, int H, int I,
                    const int32_t* row_map, const float* slot_scale, void* out, int out_rows,
                    int32_t* status, cudaStream_t stream) {
+  return moe_grouped_w2_rows(h, M, tiles, num_tiles, max_tiles, w_down, E, H, I, row_map,
+                             slot_scale, out, out_rows, MOE_BLOCK_M, status, stream);
+}
+
+int moe_grouped_w2_rows(const void* h, int M, const int32_t* tiles, const int32_t* num_tiles,
+                        int max_tiles, const void* w_down, int E, int H, int I,
+                        const int32_t* row_map, const float* slot_scale, void* out, int out_rows,
+                        int tile_rows, int32_t* status, cudaStream_t stream) {
+  if (tile_rows != MOE_BLOCK_M && tile_rows != MOE_PAIR_TILE_ROWS) return kRcBadArgument;
   return launch_w2(h, M, reinterpret_cast<const int4*>(tiles), num_tiles, max_tiles, w_down, E, H,
-                   I, row_map, slot_scale, out, out_rows, status, stream);
+                   I, row_map, slot_scale, out, out_rows, status, stream, tile_rows);
 }
 
 int moe_combine(const void* rows, int n_rows, const int32_t* slot_src, const float* slot_w,
@@ -164,6 +227,11 @@ int moe_combine(const void* rows, int n_rows, const int32_t* slot_src, const flo
 size_t moe_layer_workspace_bytes(int T, int H, int I, int E, int top_k) {
   if (T < 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0) return 0;
   return layer_layout(T, H, I, E, top_k, nullptr, [](auto&&...) {});
+}
+
+int moe_layer_tile_rows(int T, int H, int I, int E, int top_k) {
+  if (T < 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0) return 0;
+  return layer_path(static_cast<long long>(T) * top_k, H, I, E).tile_rows;
 }
 
 int moe_layer_forward(const void* x, const void* router_weight, const float* router_bias,
@@ -183,10 +251,9 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                    int* offsets, int* perm, int4* tiles, int* num_tiles, void* sorted_x, void* h,
                    void* slots) {
                  const int R = static_cast<int>(p.R);
-                 const bool small = use_gemv_w13(R);  // decode: weight-streaming kernels
-                 // Large batches: 256-row tiles for the CTA-pair GEMMs.
-                 const int tile_rows = !small && use_pair_gemm(R, E, H, I) ? kPairTileRows
-                                                                           : MOE_BLOCK_M;
+                 const LayerPath lp = layer_path(R, H, I, E);
+                 const bool small = lp.small;  // decode: weight-streaming kernels
+                 const int tile_rows = lp.tile_rows;  // 256: CTA-pair GEMMs
                  const int max_tiles = max_tiles_bound(R, E, tile_rows);
                  if (small && use_router_small(T, H, E, top_k)) {
                    rc = launch_router_sort_small(x, router_weight, router_bias, T, H, E, top_k,
@@ -201,10 +268,12 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                                             nullptr, perm, nullptr, tiles, max_tiles, num_tiles,
                                             status, stream);
                  }
-                 if (rc == kRcOk && small) {
+                 // The gate/up kernel gathers the token rows itself (always for the
+                 // decode GEMV), or a separate gather writes the copy TMA reads.
+                 if (rc == kRcOk && lp.fuse_gather) {
                    rc = launch_w13_swiglu_gather(x, T, perm, top_k, R, tiles, num_tiles,
-                                                 p.max_tiles, w_gate, w_up, E, H, I, h, status,
-                                                 stream);
+                                                 max_tiles, w_gate, w_up, E, H, I, h, status,
+                                                 stream, tile_rows);
                  } else if (rc == kRcOk) {
                    rc = launch_gather_rows(x, T, perm, R, nullptr, top_k, H, sorted_x, status,
                                            stream);

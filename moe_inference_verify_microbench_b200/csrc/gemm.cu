@@ -105,7 +105,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
   return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 
-template <int EPI, int STAGES>
+template <int EPI, int STAGES, bool GATHER_A = false>
 int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
                      const GemmArgs& args, long long work_units, cudaStream_t stream) {
   using L = PairSmem<STAGES>;
@@ -115,7 +115,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensor
   if (cudaGetDevice(&dev) != cudaSuccess) return kRcCudaError;
   const uint64_t bit = 1ull << (dev & 63);
   if ((attr_done.load(std::memory_order_acquire) & bit) == 0) {
-    if (cudaFuncSetAttribute(grouped_gemm_pair_kernel<EPI, STAGES>,
+    if (cudaFuncSetAttribute(grouped_gemm_pair_kernel<EPI, STAGES, GATHER_A>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, L::kTotal) != cudaSuccess)
       return kRcCudaError;
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
@@ -123,8 +123,9 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensor
   const long long pairs = device_sms() / 2;
   const int grid = 2 * static_cast<int>(work_units < pairs ? work_units : pairs);
   if (grid <= 0) return kRcOk;
-  const cudaError_t e = launch_pdl_cluster(grouped_gemm_pair_kernel<EPI, STAGES>, dim3(grid),
-                                           dim3(384), L::kTotal, stream, 2u, a, b0, b1, args);
+  const cudaError_t e =
+      launch_pdl_cluster(grouped_gemm_pair_kernel<EPI, STAGES, GATHER_A>, dim3(grid),
+                         dim3(pair_threads<GATHER_A>()), L::kTotal, stream, 2u, a, b0, b1, args);
   return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 
@@ -256,7 +257,7 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
 int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, int index_div,
                              int M, const int4* tiles, const int* num_tiles, int max_tiles,
                              const void* w_gate, const void* w_up, int E, int H, int I,
-                             void* h_out, int* status, cudaStream_t stream) {
+                             void* h_out, int* status, cudaStream_t stream, int tile_rows) {
   if (src == nullptr || tiles == nullptr || num_tiles == nullptr || w_gate == nullptr ||
       w_up == nullptr || h_out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 ||
       max_tiles < 0 || src_rows < 0 || index_div <= 0)
@@ -268,6 +269,33 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
     return launch_w13_gemv(src, src_rows, index, index_div, M, tiles, num_tiles, max_tiles,
                            w_gate, w_up, E, H, I, h_out, status, stream);
   if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
+  if (tile_rows == kPairTileRows) {
+    if ((I % (kPairBN / 2)) != 0) return kRcUnsupported;
+    CUtensorMap mg, mu;
+    int rc = map_3d(&mg, w_gate, E, I, H, kPairBN / 2);
+    if (rc == kRcOk) rc = map_3d(&mu, w_up, E, I, H, kPairBN / 2);
+    if (rc != kRcOk) return rc;
+    GemmArgs g = blank_args(status);
+    g.tiles = tiles;
+    g.num_tiles = num_tiles;
+    g.max_tiles = max_tiles;
+    g.n_tiles = I / (kPairBN / 2);
+    g.num_kb = H / kBK;
+    g.b_rows = kPairBN;
+    g.a_rows = M;
+    g.num_experts = E;
+    g.out = static_cast<__nv_bfloat16*>(h_out);
+    g.out_ld = I;
+    g.out_rows = M;
+    g.a_src = static_cast<const __nv_bfloat16*>(src);
+    g.a_src_rows = src_rows;
+    g.a_index = index;
+    g.a_index_div = index_div;
+    // A is gathered by the loader warps; the gate map stands in for the unused A map.
+    return launch_gemm_pair<kEpiSwiGLU, kPairStages, true>(
+        mg, mg, mu, g, static_cast<long long>(max_tiles) * g.n_tiles, stream);
+  }
+  if (tile_rows != kBM) return kRcBadArgument;
   const int bn = pick_bn(I, M, max_tiles, 7, [](int b) { return b / 2; });
   CUtensorMap mg, mu;
   int rc = map_3d(&mg, w_gate, E, I, H, bn / 2);

@@ -20,6 +20,13 @@
 // even CTA's barrier).  Every wait is bounded; a CTA leaves only after the
 // final cluster barrier, so no copy, MMA or remote arrival can target a CTA
 // that has exited.
+//
+// GATHER_A (512 threads): warps 12..15 of each CTA gather its 128 A rows from
+// the source matrix through the index with 16-byte cp.async, as in the
+// single-CTA kernel, and publish a stage kPairGatherLag stages later by
+// arriving on the even CTA's stage barrier; the TMA producer then loads only
+// B.  This fuses the permutation gather (C5/python/solution.py:137) into the
+// gate/up GEMM and removes the gathered copy's round trip through HBM.
 #pragma once
 
 #include "grouped_gemm.cuh"
@@ -28,6 +35,13 @@ namespace moe {
 
 constexpr int kPairBM = 2 * kBM;  // rows of a pair tile (M of the pair MMA)
 constexpr int kPairBN = 256;
+constexpr int kPairGatherWarp0 = 12;  // first of the four A-loader warps (GATHER_A)
+constexpr int kPairGatherLag = 4;     // a stage is published this many stages after its copies
+
+template <bool GATHER_A>
+constexpr int pair_threads() {
+  return GATHER_A ? 512 : 384;
+}
 
 template <int STAGES>
 struct PairSmem {
@@ -38,12 +52,14 @@ struct PairSmem {
   static constexpr int kTotal = 1024 + STAGES * kStageBytes + kOutBytes + 256;
 };
 
-template <int EPI, int STAGES>
-__global__ void __launch_bounds__(384, 1)
+template <int EPI, int STAGES, bool GATHER_A = false>
+__global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB0,
                              const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
   static_assert(EPI == kEpiSwiGLU || EPI == kEpiStore, "pair kernel: SwiGLU or store epilogue");
+  static_assert(!GATHER_A || kPairGatherLag < STAGES - 1,
+                "a loader must publish before it needs the stage back");
   using L = PairSmem<STAGES>;
   constexpr int BN = kPairBN;
   constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
@@ -71,7 +87,9 @@ __global__ void __launch_bounds__(384, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);   // the even CTA's producer (+ the bytes of both CTAs)
+      // The even CTA's producer (+ the bytes of both CTAs), and with GATHER_A
+      // every loader warp of both CTAs.
+      mbar_init(&full[s], GATHER_A ? 1 + 2 * 4 : 1);
       mbar_init(&empty[s], 1);  // one MMA commit
     }
     for (int a = 0; a < 2; ++a) {
@@ -88,7 +106,7 @@ __global__ void __launch_bounds__(384, 1)
     tmem_relinquish_pair();
   }
   if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&tmA);
+    if (!GATHER_A) tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB0);
     if (EPI == kEpiSwiGLU) tma_prefetch_desc(&tmB1);
   }
@@ -104,7 +122,7 @@ __global__ void __launch_bounds__(384, 1)
   const int total = num_tiles * args.n_tiles;
   const int pair = static_cast<int>(blockIdx.x >> 1);
   const int npairs = static_cast<int>(gridDim.x >> 1);
-  const uint32_t stage_tx = static_cast<uint32_t>(L::kStageBytes);
+  const uint32_t stage_tx = static_cast<uint32_t>(GATHER_A ? L::kBBytes : L::kStageBytes);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -131,7 +149,7 @@ __global__ void __launch_bounds__(384, 1)
           }
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * stage_tx);
           const uint32_t fb = cluster_addr(&full[s], 0);
-          tma_load_2d_pair(sA + s * L::kABytes, &tmA, fb, kb * kBK, arow);
+          if (!GATHER_A) tma_load_2d_pair(sA + s * L::kABytes, &tmA, fb, kb * kBK, arow);
           uint8_t* b = sB + s * L::kBBytes;
           if (EPI == kEpiSwiGLU) {
             tma_load_3d_pair(b, leader ? &tmB0 : &tmB1, fb, kb * kBK, nt * (BN / 2), t.x);
@@ -204,6 +222,77 @@ __global__ void __launch_bounds__(384, 1)
       while (!mbar_try_wait(drain, 0)) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) break;
       }
+    }
+  } else if (GATHER_A && warp >= kPairGatherWarp0) {
+    // ---------------------------------------------------------- A-row loaders
+    // Thread g = 0..127 copies 16-byte chunk (g % 8) of this CTA's tile rows
+    // (g / 8) + 16 j, j = 0..7, into the 128-byte-swizzled layout TMA would write.
+    const int g = threadIdx.x - kPairGatherWarp0 * 32;
+    const uint32_t chunk = static_cast<uint32_t>(g & 7);
+    const int row0 = g >> 3;
+    const int K = args.num_kb * kBK;
+    int s = 0;
+    uint32_t ph = 0;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int w = pair; ok && w < total; w += npairs) {
+      const int mt = w / args.n_tiles;
+      const int4 t = load_tile(args, mt);
+      const int base = t.y + kBM * static_cast<int>(rank);
+      const __nv_bfloat16* src[8];
+      uint32_t present = 0;  // bit j: row j of this thread exists
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int p = base + row0 + 16 * j;
+        src[j] = args.a_src;  // any valid address when the row is absent (zero-filled)
+        if (p < t.z) {
+          const int i = args.a_index != nullptr ? args.a_index[p] / args.a_index_div : p;
+          if (i >= 0 && i < args.a_src_rows) {
+            src[j] = args.a_src + static_cast<size_t>(i) * K + chunk * 8;
+            present |= 1u << j;
+          } else {
+            record_status(args.status, kErrBadRow);
+          }
+        }
+      }
+      for (int kb = 0; kb < args.num_kb; ++kb) {
+        bool got = mbar_wait(&empty[s], ph ^ 1u, abort_flag, args.status, kErrTimeoutEmpty);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        const uint32_t sbase = smem_u32(sA + s * L::kABytes);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t r = static_cast<uint32_t>(row0 + 16 * j);
+          const uint32_t dst = sbase + r * 128u + ((chunk ^ (r & 7u)) << 4);
+          const bool have = (present >> j) & 1u;
+          cp_async_16(dst, have ? src[j] + kb * kBK : src[j], have ? 16u : 0u);
+        }
+        cp_async_commit();
+        if (it >= static_cast<uint32_t>(kPairGatherLag)) {
+          cp_async_wait_group<kPairGatherLag>();
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0)
+            mbar_arrive_cluster(cluster_addr(&full[(it - kPairGatherLag) % STAGES], 0));
+        }
+        ++it;
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+    // Publish the stages still in flight (also on abort), then let every copy land.
+    cp_async_wait_all();
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t first = it > static_cast<uint32_t>(kPairGatherLag) ? it - kPairGatherLag : 0u;
+      for (uint32_t i = first; i < it; ++i)
+        mbar_arrive_cluster(cluster_addr(&full[i % STAGES], 0));
     }
   } else if (warp >= 4 && warp < 4 + kEpiWarps) {
     // -------------------------------------------------------------- epilogue

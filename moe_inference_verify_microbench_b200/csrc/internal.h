@@ -79,15 +79,25 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
 int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, int index_div,
                              int M, const int4* tiles, const int* num_tiles, int max_tiles,
                              const void* w_gate, const void* w_up, int E, int H, int I,
-                             void* h_out, int* status, cudaStream_t stream);
+                             void* h_out, int* status, cudaStream_t stream, int tile_rows = 128);
+
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
               void* out, int out_rows, int* status, cudaStream_t stream, int tile_rows = 128);
 
-// CTA-pair GEMMs pay off once the average expert has a full pair tile of rows.
+// CTA-pair GEMMs pay off once the average expert has kPairMinRowsPerExpert
+// rows: below that the padding of its last 256-row tile costs more tensor
+// work than the halved B traffic saves (measured crossover on B200 between
+// 512 and 1024 rows per expert).
+constexpr int kPairMinRowsPerExpert = 1024;
+// Whether the gate/up GEMM gathers the token rows itself (cp.async loader
+// warps) instead of reading a gathered copy written by a separate kernel.
+constexpr bool kFuseGatherPair = true;
+constexpr bool kFuseGatherSingle = true;
+
 inline bool use_pair_gemm(long long R, int E, int H, int I) {
-  return R >= static_cast<long long>(kPairTileRows) * E && (I % 128) == 0 && (H % 256) == 0 &&
-         (H % 64) == 0 && (I % 64) == 0;
+  return R >= static_cast<long long>(kPairMinRowsPerExpert) * E && (I % 128) == 0 &&
+         (H % 256) == 0 && (H % 64) == 0 && (I % 64) == 0;
 }
 
 int device_sm_count();

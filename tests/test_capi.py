@@ -39,9 +39,14 @@ def test_exported_dynamic_symbols_match_header():
 
 def test_host_queries():
     lib = _native.load()
-    assert lib.moe_abi_version() == 1
+    assert lib.moe_abi_version() == 2
     assert lib.moe_max_tiles(131072, 128) == 1024 + 128
     assert lib.moe_max_tiles(0, 16) == 16
+    assert lib.moe_max_tiles_rows(131072, 128, 256) == 512 + 128
+    assert lib.moe_max_tiles_rows(131072, 128, 128) == lib.moe_max_tiles(131072, 128)
+    assert lib.moe_max_tiles_rows(1024, 16, 64) == 0  # only 128- and 256-row tiles
+    assert lib.moe_layer_tile_rows(16384, 2048, 768, 128, 8) == 256  # CTA-pair GEMMs
+    assert lib.moe_layer_tile_rows(4096, 2048, 768, 128, 8) == 128
     assert lib.moe_sort_align_workspace_bytes(8192, 128) >= 2 * 128 * 4
     ws = lib.moe_layer_workspace_bytes(16384, 2048, 768, 128, 8)
     assert ws >= 16384 * 8 * (768 + 2048) * 2  # h + weighted slot rows

@@ -81,14 +81,15 @@ def test_layer_zipf_bias(cuda):
     assert mo.rel_err(y, o["y"]) <= REL_TOL
 
 
-@pytest.mark.parametrize("T,k,E", [(2048, 4, 16), (1500, 8, 32)])
+@pytest.mark.parametrize("T,k,E", [(4096, 4, 16), (3000, 8, 16)])
 def test_layer_pair_gemm_path(cuda, T, k, E):
-    """Batches with >= 256 routing records per expert run 256-row tiles on the
-    CTA-pair GEMMs (ragged experts, partial pair tiles): oracle parity, and
-    agreement with the op-by-op pipeline on 128-row tiles and single-CTA GEMMs."""
+    """Batches with >= 1024 routing records per expert run 256-row tiles on the
+    CTA-pair GEMMs, the gate/up one gathering its rows itself (ragged experts,
+    partial pair tiles): oracle parity, and agreement with the op-by-op
+    pipeline on 128-row tiles and single-CTA GEMMs."""
     H, I = 256, 128
     d = mo.make_inputs(T, H, I, E, seed=T + E)
-    assert T * k >= 256 * E
+    assert T * k >= 1024 * E
     y, ids, w, lg = _layer(cuda, d, k)
     f = {n: mo.f32_from_bf16_bits(d[n]) for n in ("x", "wr", "w_gate", "w_up", "w_down")}
     o = mo.permuted_moe(f["x"], f["wr"], f["w_gate"], f["w_up"], f["w_down"], k, True, mode="fp32",
