@@ -250,6 +250,55 @@ def layer_launches(T, tile_rows):
     return 1 + (1 if R <= 2048 else 3) + 1 + 1 + 1
 
 
+def e2e_pipelined(mod, x_host, dev, n_steps):
+    """Milliseconds for n_steps layer calls through the public module, each
+    step copying its input from pinned host memory and its result back to
+    pinned host memory.  The copies run on two copy streams so that one
+    step's input upload and the previous step's download overlap the current
+    step's compute (double-buffered device inputs and host outputs); the
+    events bracket the first upload and the last download."""
+    compute = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    xd = [torch.empty(x_host.shape, dtype=x_host.dtype, device=dev) for _ in range(2)]
+    y_host = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_ready = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+
+    def run(n):
+        for e in in_free + out_done:
+            e.record(compute)
+        for i in range(n):
+            b = i & 1
+            with torch.cuda.stream(up):
+                up.wait_event(in_free[b])
+                xd[b].copy_(x_host, non_blocking=True)
+                in_ready[b].record(up)
+            compute.wait_event(in_ready[b])
+            y = mod(xd[b])
+            in_free[b].record(compute)
+            out_ready[b].record(compute)
+            with torch.cuda.stream(down):
+                down.wait_event(out_ready[b])
+                down.wait_event(out_done[b])
+                y_host[b].copy_(y, non_blocking=True)
+                y.record_stream(down)
+                out_done[b].record(down)
+        for e in out_done:
+            compute.wait_event(e)
+
+    run(2)
+    torch.cuda.synchronize(dev)
+    a = torch.cuda.Event(enable_timing=True)
+    z = torch.cuda.Event(enable_timing=True)
+    a.record(compute)
+    run(n_steps)
+    z.record(compute)
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(z)
+
+
 def run_ours_single(args):
     from moe_inference_verify_microbench_b200 import PermutedSparseMoE, ops
 
@@ -298,17 +347,9 @@ def run_ours_single(args):
         bwd.copy_(wd)
     del wg, wu, wd
     x_host = x.cpu().pin_memory()
-    y_host = torch.empty_like(x_host).pin_memory()
     n_e2e = max(3, min(args.steps, 100))
     with torch.no_grad():
-        for _ in range(2):
-            y_host.copy_(mod(x_host.to(dev, non_blocking=True)), non_blocking=True)
-        torch.cuda.synchronize()
-        with Timer(stream) as te:
-            for _ in range(n_e2e):
-                xd = x_host.to(dev, non_blocking=True)
-                y_host.copy_(mod(xd), non_blocking=True)
-        torch.cuda.synchronize()
+        ms_e2e = e2e_pipelined(mod, x_host, dev, n_e2e)
     clk = clocks.stop()
     ops.check_status(dev)
 
@@ -333,9 +374,11 @@ def run_ours_single(args):
                            "flop_per_step": layer_flops(T), "bytes_per_step": layer_bytes(n_active, T),
                            "active_experts": n_active},
         "breakdown_ms": {n: round(v, 5) for n, v in avg.items()},
-        "e2e": {"value": T * n_e2e / (te.ms() * 1e-3), "unit": "tokens/s",
+        "e2e": {"value": T * n_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
-                "api": "PermutedSparseMoE.forward", "steps": n_e2e},
+                "api": "PermutedSparseMoE.forward", "steps": n_e2e,
+                "pipelining": "step i+1's host->device copy and step i-1's device->host copy "
+                              "run on their own streams (copy engines) while step i computes"},
         "gpu_launches": layer_launches(T, tile_rows) * args.steps,
         "clocks": clk,
     }

@@ -39,16 +39,22 @@ class CudaKernels:
     combine = staticmethod(ops.combine)
 
     @staticmethod
+    def tile_rows(expected_records, e_local, hidden, intermediate):
+        """Tile height for the local grouped GEMMs (256: CTA-pair kernels)."""
+        return ops.tile_rows_for(expected_records, e_local, hidden, intermediate)
+
+    @staticmethod
     def expert_compute(src, index, index_div, s, w_gate, w_up, w_down, row_map=None,
                        slot_scale=None, out_rows=None):
-        """SwiGLU experts on rows src[index[p] // index_div] of the sorted order
-        (rows past the sort's valid count are neither gathered nor computed), w2
-        output to row_map[p] scaled by slot_scale[row_map[p]]."""
-        e_local = s.counts.numel()
-        xs = ops.gather_rows(src, index, index_div, count=s.offsets[e_local:])
-        h = ops.grouped_w13_swiglu(xs, s.tiles, s.num_tiles, s.max_tiles, w_gate, w_up)
+        """SwiGLU experts on rows src[index[p] // index_div] of the sorted order,
+        gathered inside the gate/up GEMM (only the rows the tile table covers,
+        i.e. the sort's valid records, are read or computed), w2 output to
+        row_map[p] scaled by slot_scale[row_map[p]]."""
+        M = s.perm.numel()
+        h = ops.grouped_w13_swiglu_gather(src, index, index_div, M, s.tiles, s.num_tiles,
+                                          s.max_tiles, w_gate, w_up, tile_rows=s.tile_rows)
         return ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, w_down, row_map=row_map,
-                              slot_scale=slot_scale, out_rows=out_rows)
+                              slot_scale=slot_scale, out_rows=out_rows, tile_rows=s.tile_rows)
 
 
 class _EPBase(nn.Module):
@@ -113,8 +119,10 @@ class EPSparseMoELean(_EPBase):
         x_flat = x.reshape(-1, shape[-1]).contiguous()
         N, k = x_flat.shape[0], self.top_k
         ids, w = self._route(x_flat)                                   # full router (C6:127-133)
+        rows = K.tile_rows(N * k // self.ep_size, self.experts_per_rank, self.hidden,
+                           self.intermediate)                          # expected local records
         s = K.sort_align(ids, self.num_experts, self.expert_start,     # local filter + stable sort
-                         self.experts_per_rank)                        # (C6:141-160)
+                         self.experts_per_rank, tile_rows=rows)        # (C6:141-160)
         wg, wu, wd = self.pack()
         slots = K.expert_compute(x_flat, s.perm, k, s, wg, wu, wd,     # gather (C6:156) fused;
                                  row_map=s.perm, slot_scale=w.reshape(-1),  # weighted, to slot
@@ -170,7 +178,9 @@ def dispatch_combine(mod: _EPBase, local_x: torch.Tensor, group) -> torch.Tensor
     n_recv = recv_x.shape[0]
     wg, wu, wd = mod.pack()
     if n_recv > 0:
-        s2 = K.sort_align(recv_e, epr + 1, 0, epr, want_inv=True)    # local re-sort (C7:224-226);
+        rows = K.tile_rows(n_recv * k // ep, epr, mod.hidden, mod.intermediate)
+        s2 = K.sort_align(recv_e, epr + 1, 0, epr, want_inv=True,    # local re-sort (C7:224-226);
+                          tile_rows=rows)
         out = K.expert_compute(recv_x, s2.perm, k, s2, wg, wu, wd)    # id epr marks "not mine"
         partial = K.combine(out, n_recv, k, slot_src=s2.inv,          # weighted sum of the row's
                             slot_w=recv_w.reshape(-1))                # records (C7:259-261)

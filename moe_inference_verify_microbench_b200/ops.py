@@ -113,24 +113,36 @@ class SortResult(NamedTuple):
     tiles: torch.Tensor       # int32 [max_tiles, 4]
     num_tiles: torch.Tensor   # int32 [1]
     max_tiles: int
+    tile_rows: int = 128      # height of the tile table's row blocks (128 or 256)
 
 
-def max_tiles(R: int, e_local: int) -> int:
-    return int(_native.load().moe_max_tiles(int(R), int(e_local)))
+def max_tiles(R: int, e_local: int, tile_rows: int = 128) -> int:
+    return int(_native.load().moe_max_tiles_rows(int(R), int(e_local), int(tile_rows)))
+
+
+def tile_rows_for(records: int, e_local: int, hidden: int, intermediate: int) -> int:
+    """Tile height ``moe_layer_forward`` would pick for this many routing
+    records over ``e_local`` experts: 256 (CTA-pair GEMMs) once the average
+    expert has enough rows, else 128."""
+    return int(_native.load().moe_layer_tile_rows(int(records), int(hidden), int(intermediate),
+                                                  int(e_local), 1))
 
 
 def sort_align(ids: torch.Tensor, num_experts: int, e_begin: int = 0, e_local: int | None = None,
-               want_inv: bool = False, want_offsets64: bool = False) -> SortResult:
-    """Stable sort of the flat routing records by expert plus the 128-row tile
-    table (C5/python/solution.py:131-136, C6/python/solution.py:141-160,
-    C9/python/solution.py:142-159)."""
+               want_inv: bool = False, want_offsets64: bool = False,
+               tile_rows: int = 128) -> SortResult:
+    """Stable sort of the flat routing records by expert plus the tile table of
+    ``tile_rows``-row blocks (C5/python/solution.py:131-136,
+    C6/python/solution.py:141-160, C9/python/solution.py:142-159)."""
     _need(ids, "ids", torch.int32)
     flat = ids.reshape(-1)
     R = flat.numel()
     e_local = num_experts if e_local is None else e_local
     dev = ids.device
     lib = _native.load()
-    mt = int(lib.moe_max_tiles(R, e_local))
+    mt = int(lib.moe_max_tiles_rows(R, e_local, tile_rows))
+    if mt <= 0 and R >= 0:
+        raise ValueError(f"tile_rows must be 128 or 256, got {tile_rows}")
     ws_bytes = int(lib.moe_sort_align_workspace_bytes(R, e_local))
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     counts = torch.empty(e_local, dtype=torch.int32, device=dev)
@@ -140,10 +152,11 @@ def sort_align(ids: torch.Tensor, num_experts: int, e_begin: int = 0, e_local: i
     inv = torch.empty(R, dtype=torch.int32, device=dev) if want_inv else None
     tiles = torch.empty((max(mt, 1), 4), dtype=torch.int32, device=dev)
     num_tiles = torch.empty(1, dtype=torch.int32, device=dev)
-    _rc(lib.moe_sort_align(_p(flat), R, num_experts, e_begin, e_local, _p(ws), ws_bytes,
-                           _p(counts), _p(offsets), _p(off64), _p(perm), _p(inv), _p(tiles), mt,
-                           _p(num_tiles), _p(status_word(dev)), _stream(dev)), "moe_sort_align")
-    return SortResult(counts, offsets, off64, perm, inv, tiles, num_tiles, mt)
+    _rc(lib.moe_sort_align_rows(_p(flat), R, num_experts, e_begin, e_local, _p(ws), ws_bytes,
+                                _p(counts), _p(offsets), _p(off64), _p(perm), _p(inv), _p(tiles),
+                                mt, _p(num_tiles), tile_rows, _p(status_word(dev)), _stream(dev)),
+        "moe_sort_align_rows")
+    return SortResult(counts, offsets, off64, perm, inv, tiles, num_tiles, mt, tile_rows)
 
 
 def tiles_from_offsets(offsets: torch.Tensor, M: int):
@@ -205,7 +218,7 @@ def combine(rows: torch.Tensor, T: int, k: int, slot_src: torch.Tensor | None = 
 
 def grouped_w13_swiglu(a: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor,
                        max_tiles_: int, w_gate: torch.Tensor, w_up: torch.Tensor,
-                       out: torch.Tensor | None = None) -> torch.Tensor:
+                       out: torch.Tensor | None = None, tile_rows: int = 128) -> torch.Tensor:
     """h = silu(a @ w_gate[e]^T) * (a @ w_up[e]^T) per tile (C9/python/solution.py:218-220)."""
     _need(a, "a", torch.bfloat16, 2)
     _need(w_gate, "w_gate", torch.bfloat16, 3)
@@ -216,16 +229,17 @@ def grouped_w13_swiglu(a: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Te
         raise ValueError("w_gate / w_up must be [E, I, H] matching a [M, H]")
     h = out if out is not None else torch.empty((M, I), dtype=torch.bfloat16, device=a.device)
     lib = _native.load()
-    _rc(lib.moe_grouped_w13_swiglu(_p(a), M, _p(tiles), _p(num_tiles), max_tiles_, _p(w_gate),
-                                   _p(w_up), E, H, I, _p(h), _p(status_word(a.device)),
-                                   _stream(a.device)), "moe_grouped_w13_swiglu")
+    _rc(lib.moe_grouped_w13_swiglu_rows(_p(a), M, _p(tiles), _p(num_tiles), max_tiles_,
+                                        _p(w_gate), _p(w_up), E, H, I, _p(h), tile_rows,
+                                        _p(status_word(a.device)), _stream(a.device)),
+        "moe_grouped_w13_swiglu_rows")
     return h
 
 
 def grouped_w13_swiglu_gather(src: torch.Tensor, index: torch.Tensor, index_div: int, M: int,
                               tiles: torch.Tensor, num_tiles: torch.Tensor, max_tiles_: int,
                               w_gate: torch.Tensor, w_up: torch.Tensor,
-                              out: torch.Tensor | None = None) -> torch.Tensor:
+                              out: torch.Tensor | None = None, tile_rows: int = 128) -> torch.Tensor:
     """``grouped_w13_swiglu`` whose A row r is ``src[index[r] // index_div]``: the
     permutation gather (C5/python/solution.py:137) fused into the GEMM."""
     _need(src, "src", torch.bfloat16, 2)
@@ -240,17 +254,18 @@ def grouped_w13_swiglu_gather(src: torch.Tensor, index: torch.Tensor, index_div:
         raise ValueError("index must hold at least M entries")
     h = out if out is not None else torch.empty((M, I), dtype=torch.bfloat16, device=src.device)
     lib = _native.load()
-    _rc(lib.moe_grouped_w13_swiglu_gather(_p(src), src.shape[0], _p(index), index_div, M,
-                                          _p(tiles), _p(num_tiles), max_tiles_, _p(w_gate),
-                                          _p(w_up), E, H, I, _p(h), _p(status_word(src.device)),
-                                          _stream(src.device)), "moe_grouped_w13_swiglu_gather")
+    _rc(lib.moe_grouped_w13_swiglu_gather_rows(_p(src), src.shape[0], _p(index), index_div, M,
+                                               _p(tiles), _p(num_tiles), max_tiles_, _p(w_gate),
+                                               _p(w_up), E, H, I, _p(h), tile_rows,
+                                               _p(status_word(src.device)), _stream(src.device)),
+        "moe_grouped_w13_swiglu_gather_rows")
     return h
 
 
 def grouped_w2(h: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor, max_tiles_: int,
                w_down: torch.Tensor, row_map: torch.Tensor | None = None,
                slot_scale: torch.Tensor | None = None, out: torch.Tensor | None = None,
-               out_rows: int | None = None) -> torch.Tensor:
+               out_rows: int | None = None, tile_rows: int = 128) -> torch.Tensor:
     """out[map(r)] = scale(map(r)) * (h[r] @ w_down[e]^T) (C9/python/solution.py:221)."""
     _need(h, "h", torch.bfloat16, 2)
     _need(w_down, "w_down", torch.bfloat16, 3)
@@ -266,9 +281,10 @@ def grouped_w2(h: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor, ma
         out = torch.empty((out_rows if out_rows is not None else M, H), dtype=torch.bfloat16,
                           device=h.device)
     lib = _native.load()
-    _rc(lib.moe_grouped_w2(_p(h), M, _p(tiles), _p(num_tiles), max_tiles_, _p(w_down), E, H, I,
-                           _p(row_map), _p(slot_scale), _p(out), out.shape[0],
-                           _p(status_word(h.device)), _stream(h.device)), "moe_grouped_w2")
+    _rc(lib.moe_grouped_w2_rows(_p(h), M, _p(tiles), _p(num_tiles), max_tiles_, _p(w_down), E, H,
+                                I, _p(row_map), _p(slot_scale), _p(out), out.shape[0], tile_rows,
+                                _p(status_word(h.device)), _stream(h.device)),
+        "moe_grouped_w2_rows")
     return out
 
 

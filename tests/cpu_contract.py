@@ -28,7 +28,12 @@ class CpuContractKernels:
         return ids.to(torch.int32), w.float(), logits.to(torch.bfloat16)
 
     @staticmethod
-    def sort_align(ids, num_experts, e_begin=0, e_local=None, want_inv=False, want_offsets64=False):
+    def tile_rows(expected_records, e_local, hidden, intermediate):
+        return 128
+
+    @staticmethod
+    def sort_align(ids, num_experts, e_begin=0, e_local=None, want_inv=False, want_offsets64=False,
+                   tile_rows=128):
         e_local = num_experts if e_local is None else e_local
         flat = ids.reshape(-1).long()
         loc = flat - e_begin
