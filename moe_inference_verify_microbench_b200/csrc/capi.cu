@@ -273,7 +273,7 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                  if (rc == kRcOk && lp.fuse_gather) {
                    rc = launch_w13_swiglu_gather(x, T, perm, top_k, R, tiles, num_tiles,
                                                  max_tiles, w_gate, w_up, E, H, I, h, status,
-                                                 stream, tile_rows);
+                                                 stream, tile_rows, small ? w_down : nullptr);
                  } else if (rc == kRcOk) {
                    rc = launch_gather_rows(x, T, perm, R, nullptr, top_k, H, sorted_x, status,
                                            stream);

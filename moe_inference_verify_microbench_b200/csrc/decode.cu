@@ -105,6 +105,20 @@ __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouter
   int* sort_sm = reinterpret_cast<int*>(dyn + static_cast<size_t>(T) * vec_per_row);
   cg::cluster_group cluster = cg::this_cluster();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int per_cta = E / kRouterCluster;
+  // The router rows are weights, not outputs of an earlier kernel: the first
+  // expert row of each warp is loaded before waiting for the predecessor.
+  uint4 wv[kRouterMaxVecPerLane];
+  auto load_row = [&](int el) {
+    const uint4* row =
+        wr + (static_cast<size_t>(cluster.block_rank()) * per_cta + el) * vec_per_row;
+#pragma unroll
+    for (int j = 0; j < kRouterMaxVecPerLane; ++j) {
+      const int v = lane + 32 * j;
+      wv[j] = v < vec_per_row ? __ldg(row + v) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  if (warp < per_cta) load_row(warp);
   pdl_wait();
   pdl_trigger();
   {
@@ -123,17 +137,10 @@ __global__ void __cluster_dims__(kRouterCluster, 1, 1) __launch_bounds__(kRouter
   __syncthreads();
 
   // Warp = one expert row held in registers; tokens one by one.
-  const int per_cta = E / kRouterCluster;
   float* dst = cluster.map_shared_rank(logits, 0);
   for (int el = warp; el < per_cta; el += kRouterWarps) {
     const int e = static_cast<int>(cluster.block_rank()) * per_cta + el;
-    const uint4* row = wr + static_cast<size_t>(e) * vec_per_row;
-    uint4 wv[kRouterMaxVecPerLane];
-#pragma unroll
-    for (int j = 0; j < kRouterMaxVecPerLane; ++j) {
-      const int v = lane + 32 * j;
-      wv[j] = v < vec_per_row ? __ldg(row + v) : make_uint4(0, 0, 0, 0);
-    }
+    if (el != warp) load_row(el);
     const float be = bias != nullptr ? bias[e] : 0.0f;
 #pragma unroll 1
     for (int t = 0; t < T; ++t) {
@@ -219,7 +226,15 @@ struct StreamArgs {
   int out_rows;
   int stages;
   int* status;
+  // Gate/up only: the down weights [E][next_N][next_K] of the same experts,
+  // prefetched into L2 once this CTA has issued its own copies, when the
+  // active experts' down weights fit comfortably in L2 (decode).
+  const __nv_bfloat16* next_w;
+  int next_N, next_K;
 };
+
+constexpr long long kPrefetchMaxBytes = 64ll << 20;  // half of the 126 MB L2
+constexpr int kPrefetchRows = 32;                    // down rows per prefetch request
 
 // One warp's pass over ROWS weight rows of a stage (row j at w + j * rstride,
 // in uint4 units) for n <= NR records whose A rows are act[rows[r]], over CH
@@ -460,6 +475,28 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
           ph ^= 1u;
         }
       }
+      if (SWIGLU && a.next_w != nullptr && !*abort_flag) {
+        // This CTA's share of the next GEMM's weights, in kPrefetchRows-row
+        // requests, so the down projection streams from L2.
+        const int nblk = a.next_N / kPrefetchRows;
+        const long long bytes_all =
+            static_cast<long long>(nt) * a.next_N * a.next_K * static_cast<long long>(2);
+        if (nblk > 0 && bytes_all <= kPrefetchMaxBytes) {
+          const long long total2 = static_cast<long long>(nt) * nblk;
+          const long long p_lo = total2 * blockIdx.x / gridDim.x;
+          const long long p_hi = total2 * (blockIdx.x + 1) / gridDim.x;
+          const uint32_t req = static_cast<uint32_t>(kPrefetchRows) * a.next_K * 2;
+          for (long long q = p_lo; q < p_hi; ++q) {
+            const int ti = static_cast<int>(q / nblk);
+            const int rb = static_cast<int>(q - static_cast<long long>(ti) * nblk);
+            const int e = a.tiles[ti].x;
+            if (e < 0 || e >= a.E) continue;
+            prefetch_l2_bulk(a.next_w + (static_cast<size_t>(e) * a.next_N +
+                                         static_cast<size_t>(rb) * kPrefetchRows) * a.next_K,
+                             req);
+          }
+        }
+      }
       if (*abort_flag) {
         // Let every copy still in flight land before the CTA exits.
         const uint32_t first = issued > static_cast<uint32_t>(a.stages) ? issued - a.stages : 0u;
@@ -611,7 +648,7 @@ static int launch_stream(StreamArgs a, cudaStream_t stream) {
 int launch_w13_gemv(const void* src, int src_rows, const int* index, int index_div, int M,
                     const int4* tiles, const int* num_tiles, int max_tiles, const void* w_gate,
                     const void* w_up, int E, int H, int I, void* h_out, int* status,
-                    cudaStream_t stream) {
+                    cudaStream_t stream, const void* w_down_prefetch) {
   if (!gemv_ok(I, H, true) || !aligned16(src) || !aligned16(w_gate) || !aligned16(w_up))
     return kRcUnsupported;
   if (M == 0 || max_tiles == 0) return kRcOk;
@@ -632,6 +669,11 @@ int launch_w13_gemv(const void* src, int src_rows, const int* index, int index_d
   a.out = static_cast<__nv_bfloat16*>(h_out);
   a.out_rows = M;
   a.status = status;
+  if (w_down_prefetch != nullptr && aligned16(w_down_prefetch) && (I % 8) == 0) {
+    a.next_w = static_cast<const __nv_bfloat16*>(w_down_prefetch);
+    a.next_N = H;  // down weights are [E][H][I]
+    a.next_K = I;
+  }
   return launch_stream<true>(a, stream);
 }
 

@@ -257,7 +257,8 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
 int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, int index_div,
                              int M, const int4* tiles, const int* num_tiles, int max_tiles,
                              const void* w_gate, const void* w_up, int E, int H, int I,
-                             void* h_out, int* status, cudaStream_t stream, int tile_rows) {
+                             void* h_out, int* status, cudaStream_t stream, int tile_rows,
+                             const void* w_down_prefetch) {
   if (src == nullptr || tiles == nullptr || num_tiles == nullptr || w_gate == nullptr ||
       w_up == nullptr || h_out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 ||
       max_tiles < 0 || src_rows < 0 || index_div <= 0)
@@ -267,7 +268,7 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
   if (src_rows == 0) return kRcBadArgument;  // rows to gather, but nothing to gather from
   if (use_gemv_w13(M) && gemv_ok(I, H, true))
     return launch_w13_gemv(src, src_rows, index, index_div, M, tiles, num_tiles, max_tiles,
-                           w_gate, w_up, E, H, I, h_out, status, stream);
+                           w_gate, w_up, E, H, I, h_out, status, stream, w_down_prefetch);
   if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   if (tile_rows == kPairTileRows) {
     if ((I % (kPairBN / 2)) != 0) return kRcUnsupported;

@@ -79,7 +79,8 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
 int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, int index_div,
                              int M, const int4* tiles, const int* num_tiles, int max_tiles,
                              const void* w_gate, const void* w_up, int E, int H, int I,
-                             void* h_out, int* status, cudaStream_t stream, int tile_rows = 128);
+                             void* h_out, int* status, cudaStream_t stream, int tile_rows = 128,
+                             const void* w_down_prefetch = nullptr);
 
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
@@ -120,10 +121,12 @@ int launch_router_sort_small(const void* x, const void* wr, const float* bias, i
                              int k, int norm_topk_prob, int* ids_out, float* w_out,
                              void* logits_out, int* counts, int* offsets, int* perm, int4* tiles,
                              int max_tiles, int* num_tiles, int* status, cudaStream_t stream);
+// w_down_prefetch (optional): the down weights [E][H][I] of the same experts,
+// prefetched into L2 behind the gate/up stream when they fit.
 int launch_w13_gemv(const void* src, int src_rows, const int* index, int index_div, int M,
                     const int4* tiles, const int* num_tiles, int max_tiles, const void* w_gate,
                     const void* w_up, int E, int H, int I, void* h_out, int* status,
-                    cudaStream_t stream);
+                    cudaStream_t stream, const void* w_down_prefetch = nullptr);
 int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
                    const void* w_down, int E, int H, int I, const int* row_map,
                    const float* row_scale, void* out, int out_rows, int* status,

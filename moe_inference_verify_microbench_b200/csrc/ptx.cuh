@@ -152,6 +152,14 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       : "memory");
 }
 
+// Ask L2 to fetch `bytes` (multiple of 16, 16-byte aligned) of global memory
+// ahead of use; nothing is written to shared memory and nothing is awaited.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+               "r"(bytes)
+               : "memory");
+}
+
 // ---------------------------------------------------------------- cp.async (row gathers)
 
 // 16-byte global -> shared copy through L2 only; bytes past `src_bytes`

@@ -142,22 +142,44 @@ __global__ void __launch_bounds__(kRowsThreads) combine_rows_warp(
         src = -1;
       }
     }
-    for (int v0 = 0; v0 < vec_per_row; v0 += 32) {
-      const int v = v0 + lane;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int j = 0; j < k; ++j) {
-        const int sj = __shfl_sync(0xffffffffu, src, j);
-        const float wj = __shfl_sync(0xffffffffu, w, j);
-        if (sj >= 0 && v < vec_per_row)
-          acc_bf16x8(acc, __ldg(rows + static_cast<size_t>(sj) * vec_per_row + v), wj);
+    // The k source rows and weights, shuffled out once per token.
+    int sj[kCombineMaxK];
+    float wj[kCombineMaxK];
+#pragma unroll
+    for (int j = 0; j < kCombineMaxK; ++j) {
+      sj[j] = __shfl_sync(0xffffffffu, src, j);
+      wj[j] = __shfl_sync(0xffffffffu, w, j);
+      if (j >= k) sj[j] = -1;
+    }
+    // All k loads of a 16-byte column vector are issued before any is used,
+    // for two column vectors at a time: up to 16 loads in flight per lane.
+    for (int v0 = 0; v0 < vec_per_row; v0 += 64) {
+      uint4 val[2][kCombineMaxK];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int v = v0 + 32 * c + lane;
+#pragma unroll
+        for (int j = 0; j < kCombineMaxK; ++j) {
+          val[c][j] = make_uint4(0, 0, 0, 0);
+          if (sj[j] >= 0 && v < vec_per_row)
+            val[c][j] = __ldg(rows + static_cast<size_t>(sj[j]) * vec_per_row + v);
+        }
       }
-      if (v < vec_per_row) {
-        uint4 o;
-        o.x = pack_bf16x2(acc[0], acc[1]);
-        o.y = pack_bf16x2(acc[2], acc[3]);
-        o.z = pack_bf16x2(acc[4], acc[5]);
-        o.w = pack_bf16x2(acc[6], acc[7]);
-        y[static_cast<size_t>(n) * vec_per_row + v] = o;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int v = v0 + 32 * c + lane;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < kCombineMaxK; ++j)  // slot order, as the reference sums
+          if (sj[j] >= 0) acc_bf16x8(acc, val[c][j], wj[j]);
+        if (v < vec_per_row) {
+          uint4 o;
+          o.x = pack_bf16x2(acc[0], acc[1]);
+          o.y = pack_bf16x2(acc[2], acc[3]);
+          o.z = pack_bf16x2(acc[4], acc[5]);
+          o.w = pack_bf16x2(acc[6], acc[7]);
+          y[static_cast<size_t>(n) * vec_per_row + v] = o;
+        }
       }
     }
   }
