@@ -7,7 +7,8 @@
 // repeat_interleave).
 //
 // Three launches over R = T*k routing records (flat slot index s = n*k + j;
-// one launch, sa_small, when R <= 2048 and E_local <= 256):
+// one launch when E_local <= 256 and R <= 2048 (sa_small, one CTA) or
+// R <= 32768 (sa_cluster, a cluster of up to 8 CTAs)):
 //   1. sa_hist     per-CTA expert histograms of a contiguous record chunk
 //   2. sa_scan     one CTA: per-expert counts, offsets[E+1], the per-CTA base of
 //                  every expert, and the 128-row tile table
@@ -21,6 +22,8 @@
 // expert-parallel schedule (C6/python/solution.py:141-149).
 #include "internal.h"
 #include "sort_block.cuh"
+
+#include <cooperative_groups.h>
 
 namespace moe {
 
@@ -159,6 +162,101 @@ __global__ void __launch_bounds__(kSortThreads) sa_small(
                    tiles, max_tiles, num_tiles, status, sm);
 }
 
+// One-launch sort for mid-size batches: a cluster of up to kClusterSortMax
+// CTAs, CTA c owning records [c*chunk, (c+1)*chunk), chunk = R / 8 rounded
+// up to a multiple of the block (at most kClusterChunk records).  The
+// per-CTA histograms meet over distributed shared memory, every CTA scans
+// them (expert offsets and its own per-expert base), CTA 0 writes counts,
+// offsets and the tile table, and each CTA scatters its chunk as sa_scatter
+// does.  Same outputs, same stable order as the three-kernel path.
+constexpr int kClusterSortMax = 8;
+constexpr int kClusterChunk = 4096;
+
+__global__ void __launch_bounds__(kSortThreads) sa_cluster(
+    const int* __restrict__ ids, int R, int E, int e_begin, int E_local, int block_m,
+    int* __restrict__ counts, int* __restrict__ offsets, long long* __restrict__ offsets64,
+    int* __restrict__ perm, int* __restrict__ inv, int4* __restrict__ tiles, int max_tiles,
+    int* __restrict__ num_tiles, int chunk, int* status) {
+  namespace cg = cooperative_groups;
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ int sm[];
+  int* hist = sm;                 // [E_local] this CTA's histogram (read by the others)
+  int* base = sm + E_local;       // [E_local] next free position per expert
+  int* wcnt = sm + 2 * E_local;   // [8][E_local] per-warp counts of a round
+  __shared__ int warp_sums[32];
+  __shared__ int total;
+  constexpr int kWarps = kSortThreads / 32;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int c = static_cast<int>(cluster.block_rank());
+  const int nc = static_cast<int>(cluster.num_blocks());
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int e = tid; e < E_local; e += blockDim.x) {
+    hist[e] = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) wcnt[w * E_local + e] = 0;
+  }
+  __syncthreads();
+  const int chunk0 = c * chunk;
+  const int chunk1 = min(R, chunk0 + chunk);
+  for (int r = chunk0 + tid; r < chunk1; r += blockDim.x) {
+    const int e = local_expert(ids, r, E, e_begin, E_local, status);
+    if (e >= 0) atomicAdd(&hist[e], 1);
+  }
+  cluster.sync();  // every CTA's histogram is complete
+  int run = 0, before = 0;
+  if (tid < E_local) {
+    for (int q = 0; q < nc; ++q) {
+      const int h = cluster.map_shared_rank(hist, q)[tid];
+      if (q < c) before += h;
+      run += h;
+    }
+  }
+  const int off = block_exclusive_scan(tid < E_local ? run : 0, warp_sums, &total);
+  if (tid < E_local) base[tid] = off + before;
+  if (c == 0) {
+    if (tid < E_local) {
+      counts[tid] = run;
+      offsets[tid] = off;
+      if (offsets64 != nullptr) offsets64[tid] = off;
+    }
+    if (tid == 0) {
+      offsets[E_local] = total;
+      if (offsets64 != nullptr) offsets64[E_local] = total;
+    }
+    write_tiles(tid, E_local, run, off, block_m, tiles, max_tiles, num_tiles, warp_sums, &total);
+  }
+  cluster.sync();  // no CTA reads another's histogram after this point
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int r0 = chunk0; r0 < chunk1; r0 += kSortThreads) {
+    const int r = r0 + tid;
+    const int e = r < chunk1 ? local_expert(ids, r, E, e_begin, E_local, status) : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & lt_mask);
+    if (e >= 0 && rank == 0) wcnt[warp * E_local + e] = __popc(peers);
+    __syncthreads();
+    if (e >= 0) {
+      int p = base[e] + rank;
+      for (int w = 0; w < warp; ++w) p += wcnt[w * E_local + e];
+      perm[p] = r;
+      if (inv != nullptr) inv[r] = p;
+    } else if (r < chunk1 && inv != nullptr) {
+      inv[r] = -1;
+    }
+    __syncthreads();
+    for (int x = tid; x < E_local; x += blockDim.x) {
+      int add = 0;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        add += wcnt[w * E_local + x];
+        wcnt[w * E_local + x] = 0;
+      }
+      base[x] += add;
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void __launch_bounds__(1024) tiles_from_offsets(const long long* __restrict__ offsets,
                                                            int E, int block_m,
                                                            int4* __restrict__ tiles, int max_tiles,
@@ -195,6 +293,17 @@ int launch_sort_align(const int* ids, int R, int E, int e_begin, int E_local, in
     const cudaError_t e = launch_pdl(sa_small, dim3(1), dim3(kSortThreads), sh, stream, ids, R, E,
                                      e_begin, E_local, block_m, counts, offsets, offsets64, perm,
                                      inv, tiles, max_tiles, num_tiles, status);
+    return e == cudaSuccess ? kRcOk : kRcCudaError;
+  }
+  int chunk = (R + kClusterSortMax - 1) / kClusterSortMax;
+  chunk = (chunk + kSortThreads - 1) / kSortThreads * kSortThreads;
+  const int nclu = (R + chunk - 1) / chunk;
+  if (chunk <= kClusterChunk && E_local <= kSortThreads) {
+    const size_t sh = static_cast<size_t>(E_local) * (2 + kSortThreads / 32) * sizeof(int);
+    const cudaError_t e = launch_pdl_cluster(
+        sa_cluster, dim3(nclu), dim3(kSortThreads), sh, stream, static_cast<unsigned>(nclu), ids,
+        R, E, e_begin, E_local, block_m, counts, offsets, offsets64, perm, inv, tiles, max_tiles,
+        num_tiles, chunk, status);
     return e == cudaSuccess ? kRcOk : kRcCudaError;
   }
   int* hist = static_cast<int*>(workspace);
