@@ -234,6 +234,25 @@ MOE_API int moe_grouped_w2_rows(const void* h, int M, const int32_t* tiles,
                                 void* out, int out_rows, int tile_rows, int32_t* status,
                                 cudaStream_t stream);
 
+/*
+ * Send plan of the all_to_all expert-parallel schedule (C7/python/solution.py:
+ * 150-203), which here dispatches one row per (token, owner rank):
+ *   moe_ep_keys: keys[n*ep + r] = r if one of ids[n, 0..k) lies in rank r's
+ *     experts [r*experts_per_rank, (r+1)*experts_per_rank), else ep; a stable
+ *     moe_sort_align of the keys (E = ep + 1, E_local = ep) gives per-rank
+ *     send counts and the rank-major send order perm (pair = n*ep + r).
+ *   moe_ep_meta: for send row i < min(max_rows, *count), the int32 row
+ *     meta[i, 0..2k) = k local expert ids on r (experts_per_rank where expert
+ *     j of token n is not on r) and the k matching weights bit-cast (0 where
+ *     not on r), the metadata that travels with the row.
+ */
+MOE_API int moe_ep_keys(const int32_t* ids, int N, int k, int experts_per_rank, int ep,
+                        int32_t* keys, int32_t* status, cudaStream_t stream);
+MOE_API int moe_ep_meta(const int32_t* perm, const int32_t* count, int max_rows,
+                        const int32_t* ids, const float* weights, int N, int k,
+                        int experts_per_rank, int ep, int32_t* meta, int32_t* status,
+                        cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -56,6 +56,9 @@ SIGNATURES: dict[str, tuple] = {
                                                     _c_int, _ptr, _c_int, _ptr, _ptr]),
     "moe_grouped_w2_rows": (_c_int, [_ptr, _c_int, _ptr, _ptr, _c_int, _ptr, _c_int, _c_int,
                                      _c_int, _ptr, _ptr, _ptr, _c_int, _c_int, _ptr, _ptr]),
+    "moe_ep_keys": (_c_int, [_ptr, _c_int, _c_int, _c_int, _c_int, _ptr, _ptr, _ptr]),
+    "moe_ep_meta": (_c_int, [_ptr, _ptr, _c_int, _ptr, _ptr, _c_int, _c_int, _c_int, _c_int,
+                             _ptr, _ptr, _ptr]),
 }
 
 ABI_VERSION = 2

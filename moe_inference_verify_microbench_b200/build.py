@@ -19,7 +19,8 @@ PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libmoe_b200.so")
-SOURCES = ["capi.cu", "gemm.cu", "sort_align.cu", "rows.cu", "sort_align_static.cu", "decode.cu"]
+SOURCES = ["capi.cu", "gemm.cu", "sort_align.cu", "rows.cu", "sort_align_static.cu", "decode.cu",
+           "ep_plan.cu"]
 HEADERS = ["ptx.cuh", "grouped_gemm.cuh", "internal.h", "sort_block.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + [

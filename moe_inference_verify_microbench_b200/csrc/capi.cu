@@ -229,6 +229,22 @@ size_t moe_layer_workspace_bytes(int T, int H, int I, int E, int top_k) {
   return layer_layout(T, H, I, E, top_k, nullptr, [](auto&&...) {});
 }
 
+int moe_ep_keys(const int32_t* ids, int N, int k, int experts_per_rank, int ep, int32_t* keys,
+                int32_t* status, cudaStream_t stream) {
+  if (N > 0 && (ids == nullptr || keys == nullptr)) return kRcBadArgument;
+  return launch_ep_keys(ids, N, k, experts_per_rank, ep, keys, status, stream);
+}
+
+int moe_ep_meta(const int32_t* perm, const int32_t* count, int max_rows, const int32_t* ids,
+                const float* weights, int N, int k, int experts_per_rank, int ep, int32_t* meta,
+                int32_t* status, cudaStream_t stream) {
+  if (max_rows > 0 && (perm == nullptr || count == nullptr || ids == nullptr ||
+                       weights == nullptr || meta == nullptr))
+    return kRcBadArgument;
+  return launch_ep_meta(perm, count, max_rows, ids, weights, N, k, experts_per_rank, ep, meta,
+                        status, stream);
+}
+
 int moe_layer_tile_rows(int T, int H, int I, int E, int top_k) {
   if (T < 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0) return 0;
   return layer_path(static_cast<long long>(T) * top_k, H, I, E).tile_rows;

@@ -132,6 +132,12 @@ int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles
                    const float* row_scale, void* out, int out_rows, int* status,
                    cudaStream_t stream);
 
+// Expert-parallel send plan (ep_plan.cu).
+int launch_ep_keys(const int* ids, int N, int k, int epr, int ep, int* keys, int* status,
+                   cudaStream_t stream);
+int launch_ep_meta(const int* perm, const int* count, int max_rows, const int* ids, const float* w,
+                   int N, int k, int epr, int ep, int* meta, int* status, cudaStream_t stream);
+
 inline int max_tiles_bound(long long R, int E, int block_m) {
   return static_cast<int>((R + block_m - 1) / block_m + E);
 }

@@ -35,6 +35,8 @@ class CudaKernels:
 
     router_topk = staticmethod(ops.router_topk)
     sort_align = staticmethod(ops.sort_align)
+    ep_keys = staticmethod(ops.ep_keys)
+    ep_meta = staticmethod(ops.ep_meta)
     gather_rows = staticmethod(ops.gather_rows)
     combine = staticmethod(ops.combine)
 
@@ -148,33 +150,25 @@ def dispatch_combine(mod: _EPBase, local_x: torch.Tensor, group) -> torch.Tensor
     """
     K = mod._kernels
     N, k, E, epr, ep = local_x.shape[0], mod.top_k, mod.num_experts, mod.experts_per_rank, mod.ep_size
-    dev = local_x.device
     ids, w = mod._route(local_x)                                       # local router (C7:141-146)
     # Send plan: key each (token n, rank r) pair with r if one of n's experts lives
     # on r, else the sentinel ep; a stable sort by key gives the per-rank counts,
     # the send order (rank-major, token order inside) and each pair's position.
-    dest = ids.long() // epr                                           # owner of each record
-    sent = torch.zeros((N, ep), dtype=torch.bool, device=dev)
-    sent.scatter_(1, dest, True)
-    ranks = torch.arange(ep, dtype=torch.int32, device=dev)
-    keys = torch.where(sent, ranks, torch.full_like(ranks, ep))
+    keys = K.ep_keys(ids, epr, ep)
     plan = K.sort_align(keys, ep + 1, 0, ep, want_inv=True)
     send = plan.counts.to(torch.int64)                                 # rows per destination
     recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send, group=group)                   # count exchange (C7:190)
     send_l, recv_l = send.tolist(), recv.tolist()                     # host sync (C7:199-200)
     total = int(sum(send_l))
-    pair = plan.perm[:total].long()                                    # n * ep + r per send row
-    tok = pair // ep
-    rank_of = pair - tok * ep
-    own = dest.index_select(0, tok) == rank_of[:, None]
-    meta_e = torch.where(own, ids.index_select(0, tok) - (rank_of * epr)[:, None].to(torch.int32),
-                         torch.full_like(ids[:1], epr)).to(torch.int32)
-    meta_w = w.index_select(0, tok) * own
+    # Per send row (pair n*ep + r): the k local expert ids on r and their
+    # weights, one int32 row of 2k entries (weights bit-cast) (C7:203).
+    meta = K.ep_meta(plan.perm, plan.offsets[ep:], total, ids, w, epr, ep)
     xs = K.gather_rows(local_x, plan.perm, ep, count=plan.offsets[ep:])[:total]
     recv_x = all_to_all_variable(xs, send_l, recv_l, group)           # dispatch (C7:201)
-    recv_e = all_to_all_variable(meta_e, send_l, recv_l, group)       # (C7:203)
-    recv_w = all_to_all_variable(meta_w, send_l, recv_l, group)
+    recv_m = all_to_all_variable(meta, send_l, recv_l, group)
+    recv_e = recv_m[:, :k].contiguous()
+    recv_w = recv_m[:, k:].contiguous().view(torch.float32)
     n_recv = recv_x.shape[0]
     wg, wu, wd = mod.pack()
     if n_recv > 0:

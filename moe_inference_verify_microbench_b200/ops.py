@@ -288,6 +288,37 @@ def grouped_w2(h: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor, ma
     return out
 
 
+# --------------------------------------------------------------------------- EP send plan
+
+
+def ep_keys(ids: torch.Tensor, experts_per_rank: int, ep: int) -> torch.Tensor:
+    """keys[n, r] = r if one of token n's experts lives on rank r, else ep
+    (the send plan of the one-row-per-owner all_to_all dispatch)."""
+    _need(ids, "ids", torch.int32, 2)
+    N, k = ids.shape
+    keys = torch.empty((N, ep), dtype=torch.int32, device=ids.device)
+    _rc(_native.load().moe_ep_keys(_p(ids), N, k, experts_per_rank, ep, _p(keys),
+                                   _p(status_word(ids.device)), _stream(ids.device)), "moe_ep_keys")
+    return keys
+
+
+def ep_meta(perm: torch.Tensor, count: torch.Tensor, max_rows: int, ids: torch.Tensor,
+            w: torch.Tensor, experts_per_rank: int, ep: int) -> torch.Tensor:
+    """Per send row i (pair perm[i] = n*ep + r): int32 [2k] row of token n's
+    local expert ids on rank r (experts_per_rank where not on r) and the
+    matching weights bit-cast (0 where not on r)."""
+    _need(perm, "perm", torch.int32)
+    _need(count, "count", torch.int32)
+    _need(ids, "ids", torch.int32, 2)
+    _need(w, "w", torch.float32, 2)
+    N, k = ids.shape
+    meta = torch.empty((max_rows, 2 * k), dtype=torch.int32, device=ids.device)
+    _rc(_native.load().moe_ep_meta(_p(perm), _p(count), max_rows, _p(ids), _p(w), N, k,
+                                   experts_per_rank, ep, _p(meta), _p(status_word(ids.device)),
+                                   _stream(ids.device)), "moe_ep_meta")
+    return meta
+
+
 # --------------------------------------------------------------------------- whole layer
 
 

@@ -51,6 +51,25 @@ class CpuContractKernels:
                           None, torch.tensor([0]), 0)
 
     @staticmethod
+    def ep_keys(ids, epr, ep):
+        dest = ids.long() // epr
+        sent = torch.zeros((ids.shape[0], ep), dtype=torch.bool)
+        sent.scatter_(1, dest, True)
+        ranks = torch.arange(ep, dtype=torch.int32)
+        return torch.where(sent, ranks, torch.full_like(ranks, ep))
+
+    @staticmethod
+    def ep_meta(perm, count, max_rows, ids, w, epr, ep):
+        pair = perm[:max_rows].long()
+        tok = pair // ep
+        rank_of = pair - tok * ep
+        own = ids.index_select(0, tok).long() // epr == rank_of[:, None]
+        meta_e = torch.where(own, ids.index_select(0, tok) - (rank_of * epr)[:, None].to(torch.int32),
+                             torch.full_like(ids[:1], epr)).to(torch.int32)
+        meta_w = w.index_select(0, tok) * own
+        return torch.cat([meta_e, meta_w.contiguous().view(torch.int32)], dim=1)
+
+    @staticmethod
     def gather_rows(src, index, index_div=1, count=None, out=None):
         n = index.numel() if count is None else min(index.numel(), int(count.reshape(-1)[0]))
         dst = torch.zeros((index.numel(), src.shape[1]), dtype=src.dtype)

@@ -329,3 +329,34 @@ def test_layer_decode_equals_op_by_op(cuda, T, k, E):
     y2 = ops.combine(sl, T, k)
     ops.check_status(cuda)
     assert torch.equal(y, y2)
+
+
+# ----------------------------------------------------------------------------- EP send plan
+
+
+@pytest.mark.parametrize("N,k,E,ep", [(1000, 8, 128, 2), (4096, 8, 128, 8), (77, 4, 16, 4)])
+def test_ep_plan_kernels_match_torch(cuda, N, k, E, ep):
+    """moe_ep_keys / moe_ep_meta equal their torch formulation, bit for bit."""
+    g = torch.Generator(device=cuda)
+    g.manual_seed(N + ep)
+    scores = torch.rand(N, E, generator=g, device=cuda)
+    ids = scores.topk(k, dim=1).indices.to(torch.int32)      # distinct experts per token
+    w = torch.softmax(torch.rand(N, k, generator=g, device=cuda), dim=1)
+    epr = E // ep
+    keys = ops.ep_keys(ids, epr, ep)
+    dest = ids.long() // epr
+    sent = torch.zeros((N, ep), dtype=torch.bool, device=cuda)
+    sent.scatter_(1, dest, True)
+    ranks = torch.arange(ep, dtype=torch.int32, device=cuda)
+    assert torch.equal(keys, torch.where(sent, ranks, torch.full_like(ranks, ep)))
+    plan = ops.sort_align(keys, ep + 1, 0, ep, want_inv=True)
+    total = int(plan.offsets[ep].item())
+    meta = ops.ep_meta(plan.perm, plan.offsets[ep:], total, ids, w, epr, ep)
+    ops.check_status(cuda)
+    pair = plan.perm[:total].long()
+    tok, rank_of = pair // ep, pair % ep
+    own = dest.index_select(0, tok) == rank_of[:, None]
+    meta_e = torch.where(own, ids.index_select(0, tok) - (rank_of * epr)[:, None].to(torch.int32),
+                         torch.full_like(ids[:1], epr)).to(torch.int32)
+    meta_w = (w.index_select(0, tok) * own).contiguous().view(torch.int32)
+    assert torch.equal(meta, torch.cat([meta_e, meta_w], dim=1))
