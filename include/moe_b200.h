@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define MOE_B200_ABI_VERSION 2
+#define MOE_B200_ABI_VERSION 3
 
 #define MOE_RC_OK 0
 #define MOE_RC_BAD_ARGUMENT (-1)
@@ -43,6 +43,15 @@ extern "C" {
 #define MOE_RC_CUDA_ERROR (-3)
 #define MOE_RC_TENSOR_MAP (-4)
 #define MOE_RC_WORKSPACE (-5)
+
+/* Device status codes (first failure wins). */
+#define MOE_ERR_TIMEOUT_FULL 0x101
+#define MOE_ERR_TIMEOUT_EMPTY 0x102
+#define MOE_ERR_TIMEOUT_ACC_FULL 0x103
+#define MOE_ERR_TIMEOUT_ACC_EMPTY 0x104
+#define MOE_ERR_PEER_TIMEOUT 0x105
+#define MOE_ERR_BAD_EXPERT 0x201
+#define MOE_ERR_BAD_ROW 0x202
 
 /* Rows per M-tile of the grouped GEMMs (the C9 BLOCK_M), and the taller
  * tile of the 2-CTA cluster-pair GEMMs that large batches use (ABI 2). */
@@ -252,6 +261,55 @@ MOE_API int moe_ep_meta(const int32_t* perm, const int32_t* count, int max_rows,
                         const int32_t* ids, const float* weights, int N, int k,
                         int experts_per_rank, int ep, int32_t* meta, int32_t* status,
                         cudaStream_t stream);
+
+/*
+ * Peer-store exchange of the all_to_all expert-parallel schedule (replaces the
+ * count all_to_all + host .tolist() + dispatch and combine all_to_alls of
+ * C7/python/solution.py:186-261 and C8/python/solution.py:171-224) over NVLink
+ * with device-resident split sizes.  Every rank of the group allocates one
+ * peer buffer of moe_ep_peer_buffer_bytes(ep, cap_rows, H, k) bytes with
+ * moe_ep_peer_alloc (zeroed; 64-byte CUDA IPC handle out), exchanges the
+ * handles, and maps every other rank's buffer with moe_ep_peer_open;
+ * buffers[q] is rank q's buffer in this process (buffers[rank] its own).
+ * cap_rows bounds both the rows a rank sends and the rows it receives
+ * (ep x the largest per-rank token count); every rank passes the same
+ * ep, cap_rows, H and k.  The ranks must run on distinct GPUs.
+ *
+ * Regions of a buffer (moe_ep_peer_region_offset, region =):
+ *   0 recv_ids  int32 [cap_rows, k]  expert ids of received rows, localised
+ *                                    (experts_per_rank: not this rank's)
+ *   1 recv_w    fp32  [cap_rows, k]  their weights (0 where not this rank's)
+ *   2 recv_rows bf16  [cap_rows, H]  received token rows, source-major
+ *   3 ret_rows  bf16  [cap_rows, H]  returned partial rows in send order
+ *
+ * moe_ep_peer_dispatch (one forward's first half; all ranks, same order):
+ *   send_counts[d] rows for rank d (d < ep) in the rank-major send order
+ *   perm[i] = n*ep + d (moe_ep_keys + moe_sort_align); x [N, H] bf16;
+ *   ids [N, k] global expert ids, weights [N, k].  On return (stream order)
+ *   recv_ids/recv_w/recv_rows hold this rank's received rows and recv_ids
+ *   rows past them hold the sentinel experts_per_rank.
+ * moe_ep_peer_return (second half): out [out_rows, H] bf16 holds the expert
+ *   output of record p of the received rows at row inv[p] (inv < 0: none);
+ *   every received row's weighted record sum goes back to its source, whose
+ *   ret_rows then hold one partial row per send position.
+ * A peer that does not signal within the wait limit (10 s; ms <= 0 restores
+ * it) records MOE_ERR_PEER_TIMEOUT (0x105) in *status; the kernels still end.
+ * The limit is read when a dispatch or return is enqueued.
+ */
+MOE_API void moe_ep_peer_set_wait_limit_ms(int ms);
+MOE_API size_t moe_ep_peer_buffer_bytes(int ep, int cap_rows, int H, int k);
+MOE_API size_t moe_ep_peer_region_offset(int ep, int cap_rows, int H, int k, int region);
+MOE_API int moe_ep_peer_alloc(size_t bytes, void** buffer, void* ipc_handle);
+MOE_API int moe_ep_peer_open(const void* ipc_handle, void** buffer);
+MOE_API int moe_ep_peer_close(void* buffer);
+MOE_API int moe_ep_peer_free(void* buffer);
+MOE_API int moe_ep_peer_dispatch(void* const* buffers, int ep, int rank, int cap_rows, int H,
+                                 int k, const int32_t* send_counts, const void* x, int N,
+                                 const int32_t* perm, const int32_t* ids, const float* weights,
+                                 int experts_per_rank, int32_t* status, cudaStream_t stream);
+MOE_API int moe_ep_peer_return(void* const* buffers, int ep, int rank, int cap_rows, int H, int k,
+                               const void* out, int out_rows, const int32_t* inv,
+                               int32_t* status, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -59,9 +59,21 @@ SIGNATURES: dict[str, tuple] = {
     "moe_ep_keys": (_c_int, [_ptr, _c_int, _c_int, _c_int, _c_int, _ptr, _ptr, _ptr]),
     "moe_ep_meta": (_c_int, [_ptr, _ptr, _c_int, _ptr, _ptr, _c_int, _c_int, _c_int, _c_int,
                              _ptr, _ptr, _ptr]),
+    # ABI 3: peer-store expert-parallel exchange
+    "moe_ep_peer_buffer_bytes": (_c_size, [_c_int, _c_int, _c_int, _c_int]),
+    "moe_ep_peer_region_offset": (_c_size, [_c_int, _c_int, _c_int, _c_int, _c_int]),
+    "moe_ep_peer_set_wait_limit_ms": (None, [_c_int]),
+    "moe_ep_peer_alloc": (_c_int, [_c_size, _ptr, _ptr]),
+    "moe_ep_peer_open": (_c_int, [_ptr, _ptr]),
+    "moe_ep_peer_close": (_c_int, [_ptr]),
+    "moe_ep_peer_free": (_c_int, [_ptr]),
+    "moe_ep_peer_dispatch": (_c_int, [_ptr, _c_int, _c_int, _c_int, _c_int, _c_int, _ptr, _ptr,
+                                      _c_int, _ptr, _ptr, _ptr, _c_int, _ptr, _ptr]),
+    "moe_ep_peer_return": (_c_int, [_ptr, _c_int, _c_int, _c_int, _c_int, _c_int, _ptr, _c_int,
+                                    _ptr, _ptr, _ptr]),
 }
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

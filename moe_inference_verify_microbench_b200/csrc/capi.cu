@@ -92,6 +92,7 @@ const char* moe_error_string(int code) {
     case kErrTimeoutEmpty: return "device: TMA producer timed out waiting for a free stage";
     case kErrTimeoutAccFull: return "device: epilogue timed out waiting for the accumulator";
     case kErrTimeoutAccEmpty: return "device: MMA warp timed out waiting for the epilogue";
+    case kErrPeerTimeout: return "device: timed out waiting for a peer rank of the expert-parallel group";
     case kErrBadExpert: return "device: expert id out of range";
     case kErrBadRow: return "device: row index out of range";
     default: return "unknown code";
@@ -243,6 +244,45 @@ int moe_ep_meta(const int32_t* perm, const int32_t* count, int max_rows, const i
     return kRcBadArgument;
   return launch_ep_meta(perm, count, max_rows, ids, weights, N, k, experts_per_rank, ep, meta,
                         status, stream);
+}
+
+size_t moe_ep_peer_buffer_bytes(int ep, int cap_rows, int H, int k) {
+  if (ep < 1 || ep > kMaxEpRanks || cap_rows < 0 || H <= 0 || k < 1) return 0;
+  return peer_buffer_bytes(ep, cap_rows, H, k);
+}
+
+size_t moe_ep_peer_region_offset(int ep, int cap_rows, int H, int k, int region) {
+  if (ep < 1 || ep > kMaxEpRanks || cap_rows < 0 || H <= 0 || k < 1) return 0;
+  return peer_region_offset(ep, cap_rows, H, k, region);
+}
+
+void moe_ep_peer_set_wait_limit_ms(int ms) {
+  set_peer_wait_limit(ms > 0 ? static_cast<unsigned long long>(ms) * 1000000ull : 0ull);
+}
+
+int moe_ep_peer_alloc(size_t bytes, void** buffer, void* ipc_handle) {
+  return peer_alloc(bytes, buffer, ipc_handle);
+}
+
+int moe_ep_peer_open(const void* ipc_handle, void** buffer) { return peer_open(ipc_handle, buffer); }
+
+int moe_ep_peer_close(void* buffer) { return peer_close(buffer); }
+
+int moe_ep_peer_free(void* buffer) { return peer_free(buffer); }
+
+int moe_ep_peer_dispatch(void* const* buffers, int ep, int rank, int cap_rows, int H, int k,
+                         const int32_t* send_counts, const void* x, int N, const int32_t* perm,
+                         const int32_t* ids, const float* weights, int experts_per_rank,
+                         int32_t* status, cudaStream_t stream) {
+  return launch_ep_peer_dispatch(buffers, ep, rank, cap_rows, H, k, send_counts, x, N, perm, ids,
+                                 weights, experts_per_rank, status, stream);
+}
+
+int moe_ep_peer_return(void* const* buffers, int ep, int rank, int cap_rows, int H, int k,
+                       const void* out, int out_rows, const int32_t* inv, int32_t* status,
+                       cudaStream_t stream) {
+  return launch_ep_peer_return(buffers, ep, rank, cap_rows, H, k, out, out_rows, inv, status,
+                               stream);
 }
 
 int moe_layer_tile_rows(int T, int H, int I, int E, int top_k) {

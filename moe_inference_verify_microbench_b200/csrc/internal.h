@@ -138,6 +138,23 @@ int launch_ep_keys(const int* ids, int N, int k, int epr, int ep, int* keys, int
 int launch_ep_meta(const int* perm, const int* count, int max_rows, const int* ids, const float* w,
                    int N, int k, int epr, int ep, int* meta, int* status, cudaStream_t stream);
 
+// Peer-store expert-parallel exchange (ep_peer.cu).
+constexpr int kMaxEpRanks = 8;
+void set_peer_wait_limit(unsigned long long ns);
+size_t peer_buffer_bytes(int ep, int cap_rows, int H, int k);
+size_t peer_region_offset(int ep, int cap_rows, int H, int k, int region);
+int launch_ep_peer_dispatch(void* const* bases, int ep, int me, int cap_rows, int H, int k,
+                            const int* send_counts, const void* x, int N, const int* perm,
+                            const int* ids, const float* w, int experts_per_rank, int* status,
+                            cudaStream_t stream);
+int launch_ep_peer_return(void* const* bases, int ep, int me, int cap_rows, int H, int k,
+                          const void* out, int out_rows, const int* inv, int* status,
+                          cudaStream_t stream);
+int peer_alloc(size_t bytes, void** ptr, void* handle);
+int peer_open(const void* handle, void** ptr);
+int peer_close(void* ptr);
+int peer_free(void* ptr);
+
 inline int max_tiles_bound(long long R, int E, int block_m) {
   return static_cast<int>((R + block_m - 1) / block_m + E);
 }

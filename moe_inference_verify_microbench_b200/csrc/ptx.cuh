@@ -21,6 +21,7 @@ enum StatusCode : int {
   kErrTimeoutEmpty = 0x102,    // producer: smem stage never released
   kErrTimeoutAccFull = 0x103,  // epilogue: accumulator never committed
   kErrTimeoutAccEmpty = 0x104, // MMA warp: accumulator never drained
+  kErrPeerTimeout = 0x105,     // expert-parallel exchange: a peer rank never signalled
   kErrBadExpert = 0x201,       // an expert id outside [0, E)
   kErrBadRow = 0x202,          // a tile row range outside the A operand
 };

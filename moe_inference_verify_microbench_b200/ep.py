@@ -15,8 +15,11 @@ Experts are sharded contiguously: rank r owns [r*E/ep, (r+1)*E/ep)
 (C6:87-89, C7:96-98, C8:110-112).  Every rank issues the same collectives in
 the same order as the reference (C8:12-19), so the schedules compose with
 the reference's TP attention.  The local compute is the sm_100a kernel set of
-``ops``; the only host synchronisation is the split-size exchange that NCCL's
-variable all_to_all needs (the reference's ``.tolist()``, C7:199-200).
+``ops``.  With ``transport="nccl"`` (the default) the exchange is NCCL's
+variable all_to_all, whose split sizes the host must read (the reference's
+``.tolist()``, C7:199-200); with ``transport="peer"`` (C7 and C8) the ranks
+write into each other's buffers over NVLink with the split sizes negotiated on
+the device (``peer.PeerExchange``): no host synchronisation in the forward.
 """
 
 from __future__ import annotations
@@ -28,6 +31,9 @@ from torch import nn
 from . import ops
 from .dist_primer import all_to_all_variable
 from .experts import ExpertBank, SwiGLU_MLP, router_bias_of
+from .peer import PeerExchange, _all_gather
+
+TRANSPORTS = ("nccl", "peer")
 
 
 class CudaKernels:
@@ -184,34 +190,91 @@ def dispatch_combine(mod: _EPBase, local_x: torch.Tensor, group) -> torch.Tensor
     return K.combine(back, N, ep, slot_src=plan.inv)                  # sum over owner ranks (ep <= 8)
 
 
-class EPSparseMoEPure(_EPBase):
+def dispatch_combine_peer(mod: _EPBase, local_x: torch.Tensor, px: PeerExchange) -> torch.Tensor:
+    """``dispatch_combine`` over the peer-store exchange: the same send plan,
+    local compute and combines, with the three all_to_alls and the host read
+    of the split sizes replaced by device-signalled stores into the peers'
+    buffers.  The receive buffer has a fixed capacity; rows no source filled
+    carry the sentinel expert id, so the local sort leaves them out."""
+    K = mod._kernels
+    N, k, epr, ep = local_x.shape[0], mod.top_k, mod.experts_per_rank, mod.ep_size
+    ids, w = mod._route(local_x)                                       # local router (C7:141-146)
+    keys = K.ep_keys(ids, epr, ep)
+    plan = K.sort_align(keys, ep + 1, 0, ep, want_inv=True)
+    px.dispatch(plan.counts, local_x, plan.perm, ids, w, epr)        # counts + dispatch (C7:190-203)
+    rows = K.tile_rows(px.cap_rows * k // ep, epr, mod.hidden, mod.intermediate)
+    s2 = K.sort_align(px.recv_ids, epr + 1, 0, epr, want_inv=True,  # local re-sort (C7:224-226)
+                      tile_rows=rows)
+    wg, wu, wd = mod.pack()
+    out = K.expert_compute(px.recv_rows, s2.perm, k, s2, wg, wu, wd)
+    px.give_back(out, s2.inv)                                          # weighted row sums (C7:258-261)
+    return K.combine(px.ret_rows, N, ep, slot_src=plan.inv)           # sum over owner ranks
+
+
+class _A2ABase(_EPBase):
+    """Transport selection shared by the all_to_all schedules."""
+
+    def _init_transport(self, transport: str, max_tokens_per_rank: int | None) -> None:
+        if transport not in TRANSPORTS:
+            raise ValueError(f"transport must be one of {TRANSPORTS}, got {transport!r}")
+        self.transport = transport
+        self.max_tokens_per_rank = max_tokens_per_rank
+        self._peer: PeerExchange | None = None
+
+    def _exchange(self, local_x: torch.Tensor, group) -> torch.Tensor:
+        if self.transport == "nccl":
+            return dispatch_combine(self, local_x, group)
+        if self._peer is None:
+            # Collective, on the first forward of every rank: the capacity is
+            # ep x the largest per-rank token count, then the buffers are swapped.
+            n_max = self.max_tokens_per_rank
+            if n_max is None:
+                n_max = max(_all_gather(local_x.shape[0], group))
+            self._peer = PeerExchange(group, self.ep_size * int(n_max), self.hidden, self.top_k,
+                                      local_x.device)
+        return dispatch_combine_peer(self, local_x, self._peer)
+
+    def close(self) -> None:
+        """Collective with the peer transport: unmap and free the peer buffers."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
+
+
+class EPSparseMoEPure(_A2ABase):
     """Pure EP: distinct tokens per rank, dispatch/combine all_to_all
-    (C7/python/solution.py:65-269).  The group is kept as ``ep_group`` (C7:93)."""
+    (C7/python/solution.py:65-269).  The group is kept as ``ep_group`` (C7:93).
+    ``transport`` and ``max_tokens_per_rank`` are keyword extras (module
+    docstring); the reference's arguments keep their meaning."""
 
     def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int, ep_size: int,
                  ep_rank: int, group: dist.ProcessGroup | None = None,
-                 norm_topk_prob: bool = True) -> None:
+                 norm_topk_prob: bool = True, *, transport: str = "nccl",
+                 max_tokens_per_rank: int | None = None) -> None:
         super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
         self.ep_group = group
+        self._init_transport(transport, max_tokens_per_rank)
 
     def forward(self, local_x: torch.Tensor) -> torch.Tensor:
         shape = local_x.shape
         x_flat = local_x.reshape(-1, self.hidden).contiguous()
-        return dispatch_combine(self, x_flat, self.ep_group).reshape(shape)
+        return self._exchange(x_flat, self.ep_group).reshape(shape)
 
 
-class HybridMoE(_EPBase):
+class HybridMoE(_A2ABase):
     """TP-scoped stripe/all_gather + EP-scoped dispatch/combine
-    (C8/python/solution.py:59-230)."""
+    (C8/python/solution.py:59-230); ``transport`` as for ``EPSparseMoEPure``."""
 
     def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int, tp_size: int,
                  tp_rank: int, tp_group: dist.ProcessGroup | None, ep_size: int, ep_rank: int,
-                 ep_group: dist.ProcessGroup | None, norm_topk_prob: bool = True) -> None:
+                 ep_group: dist.ProcessGroup | None, norm_topk_prob: bool = True, *,
+                 transport: str = "nccl", max_tokens_per_rank: int | None = None) -> None:
         super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
         self.tp_size = tp_size
         self.tp_rank = tp_rank
         self.tp_group = tp_group
         self.ep_group = ep_group
+        self._init_transport(transport, max_tokens_per_rank)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
@@ -220,7 +283,7 @@ class HybridMoE(_EPBase):
         assert N_tp % self.tp_size == 0
         local_N = N_tp // self.tp_size
         local_x = x_flat[self.tp_rank * local_N:(self.tp_rank + 1) * local_N].contiguous()  # (C8:160)
-        local_y = dispatch_combine(self, local_x, self.ep_group)
+        local_y = self._exchange(local_x, self.ep_group)
         y_flat = torch.empty((N_tp, self.hidden), dtype=local_y.dtype, device=local_y.device)
         dist.all_gather_into_tensor(y_flat, local_y, group=self.tp_group)            # (C8:227)
         return y_flat.reshape(shape)

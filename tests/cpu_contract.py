@@ -109,3 +109,60 @@ class CpuContractKernels:
             valid &= (e >= e_range[0]) & (e < e_range[1])
         contrib = rows.float()[s.clamp(min=0)] * (w * valid)[:, None]
         return contrib.reshape(T, k, -1).sum(1).to(torch.bfloat16)
+
+
+class CpuPeerExchange:
+    """A torch-CPU model of ``peer.PeerExchange`` on gloo ranks: the buffer
+    contents the exchange kernels leave behind (receive rows source-major,
+    unfilled receive rows carrying the sentinel expert id, returned rows in
+    send order), moved with all_to_all instead of peer stores."""
+
+    def __init__(self, group, cap_rows, hidden, top_k):
+        import torch.distributed as dist
+        self.dist = dist
+        self.group = group
+        self.ep = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.cap_rows, self.hidden, self.top_k = cap_rows, hidden, top_k
+        self.recv_ids = torch.zeros((cap_rows, top_k), dtype=torch.int32)
+        self.recv_w = torch.zeros((cap_rows, top_k), dtype=torch.float32)
+        self.recv_rows = torch.zeros((cap_rows, hidden), dtype=torch.bfloat16)
+        self.ret_rows = torch.zeros((cap_rows, hidden), dtype=torch.bfloat16)
+
+    def _a2a(self, t, send, recv):
+        from moe_inference_verify_microbench_b200.dist_primer import all_to_all_variable
+        return all_to_all_variable(t, send, recv, self.group)
+
+    def dispatch(self, send_counts, x, perm, ids, weights, experts_per_rank):
+        ep, epr = self.ep, experts_per_rank
+        counts = send_counts[:ep].to(torch.int64).contiguous()
+        recv = torch.empty_like(counts)
+        self.dist.all_to_all_single(recv, counts, group=self.group)
+        self._send, self._recv = counts.tolist(), recv.tolist()
+        total = sum(self._send)
+        assert x.shape[0] * ep <= self.cap_rows and sum(self._recv) <= self.cap_rows
+        pairs = perm[:total].long()
+        n, d = pairs // ep, pairs % ep
+        e = ids[n].long()
+        own = (e // epr) == d[:, None]
+        loc = torch.where(own, e - d[:, None] * epr, torch.full_like(e, epr)).to(torch.int32)
+        wt = torch.where(own, weights[n], torch.zeros_like(weights[n]))
+        rx = self._a2a(x[n], self._send, self._recv)
+        nr = rx.shape[0]
+        self._nr = nr
+        self.recv_rows[:nr] = rx
+        self.recv_ids[:nr] = self._a2a(loc, self._send, self._recv)
+        self.recv_ids[nr:] = epr
+        self.recv_w[:nr] = self._a2a(wt, self._send, self._recv)
+
+    def give_back(self, out, inv):
+        nr, k = self._nr, self.top_k
+        slot = inv.reshape(-1)[:nr * k].long().reshape(nr, k)
+        valid = slot >= 0
+        contrib = out.float()[slot.clamp(min=0)] * (self.recv_w[:nr] * valid)[..., None]
+        part = contrib.sum(1).to(torch.bfloat16)
+        back = self._a2a(part, self._recv, self._send)
+        self.ret_rows[:back.shape[0]] = back
+
+    def close(self):
+        pass

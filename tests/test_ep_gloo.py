@@ -12,11 +12,11 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def _worker(rank, world, port, name, q):
+def _worker(rank, world, port, name, transport, q):
     sys.path.insert(0, HERE)
     sys.path.insert(0, os.path.dirname(HERE))
     import torch.distributed as dist
-    from cpu_contract import CpuContractKernels
+    from cpu_contract import CpuContractKernels, CpuPeerExchange
     from helpers import load_golden, to_t
     from moe_inference_verify_microbench_b200.ep_lean import EPSparseMoE as Lean
     from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
@@ -40,14 +40,17 @@ def _worker(rank, world, port, name, q):
             mod = Lean(H, I, E, k, world, rank, group=None)
             x = xall[:T]
         elif kind == "c7":
-            mod = Pure(H, I, E, k, world, rank, group=None)
+            mod = Pure(H, I, E, k, world, rank, group=None, transport=transport)
             x = xall[rank * T:(rank + 1) * T]
         else:
             groups = [dist.new_group(list(range(i * tp, (i + 1) * tp))) for i in range(world // tp)]
-            mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None)
+            mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None,
+                            transport=transport)
             x = xall[(rank // tp) * T:(rank // tp + 1) * T]
         mod = mod.to(torch.bfloat16)
         mod._kernels = CpuContractKernels
+        if transport == "peer":  # the exchange's buffer semantics, moved by gloo
+            mod._peer = CpuPeerExchange(None, world * x.shape[0], H, k)
         mod.weight_loader(wr, wg, wu, wd)
         if int(g["zipf"]):
             lin = torch.nn.Linear(H, E, bias=True).to(torch.bfloat16)
@@ -67,15 +70,18 @@ def _worker(rank, world, port, name, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("name,world", [("ep_c6_w2.npz", 2), ("ep_c6_w4.npz", 4),
-                                        ("ep_c7_w2.npz", 2), ("ep_c7_w4_zipf.npz", 4),
-                                        ("ep_c8_w4_tp2.npz", 4)])
-def test_ep_schedule_matches_reference(name, world):
+@pytest.mark.parametrize("name,world,transport", [
+    ("ep_c6_w2.npz", 2, "nccl"), ("ep_c6_w4.npz", 4, "nccl"), ("ep_c7_w2.npz", 2, "nccl"),
+    ("ep_c7_w4_zipf.npz", 4, "nccl"), ("ep_c8_w4_tp2.npz", 4, "nccl"),
+    ("ep_c7_w2.npz", 2, "peer"), ("ep_c7_w4_zipf.npz", 4, "peer"),
+    ("ep_c8_w4_tp2.npz", 4, "peer")])
+def test_ep_schedule_matches_reference(name, world, transport):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29700 + abs(hash(name)) % 200
-    procs = [ctx.Process(target=_worker, args=(r, world, port, name, q)) for r in range(world)]
+    port = 29500 + abs(hash((name, transport))) % 400
+    procs = [ctx.Process(target=_worker, args=(r, world, port, name, transport, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=240) for _ in procs]
@@ -85,3 +91,9 @@ def test_ep_schedule_matches_reference(name, world):
     for rank, err, tie in res:
         assert tie <= 0.2, (rank, tie)
         assert err <= 2e-2, (rank, err)
+
+
+def test_unknown_transport_is_refused():
+    from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE
+    with pytest.raises(ValueError):
+        EPSparseMoE(64, 32, 8, 2, 1, 0, group=None, transport="shm")

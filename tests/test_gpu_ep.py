@@ -31,7 +31,7 @@ def _init(rank, world, port):
     return dev
 
 
-def _fixture_worker(rank, world, port, name, q):
+def _fixture_worker(rank, world, port, name, transport, q):
     sys.path.insert(0, HERE)
     sys.path.insert(0, os.path.dirname(HERE))
     import torch.distributed as dist
@@ -58,11 +58,12 @@ def _fixture_worker(rank, world, port, name, q):
                 mod = Lean(H, I, E, k, world, rank, group=None)
                 x = xall[:T]
             elif kind == "c7":
-                mod = Pure(H, I, E, k, world, rank, group=None)
+                mod = Pure(H, I, E, k, world, rank, group=None, transport=transport)
                 x = xall[rank * T:(rank + 1) * T]
             else:
                 groups = [dist.new_group(list(range(i * tp, (i + 1) * tp))) for i in range(world // tp)]
-                mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None)
+                mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None,
+                                transport=transport)
                 x = xall[(rank // tp) * T:(rank // tp + 1) * T]
             mod = mod.to(torch.bfloat16)
         mod.weight_loader(wr, wg, wu, wd)
@@ -82,6 +83,8 @@ def _fixture_worker(rank, world, port, name, q):
         tie = (srt[:, k - 1] == srt[:, k]).cpu().numpy()
         yref = mo.f32_from_bf16_bits(g[f"y_rank{rank}"])
         q.put((rank, mo.rel_err(y.float().cpu().numpy()[~tie], yref[~tie]), float(tie.mean())))
+        if hasattr(mod, "close"):
+            mod.close()
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -101,12 +104,15 @@ def _spawn(target, world, args):
     return res
 
 
-@pytest.mark.parametrize("name,world", [("ep_c6_w2.npz", 2), ("ep_c7_w2.npz", 2),
-                                        ("ep_c6_w4.npz", 4), ("ep_c7_w4_zipf.npz", 4),
-                                        ("ep_c8_w4_tp2.npz", 4)])
-def test_ep_schedule_on_gpus_matches_reference(name, world):
+@pytest.mark.parametrize("name,world,transport", [
+    ("ep_c6_w2.npz", 2, "nccl"), ("ep_c7_w2.npz", 2, "nccl"), ("ep_c7_w2.npz", 2, "peer"),
+    ("ep_c6_w4.npz", 4, "nccl"), ("ep_c7_w4_zipf.npz", 4, "nccl"),
+    ("ep_c7_w4_zipf.npz", 4, "peer"), ("ep_c8_w4_tp2.npz", 4, "nccl"),
+    ("ep_c8_w4_tp2.npz", 4, "peer")])
+def test_ep_schedule_on_gpus_matches_reference(name, world, transport):
     _need(world)
-    res = _spawn(_fixture_worker, world, (29800 + world, name))
+    res = _spawn(_fixture_worker, world, (29800 + world + 10 * (transport == "peer"), name,
+                                          transport))
     for rank, err, tie in res:
         assert tie <= 0.2, (rank, tie)
         assert err <= 2e-2, (rank, err)
@@ -154,3 +160,53 @@ def test_ep_full_shapes_match_single_gpu_layer(kind):
     res = _spawn(_full_worker, world, (29900 + (kind == "c7"), kind))
     for rank, err in res:
         assert err <= 1e-2, (rank, err)
+
+
+def _peer_worker(rank, world, port, q):
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
+    from moe_inference_verify_microbench_b200 import ops
+    from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
+
+    dev = _init(rank, world, port)
+    try:
+        H, I, E, k, T = 2048, 768, 128, 8, 2048
+        g = torch.Generator(device=dev)
+        g.manual_seed(11)
+        wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wg = (torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wu = (torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        wd = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        mods = {}
+        for tr in ("nccl", "peer"):
+            with torch.device(dev):
+                mods[tr] = Pure(H, I, E, k, world, rank, group=None, transport=tr).to(torch.bfloat16)
+            mods[tr].weight_loader(wr, list(wg), list(wu), list(wd))
+        same = []
+        g.manual_seed(100 + rank)
+        with torch.no_grad():
+            for step in range(4):  # epochs; ragged token counts per step and rank
+                n = T - 97 * ((step + rank) % 3)
+                x = torch.randn(n, H, generator=g, device=dev).to(torch.bfloat16)
+                dist.barrier()
+                y_peer = mods["peer"](x)
+                y_nccl = mods["nccl"](x)
+                same.append(bool(torch.equal(y_peer, y_nccl)))
+        torch.cuda.synchronize()
+        ops.check_status(dev)
+        mods["peer"].close()
+        q.put((rank, same))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_peer_transport_bit_identical_to_nccl():
+    """The peer-store exchange and the NCCL all_to_alls sum the same rows in
+    the same order: outputs must be bit-identical, over several forwards
+    with different per-rank token counts."""
+    _need(2)
+    res = _spawn(_peer_worker, 2, (29950,))  # both transports pick the same tile height here
+    for rank, same in res:
+        assert all(same), (rank, same)
