@@ -519,6 +519,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
+                    help="N>1: peer-store exchange over NVLink, or NCCL all_to_alls")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--sweep", default="1,16,128,1024,4096",
                     help="comma-separated token counts for the graph-captured sweep ('' = none)")

@@ -1,6 +1,7 @@
 """Multi-GPU leg of ``bench.py``: the C7 expert-parallel schedule
-(``EPSparseMoE`` pure, all_to_all dispatch/combine over NCCL) with T tokens
-per rank and E/N experts per rank, one process per GPU (weak scaling).
+(``EPSparseMoE`` pure, all_to_all dispatch/combine; the peer-store exchange
+over NVLink by default, NCCL all_to_alls with ``--ep-transport nccl``) with T
+tokens per rank and E/N experts per rank, one process per GPU (weak scaling).
 
 Timing: W warm-up steps, then K steps bracketed by a barrier and a device
 synchronise on both sides, CUDA events on each rank's stream, the maximum
@@ -21,11 +22,12 @@ import torch.distributed as dist
 H, I, E, K_TOP = 2048, 768, 128, 8
 
 
-def _build(rank: int, world: int, dev: torch.device, T: int):
+def _build(rank: int, world: int, dev: torch.device, T: int, transport: str):
     from .ep_pure import EPSparseMoE
 
     with torch.device(dev):
-        mod = EPSparseMoE(H, I, E, K_TOP, world, rank, group=None).to(torch.bfloat16)
+        mod = EPSparseMoE(H, I, E, K_TOP, world, rank, group=None, transport=transport,
+                          max_tokens_per_rank=T).to(torch.bfloat16)
     wg, wu, wd = mod.pack()
     g = torch.Generator(device=dev)
     with torch.no_grad():
@@ -88,7 +90,8 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
     from . import ops
 
     T = args.tokens
-    mod, x = _build(rank, world, dev, T)
+    transport = getattr(args, "ep_transport", "nccl")
+    mod, x = _build(rank, world, dev, T, transport)
     stream = torch.cuda.current_stream(dev)
     with torch.no_grad():
         for _ in range(args.warmup):
@@ -111,6 +114,7 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
         ms_e2e = _timed(e2e_step, n_e2e, stream)
         clk = clocks.stop() if clocks is not None else None
         ops.check_status(dev)
+    mod.close()
     ms_step = ms / args.steps
     if rank != 0:
         return
@@ -131,14 +135,19 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded x~N(0,1) per rank, weights~N(0,0.02))",
-        "config": config_block(T, world),
-        "roofline": {"bound": "tensor", "kernel": "whole EP layer per rank (compute + NCCL)",
+        "config": {**config_block(T, world), "ep_transport": transport},
+        "roofline": {"bound": "tensor",
+                     "kernel": f"whole EP layer per rank (compute + {transport} exchange)",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                      "traffic": None, "peak_source": f"{src} bf16_tflops_sustained"},
         "e2e": {"value": world * T * n_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
-                "api": "EPSparseMoE.forward (C7 schedule)", "steps": n_e2e},
-        "gpu_launches": 12 * args.steps,
+                "api": f"EPSparseMoE.forward (C7 schedule, transport={transport})",
+                "steps": n_e2e},
+        # our kernels per forward: router, ep_keys, plan sort, local sort (3),
+        # w13, w2, combine + (nccl) ep_meta, gather, partial combine
+        #                   + (peer) publish, dispatch, recv wait, return, return wait
+        "gpu_launches": (14 if transport == "peer" else 12) * args.steps,
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)
