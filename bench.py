@@ -533,7 +533,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world > 1 or args.gpus > 1:
         from moe_inference_verify_microbench_b200.ep_bench import run_ep
-        run_ep(args, METRIC, config_block, ClockSampler, make_device_inputs)
+        run_ep(args, METRIC, config_block, ClockSampler)
         return
     run_ours_single(args)
 

@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(32) ep_recv_wait(const PeerArgs a) {
 // Received row i < n_recv: sum_j w[i, j] * out[inv[i*k + j]] in fp32, record
 // order (inv < 0: not one of this rank's experts), as bf16 into the source's
 // return buffer at the row's position in the source's send order.
-__global__ void __launch_bounds__(kPeerThreads, 4) ep_return(const PeerArgs a,
+__global__ void __launch_bounds__(kPeerThreads, 2) ep_return(const PeerArgs a,
                                                           const uint4* __restrict__ out,
                                                           int out_rows,
                                                           const int* __restrict__ inv) {
@@ -339,26 +339,38 @@ __global__ void __launch_bounds__(kPeerThreads, 4) ep_return(const PeerArgs a,
     }
     uint4* dst =
         reinterpret_cast<uint4*>(a.base[s] + a.L.ret_rows) + static_cast<size_t>(pos) * vec;
-    for (int v = lane; v < vec; v += 32) {
-      uint4 val[kPeerMaxK];
+    // Two column vectors per lane per pass: every record's loads of both are
+    // in flight before any is summed.
+    for (int v0 = 0; v0 < vec; v0 += 64) {
+      uint4 val[2][kPeerMaxK];
 #pragma unroll
-      for (int j = 0; j < kPeerMaxK; ++j)
-        val[j] = slot[j] >= 0 ? __ldg(out + static_cast<size_t>(slot[j]) * vec + v)
-                              : make_uint4(0u, 0u, 0u, 0u);
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int c = 0; c < 2; ++c) {
+        const int v = v0 + 32 * c + lane;
 #pragma unroll
-      for (int j = 0; j < kPeerMaxK; ++j) {
-        if (slot[j] < 0) continue;
-        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&val[j]);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float2 f = __bfloat1622float2(h2[q]);
-          acc[2 * q] = fmaf(wt[j], f.x, acc[2 * q]);
-          acc[2 * q + 1] = fmaf(wt[j], f.y, acc[2 * q + 1]);
-        }
+        for (int j = 0; j < kPeerMaxK; ++j)
+          val[c][j] = slot[j] >= 0 && v < vec
+                          ? __ldg(out + static_cast<size_t>(slot[j]) * vec + v)
+                          : make_uint4(0u, 0u, 0u, 0u);
       }
-      dst[v] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                          pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int v = v0 + 32 * c + lane;
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < kPeerMaxK; ++j) {  // record order
+          if (slot[j] < 0) continue;
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&val[c][j]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __bfloat1622float2(h2[q]);
+            acc[2 * q] = fmaf(wt[j], f.x, acc[2 * q]);
+            acc[2 * q + 1] = fmaf(wt[j], f.y, acc[2 * q + 1]);
+          }
+        }
+        if (v < vec)
+          dst[v] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                              pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+      }
     }
   }
   finish_and_signal(a, kFlagReturn, &st->ret_done, e);
@@ -391,9 +403,9 @@ static int make_args(PeerArgs* a, void* const* bases, int ep, int me, int cap_ro
   return kRcOk;
 }
 
-static int peer_grid(long long rows) {
+static int peer_grid(long long rows, int ctas_per_sm) {
   const long long want = (rows + kPeerWarps - 1) / kPeerWarps;
-  const long long cap = static_cast<long long>(device_sm_count()) * 4;
+  const long long cap = static_cast<long long>(device_sm_count()) * ctas_per_sm;
   return static_cast<int>(want < 1 ? 1 : (want < cap ? want : cap));
 }
 
@@ -432,7 +444,7 @@ int launch_ep_peer_dispatch(void* const* bases, int ep, int me, int cap_rows, in
   if (launch_pdl(ep_publish, dim3(1), dim3(kPeerThreads), 0, stream, a, send_counts) !=
       cudaSuccess)
     return kRcCudaError;
-  if (launch_pdl(ep_dispatch, dim3(peer_grid(cap_rows)), dim3(kPeerThreads), 0, stream, a,
+  if (launch_pdl(ep_dispatch, dim3(peer_grid(cap_rows, 4)), dim3(kPeerThreads), 0, stream, a,
                  static_cast<const uint4*>(x), N, perm, ids, w, experts_per_rank) != cudaSuccess)
     return kRcCudaError;
   if (launch_pdl(ep_recv_wait, dim3(1), dim3(32), 0, stream, a) != cudaSuccess)
@@ -449,7 +461,7 @@ int launch_ep_peer_return(void* const* bases, int ep, int me, int cap_rows, int 
   if (out_rows < 0 || (out_rows > 0 && out == nullptr) || (cap_rows > 0 && inv == nullptr) ||
       (reinterpret_cast<uintptr_t>(out) & 15u) != 0)
     return kRcBadArgument;
-  if (launch_pdl(ep_return, dim3(peer_grid(cap_rows)), dim3(kPeerThreads), 0, stream, a,
+  if (launch_pdl(ep_return, dim3(peer_grid(cap_rows, 2)), dim3(kPeerThreads), 0, stream, a,
                  static_cast<const uint4*>(out), out_rows, inv) != cudaSuccess)
     return kRcCudaError;
   if (launch_pdl(ep_ret_wait, dim3(1), dim3(32), 0, stream, a) != cudaSuccess)

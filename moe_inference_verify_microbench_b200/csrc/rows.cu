@@ -118,7 +118,10 @@ __global__ void __launch_bounds__(kRowsThreads) combine_rows(
 }
 
 // Large batches: one warp per token, each lane sums 16-byte vectors of the k
-// rows (plenty of warps in flight hide the per-warp load chain).
+// rows.  All loads of COLS column vectors are issued before any is used
+// (KMAX x COLS = 16 loads in flight per lane), so a small k (the per-owner
+// partial rows of the expert-parallel combine) still keeps 16 in flight.
+template <int KMAX, int COLS>
 __global__ void __launch_bounds__(kRowsThreads) combine_rows_warp(
     const uint4* __restrict__ rows, int n_rows, const int* __restrict__ slot_src,
     const float* __restrict__ slot_w, const int* __restrict__ ids, int e_begin, int e_end, int T,
@@ -143,34 +146,32 @@ __global__ void __launch_bounds__(kRowsThreads) combine_rows_warp(
       }
     }
     // The k source rows and weights, shuffled out once per token.
-    int sj[kCombineMaxK];
-    float wj[kCombineMaxK];
+    int sj[KMAX];
+    float wj[KMAX];
 #pragma unroll
-    for (int j = 0; j < kCombineMaxK; ++j) {
+    for (int j = 0; j < KMAX; ++j) {
       sj[j] = __shfl_sync(0xffffffffu, src, j);
       wj[j] = __shfl_sync(0xffffffffu, w, j);
       if (j >= k) sj[j] = -1;
     }
-    // All k loads of a 16-byte column vector are issued before any is used,
-    // for two column vectors at a time: up to 16 loads in flight per lane.
-    for (int v0 = 0; v0 < vec_per_row; v0 += 64) {
-      uint4 val[2][kCombineMaxK];
+    for (int v0 = 0; v0 < vec_per_row; v0 += 32 * COLS) {
+      uint4 val[COLS][KMAX];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < COLS; ++c) {
         const int v = v0 + 32 * c + lane;
 #pragma unroll
-        for (int j = 0; j < kCombineMaxK; ++j) {
+        for (int j = 0; j < KMAX; ++j) {
           val[c][j] = make_uint4(0, 0, 0, 0);
           if (sj[j] >= 0 && v < vec_per_row)
             val[c][j] = __ldg(rows + static_cast<size_t>(sj[j]) * vec_per_row + v);
         }
       }
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < COLS; ++c) {
         const int v = v0 + 32 * c + lane;
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < kCombineMaxK; ++j)  // slot order, as the reference sums
+        for (int j = 0; j < KMAX; ++j)  // slot order, as the reference sums
           if (sj[j] >= 0) acc_bf16x8(acc, val[c][j], wj[j]);
         if (v < vec_per_row) {
           uint4 o;
@@ -210,10 +211,12 @@ int launch_combine(const void* rows, int n_rows, const int* slot_src, const floa
   if (T < 0 || k <= 0 || k > kCombineMaxK || H <= 0 || (H % 8) != 0) return kRcBadArgument;
   if (T == 0) return kRcOk;
   if (T >= 1024) {
-    const cudaError_t e = launch_pdl(combine_rows_warp, dim3(rows_grid(T)), dim3(kRowsThreads), 0,
-                                     stream, static_cast<const uint4*>(rows), n_rows, slot_src,
-                                     slot_w, ids, e_begin, e_end, T, k, H / 8,
-                                     static_cast<uint4*>(y), status);
+    auto kern = k > 4 ? combine_rows_warp<8, 2> : k > 2 ? combine_rows_warp<4, 4>
+                                                        : combine_rows_warp<2, 8>;
+    const cudaError_t e = launch_pdl(kern, dim3(rows_grid(T)), dim3(kRowsThreads), 0, stream,
+                                     static_cast<const uint4*>(rows), n_rows, slot_src, slot_w,
+                                     ids, e_begin, e_end, T, k, H / 8, static_cast<uint4*>(y),
+                                     status);
     return e == cudaSuccess ? kRcOk : kRcCudaError;
   }
   const long long threads = static_cast<long long>(T) * (H / 8);

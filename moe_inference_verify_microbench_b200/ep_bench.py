@@ -42,7 +42,7 @@ def _build(rank: int, world: int, dev: torch.device, T: int, transport: str):
     return mod, x
 
 
-def run_ep(args, metric, config_block, clock_sampler_cls, _make_inputs) -> None:
+def run_ep(args, metric, config_block, clock_sampler_cls) -> None:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     local = int(os.environ.get("LOCAL_RANK", str(rank)))
@@ -103,6 +103,9 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
             clocks.start()
             time.sleep(0.3)
         ms = _timed(lambda: mod(x), args.steps, stream)
+        # Serial copies: with two ranks on one host, overlapping every rank's
+        # upload and download with compute measured slower (6.5M against 8.4M
+        # tokens/s at N=2) than upload, forward, download in turn.
         x_host = x.cpu().pin_memory()
         y_host = torch.empty_like(x_host).pin_memory()
         n_e2e = max(3, min(args.steps, 50))
@@ -143,7 +146,8 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
         "e2e": {"value": world * T * n_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
                 "api": f"EPSparseMoE.forward (C7 schedule, transport={transport})",
-                "steps": n_e2e},
+                "steps": n_e2e, "copies": "pinned host, upload / forward / download in "
+                                          "turn on the compute stream; max over ranks"},
         # our kernels per forward: router, ep_keys, plan sort, local sort (3),
         # w13, w2, combine + (nccl) ep_meta, gather, partial combine
         #                   + (peer) publish, dispatch, recv wait, return, return wait
