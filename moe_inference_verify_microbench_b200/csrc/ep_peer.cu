@@ -231,8 +231,21 @@ __global__ void __launch_bounds__(kPeerThreads, 4) ep_dispatch(
     }
     __syncthreads();
     const int total = min(send_off[ep], cap);
+    int max_cnt = 0;
+    for (int d = 0; d < ep; ++d) max_cnt = max(max_cnt, send_off[d + 1] - send_off[d]);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int i = blockIdx.x * kPeerWarps + warp; i < total; i += gridDim.x * kPeerWarps) {
+    // Warp task t serves destination (t + me) % ep: adjacent warps write to
+    // different ranks, so every rank spreads its rows over all destinations
+    // at once (no rank's ingress takes every sender's traffic while the
+    // others idle) and the local copy runs beside the NVLink stores.
+    const long long tasks = static_cast<long long>(ep) * max_cnt;
+    for (long long t = blockIdx.x * kPeerWarps + warp; t < tasks;
+         t += static_cast<long long>(gridDim.x) * kPeerWarps) {
+      const int dd = static_cast<int>((t + me) % ep);
+      const int j = static_cast<int>(t / ep);
+      if (j >= send_off[dd + 1] - send_off[dd]) continue;
+      const int i = send_off[dd] + j;
+      if (i >= total) continue;
       const int pair = perm[i];
       const int n = pair / ep, d = pair - (pair / ep) * ep;
       const int pos = pair >= 0 ? base_in[d] + (i - send_off[d]) : -1;
@@ -314,10 +327,18 @@ __global__ void __launch_bounds__(kPeerThreads, 2) ep_return(const PeerArgs a,
   const int rows = min(st->n_recv, a.L.cap_rows);
   const float* wr = reinterpret_cast<const float*>(a.base[a.me] + a.L.recv_w);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = blockIdx.x * kPeerWarps + warp; i < rows; i += gridDim.x * kPeerWarps) {
-    int s = 0;
-    while (s + 1 < ep && base[s + 1] <= i) ++s;
-    const int pos = src_off[s] + (i - base[s]);
+  int max_cnt = 0;
+  for (int q = 0; q < ep; ++q) max_cnt = max(max_cnt, base[q + 1] - base[q]);
+  // Warp task t serves source (t + me) % ep, as in ep_dispatch.
+  const long long tasks = static_cast<long long>(ep) * max_cnt;
+  for (long long t = blockIdx.x * kPeerWarps + warp; t < tasks;
+       t += static_cast<long long>(gridDim.x) * kPeerWarps) {
+    const int s = static_cast<int>((t + a.me) % ep);
+    const int j = static_cast<int>(t / ep);
+    if (j >= base[s + 1] - base[s]) continue;
+    const int i = base[s] + j;
+    if (i >= rows) continue;
+    const int pos = src_off[s] + j;
     if (pos < 0 || pos >= a.L.cap_rows) {
       if (lane == 0) record_status(a.status, kErrBadRow);
       continue;
