@@ -36,7 +36,7 @@ namespace moe {
 constexpr int kPairBM = 2 * kBM;  // rows of a pair tile (M of the pair MMA)
 constexpr int kPairBN = 256;
 constexpr int kPairGatherWarp0 = 12;  // first of the four A-loader warps (GATHER_A)
-constexpr int kPairGatherLag = 4;     // a stage is published this many stages after its copies
+constexpr int kPairGatherLag = 2;     // a stage is published this many stages after its copies
 
 template <bool GATHER_A>
 constexpr int pair_threads() {
