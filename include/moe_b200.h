@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define MOE_B200_ABI_VERSION 3
+#define MOE_B200_ABI_VERSION 4
 
 #define MOE_RC_OK 0
 #define MOE_RC_BAD_ARGUMENT (-1)
@@ -57,6 +57,14 @@ extern "C" {
  * tile of the 2-CTA cluster-pair GEMMs that large batches use (ABI 2). */
 #define MOE_BLOCK_M 128
 #define MOE_PAIR_TILE_ROWS 256
+
+/* How the weighted expert rows become y (ABI 4): MOE_COMBINE_SLOTS writes
+ * every record's row to its slot and sums each token's k slots in slot order
+ * (bitwise reproducible); MOE_COMBINE_ATOMIC adds every record's row into its
+ * token's fp32 row with atomics, as index_add_ does on CUDA, and rounds once
+ * (the order of the k additions, hence the last fp32 bits, may vary). */
+#define MOE_COMBINE_SLOTS 0
+#define MOE_COMBINE_ATOMIC 1
 
 MOE_API int moe_abi_version(void);
 
@@ -242,6 +250,38 @@ MOE_API int moe_grouped_w2_rows(const void* h, int M, const int32_t* tiles,
                                 int H, int I, const int32_t* row_map, const float* slot_scale,
                                 void* out, int out_rows, int tile_rows, int32_t* status,
                                 cudaStream_t stream);
+
+/*
+ * ABI 4: the index_add_ semantics switch.  The reference un-permutes with
+ * index_add_ (C5/python/solution.py:160, C6/python/solution.py:175-176), an
+ * atomic fp32 accumulation on CUDA; the default here is the reproducible slot
+ * rows + k-sum.  moe_layer_forward_ex takes the combine mode
+ * (MOE_COMBINE_SLOTS: identical to moe_layer_forward; MOE_COMBINE_ATOMIC:
+ * the down GEMM adds every record's weighted row into its token's fp32 row in
+ * the workspace, then one rounding to y; decode-size batches that run the
+ * weight-streaming kernels keep the slot rows).  Its workspace is
+ * moe_layer_workspace_bytes_ex(..., combine_mode).
+ *   moe_grouped_w2_atomic_rows: out_f32[row_map[p] / red_div, :] +=
+ *     slot_scale[row_map[p]] * (h[p] @ w_down[e]^T) for the rows of the tile
+ *     table (row_map NULL: identity; slot_scale NULL: 1; row_map[p] <
+ *     n_slots); out_f32 [n_slots / red_div, H] fp32, zeroed by the caller.
+ *   moe_cast_f32_to_bf16: y[i] = bf16(src[i]), n a multiple of 8.
+ */
+MOE_API size_t moe_layer_workspace_bytes_ex(int T, int H, int I, int E, int top_k,
+                                            int combine_mode);
+MOE_API int moe_layer_forward_ex(const void* x, const void* router_weight,
+                                 const float* router_bias, const void* w_gate, const void* w_up,
+                                 const void* w_down, int T, int H, int I, int E, int top_k,
+                                 int norm_topk_prob, int combine_mode, void* workspace,
+                                 size_t workspace_bytes, void* y, int32_t* status,
+                                 cudaStream_t stream);
+MOE_API int moe_grouped_w2_atomic_rows(const void* h, int M, const int32_t* tiles,
+                                       const int32_t* num_tiles, int max_tiles,
+                                       const void* w_down, int E, int H, int I,
+                                       const int32_t* row_map, const float* slot_scale,
+                                       int n_slots, int red_div, float* out_f32, int tile_rows,
+                                       int32_t* status, cudaStream_t stream);
+MOE_API int moe_cast_f32_to_bf16(const float* src, long long n, void* y, cudaStream_t stream);
 
 /*
  * Send plan of the all_to_all expert-parallel schedule (C7/python/solution.py:

@@ -71,9 +71,18 @@ SIGNATURES: dict[str, tuple] = {
                                       _c_int, _ptr, _ptr, _ptr, _c_int, _ptr, _ptr]),
     "moe_ep_peer_return": (_c_int, [_ptr, _c_int, _c_int, _c_int, _c_int, _c_int, _ptr, _c_int,
                                     _ptr, _ptr, _ptr]),
+    # ABI 4: index_add_ semantics switch (atomic fp32 combine)
+    "moe_layer_workspace_bytes_ex": (_c_size, [_c_int, _c_int, _c_int, _c_int, _c_int, _c_int]),
+    "moe_layer_forward_ex": (_c_int, [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _c_int, _c_int, _c_int,
+                                      _c_int, _c_int, _c_int, _c_int, _ptr, _c_size, _ptr, _ptr,
+                                      _ptr]),
+    "moe_grouped_w2_atomic_rows": (_c_int, [_ptr, _c_int, _ptr, _ptr, _c_int, _ptr, _c_int,
+                                            _c_int, _c_int, _ptr, _ptr, _c_int, _c_int, _ptr,
+                                            _c_int, _ptr, _ptr]),
+    "moe_cast_f32_to_bf16": (_c_int, [_ptr, ctypes.c_longlong, _ptr, _ptr]),
 }
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

@@ -54,8 +54,14 @@ LayerPath layer_path(long long R, int H, int I, int E) {
   return lp;
 }
 
+// The atomic combine applies to the GEMM paths; decode-size batches keep the
+// slot rows and the k-sum (one of the results the atomic order allows).
+bool use_atomic_combine(int mode, const LayerPath& lp) {
+  return mode == MOE_COMBINE_ATOMIC && !lp.small;
+}
+
 template <class Body>
-size_t layer_layout(int T, int H, int I, int E, int k, void* ws, Body&& body) {
+size_t layer_layout(int T, int H, int I, int E, int k, int mode, void* ws, Body&& body) {
   const LayerPlan p = plan_layer(T, E, k);
   const LayerPath lp = layer_path(p.R, H, I, E);
   Carver c(ws);
@@ -69,7 +75,10 @@ size_t layer_layout(int T, int H, int I, int E, int k, void* ws, Body&& body) {
   int* num_tiles = c.take<int>(1);
   void* sorted_x = lp.fuse_gather ? nullptr : c.take<__nv_bfloat16>(p.R * H);
   void* h = c.take<__nv_bfloat16>(p.R * I);
-  void* slots = c.take<__nv_bfloat16>(p.R * H);
+  // slot rows [R, H] bf16, or with the atomic combine fp32 token rows [T, H]
+  void* slots = use_atomic_combine(mode, lp)
+                    ? static_cast<void*>(c.take<float>(static_cast<size_t>(T) * H))
+                    : static_cast<void*>(c.take<__nv_bfloat16>(p.R * H));
   body(p, ids, w, sort_ws, counts, offsets, perm, tiles, num_tiles, sorted_x, h, slots);
   return c.used;
 }
@@ -226,8 +235,27 @@ int moe_combine(const void* rows, int n_rows, const int32_t* slot_src, const flo
 }
 
 size_t moe_layer_workspace_bytes(int T, int H, int I, int E, int top_k) {
+  return moe_layer_workspace_bytes_ex(T, H, I, E, top_k, MOE_COMBINE_SLOTS);
+}
+
+size_t moe_layer_workspace_bytes_ex(int T, int H, int I, int E, int top_k, int combine_mode) {
   if (T < 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0) return 0;
-  return layer_layout(T, H, I, E, top_k, nullptr, [](auto&&...) {});
+  if (combine_mode != MOE_COMBINE_SLOTS && combine_mode != MOE_COMBINE_ATOMIC) return 0;
+  return layer_layout(T, H, I, E, top_k, combine_mode, nullptr, [](auto&&...) {});
+}
+
+int moe_grouped_w2_atomic_rows(const void* h, int M, const int32_t* tiles,
+                               const int32_t* num_tiles, int max_tiles, const void* w_down, int E,
+                               int H, int I, const int32_t* row_map, const float* slot_scale,
+                               int n_slots, int red_div, float* out_f32, int tile_rows,
+                               int32_t* status, cudaStream_t stream) {
+  return launch_w2_atomic(h, M, reinterpret_cast<const int4*>(tiles), num_tiles, max_tiles,
+                          w_down, E, H, I, row_map, slot_scale, n_slots, red_div, out_f32, status,
+                          stream, tile_rows);
+}
+
+int moe_cast_f32_to_bf16(const float* src, long long n, void* y, cudaStream_t stream) {
+  return launch_cast_f32_bf16(src, n, y, stream);
 }
 
 int moe_ep_keys(const int32_t* ids, int N, int k, int experts_per_rank, int ep, int32_t* keys,
@@ -294,15 +322,28 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                       const void* w_gate, const void* w_up, const void* w_down, int T, int H,
                       int I, int E, int top_k, int norm_topk_prob, void* workspace,
                       size_t workspace_bytes, void* y, int32_t* status, cudaStream_t stream) {
+  return moe_layer_forward_ex(x, router_weight, router_bias, w_gate, w_up, w_down, T, H, I, E,
+                              top_k, norm_topk_prob, MOE_COMBINE_SLOTS, workspace,
+                              workspace_bytes, y, status, stream);
+}
+
+int moe_layer_forward_ex(const void* x, const void* router_weight, const float* router_bias,
+                         const void* w_gate, const void* w_up, const void* w_down, int T, int H,
+                         int I, int E, int top_k, int norm_topk_prob, int combine_mode,
+                         void* workspace, size_t workspace_bytes, void* y, int32_t* status,
+                         cudaStream_t stream) {
+  if (combine_mode != MOE_COMBINE_SLOTS && combine_mode != MOE_COMBINE_ATOMIC)
+    return kRcBadArgument;
   if (x == nullptr || router_weight == nullptr || w_gate == nullptr || w_up == nullptr ||
       w_down == nullptr || y == nullptr || workspace == nullptr || T < 0 || H <= 0 || I <= 0 ||
       E <= 0 || top_k <= 0 || top_k > E)
     return kRcBadArgument;
   if (static_cast<long long>(T) * top_k > 0x7fffffffLL) return kRcUnsupported;
-  if (workspace_bytes < moe_layer_workspace_bytes(T, H, I, E, top_k)) return kRcWorkspace;
+  if (workspace_bytes < moe_layer_workspace_bytes_ex(T, H, I, E, top_k, combine_mode))
+    return kRcWorkspace;
   if (T == 0) return kRcOk;
   int rc = kRcOk;
-  layer_layout(T, H, I, E, top_k, workspace,
+  layer_layout(T, H, I, E, top_k, combine_mode, workspace,
                [&](const LayerPlan& p, int* ids, float* w, void* sort_ws, int* counts,
                    int* offsets, int* perm, int4* tiles, int* num_tiles, void* sorted_x, void* h,
                    void* slots) {
@@ -336,6 +377,21 @@ int moe_layer_forward(const void* x, const void* router_weight, const float* rou
                    if (rc == kRcOk)
                      rc = launch_w13_swiglu(sorted_x, R, tiles, num_tiles, max_tiles, w_gate,
                                             w_up, E, H, I, h, status, stream, tile_rows);
+                 }
+                 if (use_atomic_combine(combine_mode, lp)) {
+                   // index_add_ semantics: every record adds its weighted row into
+                   // its token's fp32 row, then one rounding to bf16.
+                   float* acc = static_cast<float*>(slots);
+                   if (rc == kRcOk &&
+                       cudaMemsetAsync(acc, 0, static_cast<size_t>(T) * H * sizeof(float),
+                                       stream) != cudaSuccess)
+                     rc = kRcCudaError;
+                   if (rc == kRcOk)
+                     rc = launch_w2_atomic(h, R, tiles, num_tiles, max_tiles, w_down, E, H, I,
+                                           perm, w, R, top_k, acc, status, stream, tile_rows);
+                   if (rc == kRcOk)
+                     rc = launch_cast_f32_bf16(acc, static_cast<long long>(T) * H, y, stream);
+                   return;
                  }
                  if (rc == kRcOk)
                    rc = launch_w2(h, R, tiles, num_tiles, max_tiles, w_down, E, H, I, perm, w,

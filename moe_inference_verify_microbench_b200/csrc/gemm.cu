@@ -325,6 +325,55 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
   return launch_gemm<64, kEpiSwiGLU, 8, true>(mg, mg, mu, g, units, stream);
 }
 
+// Down GEMM on 256-row pair tiles or 128-row tiles; EPI = kEpiStore writes
+// scaled bf16 rows to out[row_map[p]], kEpiAtomic adds them in fp32 to
+// out_f32[row_map[p] / red_div].
+template <int EPI>
+static int launch_w2_gemm(const void* h, int M, const int4* tiles, const int* num_tiles,
+                          int max_tiles, const void* w_down, int E, int H, int I,
+                          const int* row_map, const float* row_scale, void* out, float* out_f32,
+                          int red_div, int out_rows, int* status, cudaStream_t stream,
+                          int tile_rows) {
+  if ((I % kBK) != 0 || (H % 64) != 0) return kRcUnsupported;
+  GemmArgs g = blank_args(status);
+  g.tiles = tiles;
+  g.num_tiles = num_tiles;
+  g.max_tiles = max_tiles;
+  g.num_kb = I / kBK;
+  g.a_rows = M;
+  g.num_experts = E;
+  g.out = static_cast<__nv_bfloat16*>(out);
+  g.out_f32 = out_f32;
+  g.red_div = red_div;
+  g.out_ld = H;
+  g.out_rows = out_rows;
+  g.row_map = row_map;
+  g.row_scale = row_scale;
+  if (tile_rows == kPairTileRows) {
+    if ((H % kPairBN) != 0) return kRcUnsupported;
+    CUtensorMap ma, md;
+    int rc = map_2d(&ma, h, M, I, kBM);
+    if (rc == kRcOk) rc = map_3d(&md, w_down, E, H, I, kPairBN / 2);
+    if (rc != kRcOk) return rc;
+    g.n_tiles = H / kPairBN;
+    g.b_rows = kPairBN;
+    return launch_gemm_pair<EPI, kPairStages>(
+        ma, md, md, g, static_cast<long long>(max_tiles) * g.n_tiles, stream);
+  }
+  if (tile_rows != kBM) return kRcBadArgument;
+  const int bn = pick_bn(H, M, max_tiles, 7, [](int b) { return b; });
+  CUtensorMap ma, md;
+  int rc = map_2d(&ma, h, M, I, kBM);
+  if (rc == kRcOk) rc = map_3d(&md, w_down, E, H, I, bn);
+  if (rc != kRcOk) return rc;
+  g.n_tiles = H / bn;
+  g.b_rows = bn;
+  const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
+  if (bn == 256) return launch_gemm<256, EPI, 4>(ma, md, md, g, units, stream);
+  if (bn == 128) return launch_gemm<128, EPI, 6>(ma, md, md, g, units, stream);
+  return launch_gemm<64, EPI, 8>(ma, md, md, g, units, stream);
+}
+
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
               void* out, int out_rows, int* status, cudaStream_t stream, int tile_rows) {
@@ -335,54 +384,23 @@ int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int
   if (use_gemv_w2(M) && gemv_ok(H, I, false))
     return launch_w2_gemv(h, M, tiles, num_tiles, max_tiles, w_down, E, H, I, row_map, row_scale,
                           out, out_rows, status, stream);
-  if ((I % kBK) != 0 || (H % 64) != 0) return kRcUnsupported;
-  if (tile_rows == kPairTileRows) {
-    if ((H % kPairBN) != 0) return kRcUnsupported;
-    CUtensorMap ma, md;
-    int rc = map_2d(&ma, h, M, I, kBM);
-    if (rc == kRcOk) rc = map_3d(&md, w_down, E, H, I, kPairBN / 2);
-    if (rc != kRcOk) return rc;
-    GemmArgs g = blank_args(status);
-    g.tiles = tiles;
-    g.num_tiles = num_tiles;
-    g.max_tiles = max_tiles;
-    g.n_tiles = H / kPairBN;
-    g.num_kb = I / kBK;
-    g.b_rows = kPairBN;
-    g.a_rows = M;
-    g.num_experts = E;
-    g.out = static_cast<__nv_bfloat16*>(out);
-    g.out_ld = H;
-    g.out_rows = out_rows;
-    g.row_map = row_map;
-    g.row_scale = row_scale;
-    return launch_gemm_pair<kEpiStore, kPairStages>(
-        ma, md, md, g, static_cast<long long>(max_tiles) * g.n_tiles, stream);
-  }
-  if (tile_rows != kBM) return kRcBadArgument;
-  const int bn = pick_bn(H, M, max_tiles, 7, [](int b) { return b; });
-  CUtensorMap ma, md;
-  int rc = map_2d(&ma, h, M, I, kBM);
-  if (rc == kRcOk) rc = map_3d(&md, w_down, E, H, I, bn);
-  if (rc != kRcOk) return rc;
-  GemmArgs g = blank_args(status);
-  g.tiles = tiles;
-  g.num_tiles = num_tiles;
-  g.max_tiles = max_tiles;
-  g.n_tiles = H / bn;
-  g.num_kb = I / kBK;
-  g.b_rows = bn;
-  g.a_rows = M;
-  g.num_experts = E;
-  g.out = static_cast<__nv_bfloat16*>(out);
-  g.out_ld = H;
-  g.out_rows = out_rows;
-  g.row_map = row_map;
-  g.row_scale = row_scale;
-  const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
-  if (bn == 256) return launch_gemm<256, kEpiStore, 4>(ma, md, md, g, units, stream);
-  if (bn == 128) return launch_gemm<128, kEpiStore, 6>(ma, md, md, g, units, stream);
-  return launch_gemm<64, kEpiStore, 8>(ma, md, md, g, units, stream);
+  return launch_w2_gemm<kEpiStore>(h, M, tiles, num_tiles, max_tiles, w_down, E, H, I, row_map,
+                                   row_scale, out, nullptr, 1, out_rows, status, stream, tile_rows);
+}
+
+int launch_w2_atomic(const void* h, int M, const int4* tiles, const int* num_tiles,
+                     int max_tiles, const void* w_down, int E, int H, int I, const int* row_map,
+                     const float* row_scale, int n_slots, int red_div, float* out_f32,
+                     int* status, cudaStream_t stream, int tile_rows) {
+  if (h == nullptr || tiles == nullptr || num_tiles == nullptr || w_down == nullptr ||
+      out_f32 == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0 ||
+      n_slots < 0 || red_div <= 0)
+    return kRcBadArgument;
+  if ((reinterpret_cast<uintptr_t>(out_f32) & 15u) != 0) return kRcBadArgument;
+  if (M == 0 || max_tiles == 0) return kRcOk;
+  return launch_w2_gemm<kEpiAtomic>(h, M, tiles, num_tiles, max_tiles, w_down, E, H, I, row_map,
+                                    row_scale, nullptr, out_f32, red_div, n_slots, status, stream,
+                                    tile_rows);
 }
 
 }  // namespace moe

@@ -38,6 +38,7 @@ enum EpiKind : int {
   kEpiSwiGLU = 0,  // out[row, nt*BN/2 + c] = silu(acc[c]) * acc[BN/2 + c]
   kEpiStore = 1,   // out[map(row), nt*BN + c] = scale(map(row)) * acc[c]
   kEpiRouter = 2,  // per row: bf16 logits -> top-k -> softmax
+  kEpiAtomic = 3,  // out_f32[map(row) / red_div, nt*BN + c] += scale(map(row)) * acc[c]
 };
 
 struct GemmArgs {
@@ -55,6 +56,9 @@ struct GemmArgs {
   int out_rows;          // output rows (bounds check)
   const int* row_map;    // kEpiStore: out row = row_map[row] (null = identity)
   const float* row_scale;  // kEpiStore: multiplier indexed by the mapped row (null = 1)
+  // kEpiAtomic (with out_ld, out_rows, row_map, row_scale as for kEpiStore)
+  float* out_f32;        // fp32 accumulation rows, added to with vector atomics
+  int red_div;           // accumulation row = mapped row / red_div (top-k: slot -> token)
   // GATHER_A
   const __nv_bfloat16* a_src;  // source rows [a_src_rows, K]
   int a_src_rows;
@@ -215,6 +219,59 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tb,
                    : "memory");
       if (ok)
         *reinterpret_cast<uint4*>(out_base + static_cast<size_t>(o) * args.out_ld + c0 + j * 8) = v;
+    }
+    __syncwarp();
+  }
+}
+
+// Atomic-combine epilogue (the reference's index_add_ on CUDA, C5:160): each
+// row's scaled fp32 results are added into its token's accumulation row with
+// 16-byte fp32 vector atomics.  Rows are staged through this warp's shared
+// memory so that eight lanes cover one 128-byte segment of a row and each
+// instruction touches four whole segments.  The order in which the k records
+// of a token land is not fixed, so the sums are not bitwise reproducible.
+template <int BN, int kHalves>
+__device__ __forceinline__ void epilogue_tile_atomic(const GemmArgs& args, uint32_t tb, bool st,
+                                                     int orow_idx, float scale, int nt, int half,
+                                                     uint8_t* stage, int lane) {
+  constexpr int kSplit = (BN / kHalves >= 32) ? kHalves : 1;
+  constexpr int kCols = BN / kSplit;
+  static_assert(kCols % 32 == 0, "epilogue works in 32-column chunks");
+  if (half >= kSplit) return;
+  const uint32_t my_stage = smem_u32(stage);
+  const int j = lane & 7;
+  const int rsub = lane >> 3;
+  const int tok = st ? orow_idx / args.red_div : 0;
+  float* const out_base = args.out_f32 + static_cast<size_t>(nt) * BN;
+#pragma unroll 1
+  for (int c0 = half * kCols; c0 < (half + 1) * kCols; c0 += 32) {
+    uint32_t r[32];
+    tmem_ld32(tb + c0, r);
+    tc_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t a = my_stage + stage_slot<128>(lane, q);
+      asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                   "f"(__uint_as_float(r[4 * q]) * scale), "f"(__uint_as_float(r[4 * q + 1]) * scale),
+                   "f"(__uint_as_float(r[4 * q + 2]) * scale),
+                   "f"(__uint_as_float(r[4 * q + 3]) * scale)
+                   : "memory");
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int rr = i * 4 + rsub;
+      const int t = __shfl_sync(0xffffffffu, tok, rr);
+      const bool ok = __shfl_sync(0xffffffffu, st ? 1 : 0, rr) != 0;
+      float4 v;
+      asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                   : "r"(my_stage + stage_slot<128>(rr, j))
+                   : "memory");
+      if (ok)
+        atomicAdd(reinterpret_cast<float4*>(out_base + static_cast<size_t>(t) * args.out_ld + c0 +
+                                             j * 4),
+                  v);
     }
     __syncwarp();
   }
@@ -486,7 +543,7 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
       int orow_idx = row;
       float scale = 1.0f;
       bool st = valid;
-      if constexpr (EPI == kEpiStore) {
+      if constexpr (EPI == kEpiStore || EPI == kEpiAtomic) {
         if (st) {
           if (args.row_map != nullptr) orow_idx = args.row_map[row];
           if (orow_idx < 0 || orow_idx >= args.out_rows) {
@@ -506,6 +563,9 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
       if constexpr (EPI == kEpiSwiGLU || EPI == kEpiStore) {
         epilogue_tile<BN, EPI, kHalves>(args, tb, row, valid, st, orow_idx, scale, nt, half,
                                         sOut + (warp - 4) * kEpiStageBytes, lane);
+      } else if constexpr (EPI == kEpiAtomic) {
+        epilogue_tile_atomic<BN, kHalves>(args, tb, st, orow_idx, scale, nt, half,
+                                          sOut + (warp - 4) * kEpiStageBytes, lane);
       } else {
         if (half == 0) {  // one warp per lane quarter: rows are not split by columns
           // Router: the row's E logits -> bf16 -> top-k (value desc, id asc) -> softmax.

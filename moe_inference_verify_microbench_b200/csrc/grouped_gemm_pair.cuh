@@ -57,7 +57,8 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB0,
                              const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
-  static_assert(EPI == kEpiSwiGLU || EPI == kEpiStore, "pair kernel: SwiGLU or store epilogue");
+  static_assert(EPI == kEpiSwiGLU || EPI == kEpiStore || EPI == kEpiAtomic,
+                "pair kernel: SwiGLU, store or atomic epilogue");
   static_assert(!GATHER_A || kPairGatherLag < STAGES - 1,
                 "a loader must publish before it needs the stage back");
   using L = PairSmem<STAGES>;
@@ -313,7 +314,7 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
       int orow_idx = row;
       float scale = 1.0f;
       bool st = valid;
-      if constexpr (EPI == kEpiStore) {
+      if constexpr (EPI == kEpiStore || EPI == kEpiAtomic) {
         if (st) {
           if (args.row_map != nullptr) orow_idx = args.row_map[row];
           if (orow_idx < 0 || orow_idx >= args.out_rows) {
@@ -330,8 +331,12 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
-      epilogue_tile<BN, EPI, kHalves>(args, tb, row, valid, st, orow_idx, scale, nt, half,
-                                      sOut + (warp - 4) * kEpiStageBytes, lane);
+      if constexpr (EPI == kEpiAtomic)
+        epilogue_tile_atomic<BN, kHalves>(args, tb, st, orow_idx, scale, nt, half,
+                                          sOut + (warp - 4) * kEpiStageBytes, lane);
+      else
+        epilogue_tile<BN, EPI, kHalves>(args, tb, row, valid, st, orow_idx, scale, nt, half,
+                                        sOut + (warp - 4) * kEpiStageBytes, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? release1 : release0);

@@ -132,6 +132,15 @@ int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles
                    const float* row_scale, void* out, int out_rows, int* status,
                    cudaStream_t stream);
 
+// Down GEMM with the atomic combine: out_f32[row_map[p] / red_div] +=
+// row_scale[row_map[p]] * (h[p] @ w_down[e]^T) in fp32 (row_map[p] < n_slots).
+int launch_w2_atomic(const void* h, int M, const int4* tiles, const int* num_tiles,
+                     int max_tiles, const void* w_down, int E, int H, int I, const int* row_map,
+                     const float* row_scale, int n_slots, int red_div, float* out_f32,
+                     int* status, cudaStream_t stream, int tile_rows = 128);
+// y[i] = bf16(src[i]) for n elements (n % 8 == 0).
+int launch_cast_f32_bf16(const float* src, long long n, void* y, cudaStream_t stream);
+
 // Expert-parallel send plan (ep_plan.cu).
 int launch_ep_keys(const int* ids, int N, int k, int epr, int ep, int* keys, int* status,
                    cudaStream_t stream);

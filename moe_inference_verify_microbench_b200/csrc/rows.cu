@@ -186,6 +186,20 @@ __global__ void __launch_bounds__(kRowsThreads) combine_rows_warp(
   }
 }
 
+// y = bf16(src), eight elements per thread (two 16-byte loads, one 16-byte
+// store): the final rounding of the atomic combine's fp32 accumulation rows.
+__global__ void __launch_bounds__(kRowsThreads) cast_f32_bf16(const float4* __restrict__ src,
+                                                              long long n8, uint4* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 a = __ldcs(src + 2 * i), b = __ldcs(src + 2 * i + 1);
+    y[i] = make_uint4(pack_bf16x2(a.x, a.y), pack_bf16x2(a.z, a.w), pack_bf16x2(b.x, b.y),
+                      pack_bf16x2(b.z, b.w));
+  }
+}
+
 static int rows_grid(long long rows) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -225,6 +239,21 @@ int launch_combine(const void* rows, int n_rows, const int* slot_src, const floa
   const cudaError_t e = launch_pdl(combine_rows, dim3(grid), dim3(kRowsThreads), 0, stream,
                                    static_cast<const uint4*>(rows), n_rows, slot_src, slot_w, ids,
                                    e_begin, e_end, T, k, H / 8, static_cast<uint4*>(y), status);
+  return e == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+int launch_cast_f32_bf16(const float* src, long long n, void* y, cudaStream_t stream) {
+  if (n < 0 || (n % 8) != 0 || (n > 0 && (src == nullptr || y == nullptr)) ||
+      (reinterpret_cast<uintptr_t>(src) & 15u) != 0 || (reinterpret_cast<uintptr_t>(y) & 15u) != 0)
+    return kRcBadArgument;
+  if (n == 0) return kRcOk;
+  const long long n8 = n / 8;
+  const long long blocks = (n8 + kRowsThreads - 1) / kRowsThreads;
+  const long long cap = static_cast<long long>(device_sm_count()) * 8;
+  const int grid = static_cast<int>(blocks < cap ? blocks : cap);
+  const cudaError_t e = launch_pdl(cast_f32_bf16, dim3(grid), dim3(kRowsThreads), 0, stream,
+                                   reinterpret_cast<const float4*>(src), n8,
+                                   static_cast<uint4*>(y));
   return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 

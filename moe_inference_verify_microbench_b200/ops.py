@@ -288,6 +288,49 @@ def grouped_w2(h: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor, ma
     return out
 
 
+INDEX_ADD_MODES = {"deterministic": 0, "atomic": 1}  # MOE_COMBINE_SLOTS / MOE_COMBINE_ATOMIC
+
+
+def _combine_mode(index_add: str) -> int:
+    if index_add not in INDEX_ADD_MODES:
+        raise ValueError(f"index_add must be one of {tuple(INDEX_ADD_MODES)}, got {index_add!r}")
+    return INDEX_ADD_MODES[index_add]
+
+
+def grouped_w2_atomic(h: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor,
+                      max_tiles_: int, w_down: torch.Tensor, row_map: torch.Tensor | None,
+                      slot_scale: torch.Tensor | None, n_slots: int, red_div: int,
+                      out_f32: torch.Tensor, tile_rows: int = 128) -> torch.Tensor:
+    """out_f32[map(r) // red_div] += scale(map(r)) * (h[r] @ w_down[e]^T) with fp32
+    atomics: the index_add_ un-permute of C5/python/solution.py:158-160 fused into
+    the down GEMM.  ``out_f32`` [n_slots // red_div, H] must start at zero."""
+    _need(h, "h", torch.bfloat16, 2)
+    _need(w_down, "w_down", torch.bfloat16, 3)
+    _need(out_f32, "out_f32", torch.float32, 2)
+    M, I = h.shape
+    E, H, I2 = w_down.shape
+    if I2 != I or out_f32.shape[1] != H or out_f32.shape[0] * red_div < n_slots:
+        raise ValueError("w_down must be [E, H, I] matching h [M, I]; out_f32 [n_slots/red_div, H]")
+    if row_map is not None:
+        _need(row_map, "row_map", torch.int32)
+    if slot_scale is not None:
+        _need(slot_scale, "slot_scale", torch.float32)
+    _rc(_native.load().moe_grouped_w2_atomic_rows(
+        _p(h), M, _p(tiles), _p(num_tiles), max_tiles_, _p(w_down), E, H, I, _p(row_map),
+        _p(slot_scale), n_slots, red_div, _p(out_f32), tile_rows, _p(status_word(h.device)),
+        _stream(h.device)), "moe_grouped_w2_atomic_rows")
+    return out_f32
+
+
+def cast_f32_bf16(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 copy of an fp32 tensor (element count a multiple of 8)."""
+    _need(src, "src", torch.float32)
+    y = out if out is not None else torch.empty(src.shape, dtype=torch.bfloat16, device=src.device)
+    _rc(_native.load().moe_cast_f32_to_bf16(_p(src), src.numel(), _p(y), _stream(src.device)),
+        "moe_cast_f32_to_bf16")
+    return y
+
+
 # --------------------------------------------------------------------------- EP send plan
 
 
@@ -325,8 +368,13 @@ def ep_meta(perm: torch.Tensor, count: torch.Tensor, max_rows: int, ids: torch.T
 def moe_layer(x: torch.Tensor, router_weight: torch.Tensor, w_gate: torch.Tensor,
               w_up: torch.Tensor, w_down: torch.Tensor, top_k: int, norm_topk_prob: bool = True,
               bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
-              workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Single-device MoE layer (C5/python/solution.py:108-161) in one C-ABI call."""
+              workspace: torch.Tensor | None = None,
+              index_add: str = "deterministic") -> torch.Tensor:
+    """Single-device MoE layer (C5/python/solution.py:108-161) in one C-ABI call.
+    ``index_add``: "deterministic" (slot rows + k-sum in slot order, bitwise
+    reproducible) or "atomic" (fp32 atomic accumulation per token, the
+    reference's index_add_ on CUDA; decode-size batches keep the slot rows)."""
+    mode = _combine_mode(index_add)
     _need(x, "x", torch.bfloat16, 2)
     for name, t in (("router_weight", router_weight), ("w_gate", w_gate), ("w_up", w_up),
                     ("w_down", w_down)):
@@ -336,16 +384,26 @@ def moe_layer(x: torch.Tensor, router_weight: torch.Tensor, w_gate: torch.Tensor
     T, H = x.shape
     E, I, _ = w_gate.shape
     lib = _native.load()
-    ws_bytes = int(lib.moe_layer_workspace_bytes(T, H, I, E, top_k))
+    ws_bytes = int(lib.moe_layer_workspace_bytes_ex(T, H, I, E, top_k, mode))
     if workspace is None or workspace.numel() < ws_bytes:
         workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
     y = out if out is not None else torch.empty_like(x)
-    _rc(lib.moe_layer_forward(_p(x), _p(router_weight), _p(bias), _p(w_gate), _p(w_up),
-                              _p(w_down), T, H, I, E, top_k, int(bool(norm_topk_prob)),
-                              _p(workspace), workspace.numel(), _p(y), _p(status_word(x.device)),
-                              _stream(x.device)), "moe_layer_forward")
+    if mode == 0:
+        _rc(lib.moe_layer_forward(_p(x), _p(router_weight), _p(bias), _p(w_gate), _p(w_up),
+                                  _p(w_down), T, H, I, E, top_k, int(bool(norm_topk_prob)),
+                                  _p(workspace), workspace.numel(), _p(y),
+                                  _p(status_word(x.device)), _stream(x.device)),
+            "moe_layer_forward")
+    else:
+        _rc(lib.moe_layer_forward_ex(_p(x), _p(router_weight), _p(bias), _p(w_gate), _p(w_up),
+                                     _p(w_down), T, H, I, E, top_k, int(bool(norm_topk_prob)),
+                                     mode, _p(workspace), workspace.numel(), _p(y),
+                                     _p(status_word(x.device)), _stream(x.device)),
+            "moe_layer_forward_ex")
     return y
 
 
-def layer_workspace_bytes(T: int, H: int, I: int, E: int, top_k: int) -> int:
-    return int(_native.load().moe_layer_workspace_bytes(T, H, I, E, top_k))
+def layer_workspace_bytes(T: int, H: int, I: int, E: int, top_k: int,
+                          index_add: str = "deterministic") -> int:
+    return int(_native.load().moe_layer_workspace_bytes_ex(T, H, I, E, top_k,
+                                                           _combine_mode(index_add)))

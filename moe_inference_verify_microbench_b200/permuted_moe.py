@@ -6,7 +6,9 @@ call, ``moe_layer_forward``: router + top-k on tcgen05, a stable counting
 sort, the row gather, the w13 grouped GEMM with SwiGLU fused, the w2 grouped
 GEMM with the top-k weight fused, and a deterministic k-way combine.  It
 issues no host synchronisation (the reference syncs once per expert on
-``.item()``, C5:144).
+``.item()``, C5:144).  The keyword extra ``index_add="atomic"`` switches the
+un-permute to the reference's own semantics (index_add_, C5:160: fp32 atomic
+accumulation per token, fused into the down GEMM).
 
 The module must be bf16 on a CUDA device: there is no CPU path.
 """
@@ -26,8 +28,10 @@ class PermutedSparseMoE(nn.Module):
     """Single-GPU sparse MoE with permutation + grouped compute (C5:82-161)."""
 
     def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int,
-                 norm_topk_prob: bool = True) -> None:
+                 norm_topk_prob: bool = True, *, index_add: str = "deterministic") -> None:
         super().__init__()
+        ops._combine_mode(index_add)  # validate
+        self.index_add = index_add
         self.hidden = hidden
         self.intermediate = intermediate
         self.num_experts = num_experts
@@ -53,5 +57,5 @@ class PermutedSparseMoE(nn.Module):
             x_flat = x_flat.contiguous()
         wg, wu, wd = self.pack()
         y = ops.moe_layer(x_flat, self.gate.weight, wg, wu, wd, self.top_k, self.norm_topk_prob,
-                          bias=router_bias_of(self.gate))
+                          bias=router_bias_of(self.gate), index_add=self.index_add)
         return y.reshape(shape)

@@ -39,7 +39,7 @@ def test_exported_dynamic_symbols_match_header():
 
 def test_host_queries():
     lib = _native.load()
-    assert lib.moe_abi_version() == 3
+    assert lib.moe_abi_version() == 4
     assert lib.moe_max_tiles(131072, 128) == 1024 + 128
     assert lib.moe_max_tiles(0, 16) == 16
     assert lib.moe_max_tiles_rows(131072, 128, 256) == 512 + 128
@@ -69,3 +69,18 @@ def test_null_arguments_rejected_without_launch():
                                  None, 0, None, None, None) == -1
     assert lib.moe_sort_align(None, 8, 16, 0, 16, None, 0, None, None, None, None, None, None, 0,
                               None, None, None) == -1
+
+
+def test_index_add_mode_is_validated():
+    import torch
+    from moe_inference_verify_microbench_b200 import PermutedSparseMoE, ops
+    with pytest.raises(ValueError):
+        PermutedSparseMoE(64, 32, 8, 2, index_add="sorted")
+    x = torch.zeros(4, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        ops.moe_layer(x, x, x, x, x, 2, index_add="fast")
+    lib = ops._native.load()
+    assert lib.moe_layer_workspace_bytes_ex(16, 2048, 768, 128, 8, 2) == 0
+    # the atomic combine's fp32 token rows replace the bf16 slot rows
+    assert (lib.moe_layer_workspace_bytes_ex(16384, 2048, 768, 128, 8, 1)
+            < lib.moe_layer_workspace_bytes_ex(16384, 2048, 768, 128, 8, 0))

@@ -199,3 +199,75 @@ def test_layer_decode_sizes_full_shapes(cuda, T):
     lids = np.vectorize(remap.get)(ids_np)
     ref = sample_token_outputs(to_f32(x), f(wg), f(wu), f(wd), lids, w.cpu().numpy(), np.arange(T))
     assert mo.rel_err(to_f32(y), ref) <= REL_TOL
+
+
+# ------------------------------------------------------------ index_add_ switch
+
+
+@pytest.mark.parametrize("T,k,E", [(300, 8, 128), (4096, 8, 128), (3000, 8, 16), (1, 8, 128)])
+def test_layer_atomic_index_add(cuda, T, k, E):
+    """The atomic combine (index_add_ semantics, C5:160) against the fp32 oracle
+    and against the reproducible slot combine; T=1 runs the decode kernels,
+    which keep the slot rows; (3000, 8, 16) runs the CTA-pair GEMMs."""
+    H, I = 2048, 768
+    d = mo.make_inputs(T, H, I, E, seed=40 + T)
+    args = [to_t(d[n], cuda) for n in ("x", "wr", "w_gate", "w_up", "w_down")]
+    y_at = ops.moe_layer(*args, top_k=k, index_add="atomic")
+    y_det = ops.moe_layer(*args, top_k=k)
+    ids, w, lg = ops.router_topk(args[0], args[1], k, return_logits=True)
+    ops.check_status(cuda)
+    # the two combines differ in the order of the fp32 additions and in the
+    # slot path's bf16 rounding of every weighted record row
+    assert mo.rel_err(to_f32(y_at), to_f32(y_det)) <= 1e-2
+    f = {n: mo.f32_from_bf16_bits(d[n]) for n in ("x", "w_gate", "w_up", "w_down")}
+    tok = np.unique(np.linspace(0, T - 1, min(T, 40)).astype(np.int64))
+    ref = sample_token_outputs(f["x"], f["w_gate"], f["w_up"], f["w_down"], ids.cpu().numpy(),
+                               w.cpu().numpy(), tok)
+    assert mo.rel_err(to_f32(y_at)[tok], ref) <= REL_TOL
+
+
+def test_permuted_sparse_moe_atomic_matches_fixture(cuda):
+    """C5 drop-in with index_add="atomic" against the reference's own output."""
+    g = load_golden("c5_full_t256.npz")
+    d = mo.make_inputs(256, 2048, 768, 128, seed=0)
+    with torch.device(cuda):
+        mod = PermutedSparseMoE(2048, 768, 128, 8, index_add="atomic").to(torch.bfloat16)
+    mod.gate.weight.data.copy_(to_t(d["wr"], cuda))
+    wg, wu, wd = mod.pack()
+    wg.copy_(to_t(d["w_gate"], cuda))
+    wu.copy_(to_t(d["w_up"], cuda))
+    wd.copy_(to_t(d["w_down"], cuda))
+    x = to_t(d["x"], cuda)
+    with torch.no_grad():
+        y = to_f32(mod(x))
+    ids, _, _ = ops.router_topk(x, mod.gate.weight, 8)
+    ops.check_status(cuda)
+    same = (np.sort(ids.cpu().numpy(), 1) == np.sort(g["topk_ids"], 1)).all(1)
+    assert same.mean() >= 0.85
+    assert mo.rel_err(y[same], mo.f32_from_bf16_bits(g["y"])[same]) <= REL_TOL
+
+
+def test_grouped_w2_atomic_op(cuda):
+    """moe_grouped_w2_atomic_rows + moe_cast_f32_to_bf16 against moe_grouped_w2
+    (slot rows) + moe_combine, on 128- and 256-row tile tables."""
+    T, H, I, E, k = 2048, 2048, 768, 16, 8
+    d = mo.make_inputs(T, H, I, E, seed=77)
+    x, wr, wg, wu, wd = (to_t(d[n], cuda) for n in ("x", "wr", "w_gate", "w_up", "w_down"))
+    ids, w, _ = ops.router_topk(x, wr, k)
+    for rows in (128, 256):
+        s = ops.sort_align(ids, E, tile_rows=rows)
+        h = ops.grouped_w13_swiglu_gather(x, s.perm, k, T * k, s.tiles, s.num_tiles, s.max_tiles,
+                                          wg, wu, tile_rows=rows)
+        sl = ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, wd, row_map=s.perm,
+                            slot_scale=w.reshape(-1), tile_rows=rows)
+        y_det = ops.combine(sl, T, k)
+        acc = torch.zeros(T, H, dtype=torch.float32, device=cuda)
+        ops.grouped_w2_atomic(h, s.tiles, s.num_tiles, s.max_tiles, wd, s.perm, w.reshape(-1),
+                              T * k, k, acc, tile_rows=rows)
+        y_at = ops.cast_f32_bf16(acc)
+        ops.check_status(cuda)
+        # the slot rows (bf16-rounded weighted records) summed in fp32: equal up
+        # to that rounding and the order of the additions
+        ref = sl.float().reshape(T, k, H).sum(1)
+        assert mo.rel_err(acc.cpu().numpy(), ref.cpu().numpy()) <= 1e-2, rows
+        assert mo.rel_err(to_f32(y_at), to_f32(y_det)) <= 1e-2, rows
