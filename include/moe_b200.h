@@ -284,6 +284,17 @@ MOE_API int moe_grouped_w2_atomic_rows(const void* h, int M, const int32_t* tile
 MOE_API int moe_cast_f32_to_bf16(const float* src, long long n, void* y, cudaStream_t stream);
 
 /*
+ * Decoder-block glue around the MoE (C8/python/solution.py:235-325, whose
+ * block is h = x + attn(norm(x)); y = h + moe(norm(h)) with the suite's
+ * RMSNorm: fp32 x * rsqrt(mean(x^2) + eps) * weight, cast back to bf16):
+ * h_out = bf16(x + delta) (skipped when delta is NULL: h = x), then
+ * y = RMSNorm(h) with weight fp32 [H].  x, delta, h_out, y bf16 [T, H],
+ * H % 8 == 0, one pass over the rows.
+ */
+MOE_API int moe_add_rmsnorm(const void* x, const void* delta, const float* weight, int T, int H,
+                            float eps, void* h_out, void* y, cudaStream_t stream);
+
+/*
  * Send plan of the all_to_all expert-parallel schedule (C7/python/solution.py:
  * 150-203), which here dispatches one row per (token, owner rank):
  *   moe_ep_keys: keys[n*ep + r] = r if one of ids[n, 0..k) lies in rank r's

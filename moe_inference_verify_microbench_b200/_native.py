@@ -80,6 +80,8 @@ SIGNATURES: dict[str, tuple] = {
                                             _c_int, _c_int, _ptr, _ptr, _c_int, _c_int, _ptr,
                                             _c_int, _ptr, _ptr]),
     "moe_cast_f32_to_bf16": (_c_int, [_ptr, ctypes.c_longlong, _ptr, _ptr]),
+    "moe_add_rmsnorm": (_c_int, [_ptr, _ptr, _ptr, _c_int, _c_int, ctypes.c_float, _ptr, _ptr,
+                                 _ptr]),
 }
 
 ABI_VERSION = 4

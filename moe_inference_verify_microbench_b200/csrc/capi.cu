@@ -254,6 +254,11 @@ int moe_grouped_w2_atomic_rows(const void* h, int M, const int32_t* tiles,
                           stream, tile_rows);
 }
 
+int moe_add_rmsnorm(const void* x, const void* delta, const float* weight, int T, int H,
+                    float eps, void* h_out, void* y, cudaStream_t stream) {
+  return launch_add_rmsnorm(x, delta, weight, T, H, eps, h_out, y, stream);
+}
+
 int moe_cast_f32_to_bf16(const float* src, long long n, void* y, cudaStream_t stream) {
   return launch_cast_f32_bf16(src, n, y, stream);
 }

@@ -138,6 +138,9 @@ int launch_w2_atomic(const void* h, int M, const int4* tiles, const int* num_til
                      int max_tiles, const void* w_down, int E, int H, int I, const int* row_map,
                      const float* row_scale, int n_slots, int red_div, float* out_f32,
                      int* status, cudaStream_t stream, int tile_rows = 128);
+// Block glue: h = delta ? bf16(x + delta) : x; y = bf16(h * rsqrt(mean(h^2) + eps) * w).
+int launch_add_rmsnorm(const void* x, const void* delta, const float* w, int T, int H, float eps,
+                       void* h_out, void* y, cudaStream_t stream);
 // y[i] = bf16(src[i]) for n elements (n % 8 == 0).
 int launch_cast_f32_bf16(const float* src, long long n, void* y, cudaStream_t stream);
 

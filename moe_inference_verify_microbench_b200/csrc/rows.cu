@@ -200,6 +200,68 @@ __global__ void __launch_bounds__(kRowsThreads) cast_f32_bf16(const float4* __re
   }
 }
 
+// Pre-norm decoder block glue (the residual add and RMSNorm around the MoE of
+// C8/python/solution.py:235-325, RMSNorm as the suite's harness defines it):
+//   h = delta ? bf16(x + delta) : x
+//   y = bf16((float(h) * rsqrt(mean_j float(h_j)^2 + eps)) * w)
+// one warp per row, fp32 throughout, the row's sum of squares reduced across
+// the warp; the second pass re-reads the row (L1/L2 hits).
+__global__ void __launch_bounds__(kRowsThreads) add_rmsnorm_rows(
+    const uint4* __restrict__ x, const uint4* __restrict__ delta, const float* __restrict__ w,
+    int T, int vec, float eps, uint4* __restrict__ h_out, uint4* __restrict__ y) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float inv_h = 1.0f / static_cast<float>(vec * 8);
+  for (int n = blockIdx.x * kRowsWarps + warp; n < T; n += gridDim.x * kRowsWarps) {
+    const uint4* xr = x + static_cast<size_t>(n) * vec;
+    const uint4* dr = delta != nullptr ? delta + static_cast<size_t>(n) * vec : nullptr;
+    float ss = 0.0f;
+    for (int v = lane; v < vec; v += 32) {
+      uint4 a = __ldg(xr + v);
+      if (dr != nullptr) {
+        const uint4 b = __ldg(dr + v);
+        const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 fa = __bfloat1622float2(a2[q]), fb = __bfloat1622float2(b2[q]);
+          o[q] = pack_bf16x2(fa.x + fb.x, fa.y + fb.y);
+        }
+        a = make_uint4(o[0], o[1], o[2], o[3]);
+        h_out[static_cast<size_t>(n) * vec + v] = a;
+      }
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h2[q]);
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float r = rsqrtf(ss * inv_h + eps);
+    // Each lane re-reads only the h_out vectors it stored itself.
+    const uint4* hr = dr != nullptr ? h_out + static_cast<size_t>(n) * vec : xr;
+    for (int v = lane; v < vec; v += 32) {
+      const uint4 a = dr != nullptr ? hr[v] : __ldg(hr + v);
+      const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * v);
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * v + 1);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h2[q]);
+        o[q] = pack_bf16x2((f.x * r) * wv[2 * q], (f.y * r) * wv[2 * q + 1]);
+      }
+      y[static_cast<size_t>(n) * vec + v] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 static int rows_grid(long long rows) {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -239,6 +301,23 @@ int launch_combine(const void* rows, int n_rows, const int* slot_src, const floa
   const cudaError_t e = launch_pdl(combine_rows, dim3(grid), dim3(kRowsThreads), 0, stream,
                                    static_cast<const uint4*>(rows), n_rows, slot_src, slot_w, ids,
                                    e_begin, e_end, T, k, H / 8, static_cast<uint4*>(y), status);
+  return e == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+int launch_add_rmsnorm(const void* x, const void* delta, const float* w, int T, int H, float eps,
+                       void* h_out, void* y, cudaStream_t stream) {
+  if (T < 0 || H <= 0 || (H % 8) != 0 || !(eps >= 0.0f) ||
+      (T > 0 && (x == nullptr || w == nullptr || y == nullptr ||
+                 (delta != nullptr && h_out == nullptr))))
+    return kRcBadArgument;
+  for (const void* p : {x, delta, static_cast<const void*>(w), static_cast<const void*>(h_out),
+                        static_cast<const void*>(y)})
+    if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return kRcBadArgument;
+  if (T == 0) return kRcOk;
+  const cudaError_t e = launch_pdl(add_rmsnorm_rows, dim3(rows_grid(T)), dim3(kRowsThreads), 0,
+                                   stream, static_cast<const uint4*>(x),
+                                   static_cast<const uint4*>(delta), w, T, H / 8, eps,
+                                   static_cast<uint4*>(h_out), static_cast<uint4*>(y));
   return e == cudaSuccess ? kRcOk : kRcCudaError;
 }
 

@@ -331,6 +331,29 @@ def cast_f32_bf16(src: torch.Tensor, out: torch.Tensor | None = None) -> torch.T
     return y
 
 
+def add_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float,
+                delta: torch.Tensor | None = None):
+    """RMSNorm of the rows of ``x`` (or of ``h = x + delta`` in bf16), as the
+    decoder block around C8's MoE computes it (C8/python/solution.py:235-325):
+    fp32 ``h * rsqrt(mean(h^2) + eps) * weight`` rounded to bf16.  Returns
+    ``y`` or ``(h, y)`` when ``delta`` is given."""
+    _need(x, "x", torch.bfloat16)
+    H = x.shape[-1]
+    T = x.numel() // max(H, 1)
+    if delta is not None:
+        _need(delta, "delta", torch.bfloat16)
+        if delta.shape != x.shape:
+            raise ValueError("delta must have the shape of x")
+    w = weight.detach().float().contiguous()
+    if w.device != x.device or w.numel() != H:
+        raise ValueError("weight must be [H] on the device of x")
+    y = torch.empty_like(x)
+    h = torch.empty_like(x) if delta is not None else None
+    _rc(_native.load().moe_add_rmsnorm(_p(x), _p(delta), _p(w), T, H, float(eps), _p(h), _p(y),
+                                       _stream(x.device)), "moe_add_rmsnorm")
+    return (h, y) if delta is not None else y
+
+
 # --------------------------------------------------------------------------- EP send plan
 
 

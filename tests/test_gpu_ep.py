@@ -210,3 +210,48 @@ def test_ep_peer_transport_bit_identical_to_nccl():
     res = _spawn(_peer_worker, 2, (29950,))  # both transports pick the same tile height here
     for rank, same in res:
         assert all(same), (rank, same)
+
+
+def _block_worker(rank, world, port, q):
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
+    from moe_inference_verify_microbench_b200 import ops
+    from moe_inference_verify_microbench_b200.hybrid import HybridBlock
+
+    dev = _init(rank, world, port)
+    try:
+        H, I, E, k, nh, nkv, hd = 2048, 768, 128, 8, 32, 4, 128
+        g = torch.Generator(device=dev)
+        g.manual_seed(21)
+        r = lambda *s, sc=0.02: (torch.randn(*s, generator=g, device=dev) * sc).to(torch.bfloat16)
+        with torch.device(dev):
+            blk = HybridBlock(H, I, nh, nkv, hd, E, k, world, rank, None, world, rank,
+                              None).to(torch.bfloat16)
+        wg, wu, wd = r(E, I, H), r(E, I, H), r(E, H, I)
+        blk.weight_loader(1.0 + r(H, sc=0.1), r(nh * hd, H), r(nkv * hd, H), r(nkv * hd, H),
+                          r(H, nh * hd), 1.0 + r(H, sc=0.1), r(E, H), list(wg), list(wu), list(wd))
+        x = r(2, 64, H, sc=1.0)
+        with torch.no_grad():
+            y = blk(x)
+            # the same block with the harness norms and the single-GPU layer
+            h_ref = x + blk.attn(blk.attn_norm(x))
+            n2 = blk.moe_norm(h_ref).reshape(-1, H).contiguous()
+            y_ref = h_ref + ops.moe_layer(n2, blk.moe.gate.weight, wg, wu, wd, k).reshape(x.shape)
+        torch.cuda.synchronize()
+        ops.check_status(dev)
+        err = ((y.float() - y_ref.float()).abs().amax(-1) /
+               y_ref.float().abs().amax(-1)).reshape(-1).cpu()
+        q.put((rank, float((err <= 2e-2).float().mean())))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_hybrid_block_glue_matches_harness():
+    """HybridBlock with the fused residual-add + RMSNorm row kernel against the
+    harness norms + single-GPU layer (tp = ep = 1, one process)."""
+    _need(1)
+    res = _spawn(_block_worker, 1, (29960,))
+    for rank, frac in res:
+        assert frac >= 0.97, (rank, frac)  # a norm's last bit may flip a top-k boundary
