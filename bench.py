@@ -233,7 +233,7 @@ class Timer:
 # DRAM bytes (read + write) of one launch of the gate/up GEMM at the bench
 # workload, from the one-pass ncu capture summarised in
 # profiles/w13_pair_gather_t16384.md.
-W13_TRAFFIC = {(16384, 256): 1210507520 + 192126208}
+W13_TRAFFIC = {(16384, 256): 1211178240 + 192313344}
 
 
 def w13_kernel_name(tile_rows):
