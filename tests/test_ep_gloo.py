@@ -97,3 +97,11 @@ def test_unknown_transport_is_refused():
     from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE
     with pytest.raises(ValueError):
         EPSparseMoE(64, 32, 8, 2, 1, 0, group=None, transport="shm")
+
+
+def test_peer_exchange_rejects_bad_shapes_before_touching_the_gpu():
+    import torch
+    from moe_inference_verify_microbench_b200.peer import PeerExchange
+    for hidden, k, cap in ((100, 8, 64), (2048, 9, 64), (2048, 8, -1)):
+        with pytest.raises(ValueError):
+            PeerExchange(None, cap, hidden, k, torch.device("cpu"))
