@@ -1,17 +1,21 @@
 """Benchmark of the MoE-layer hot path (H=2048, I=768, E=128, top-8, bf16).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
+                    [--ep-schedule c7|c6|c8] [--ep-transport peer|nccl] [--tp TP]
 
 One step = one MoE-layer forward over T tokens.  At N=1 the workload is the
 single-B200 fused MoE layer at T=16384 (router, sort, gather, w13+SwiGLU, w2,
 combine) through ``moe_layer_forward``; ``value`` is tokens/s with inputs
 resident in HBM, ``e2e`` the same through ``PermutedSparseMoE.forward`` with the
 input copied from pinned host memory and the output copied back inside the
-timed region.  At N>1 every rank runs the expert-parallel all_to_all schedule
-(``EPSparseMoE``, C7 semantics) on its own T tokens with E/N experts
-(weak scaling).  ``--impl reference`` times the reference algorithm's CPU
-restatement (the oracle) on the host cores on a bounded sample of the same
-workload.  Rank 0 prints one JSON line.
+timed region.  At N>1 every rank runs an expert-parallel schedule with E/N
+experts per rank: by default the all_to_all schedule (``EPSparseMoE``, C7
+semantics) on its own T=16384 tokens (weak scaling); ``--ep-schedule c6`` the
+replicated-input schedule with one all_reduce on T=4096 tokens, ``c8`` the
+hybrid TP x EP schedule on T=16384 tokens (8 sequences x 2048) with
+tp=``--tp`` (strong scaling, see ``ep_bench``).  ``--impl reference`` times
+the reference algorithm's CPU restatement (the oracle) on the host cores on a
+bounded sample of the same workload.  Rank 0 prints one JSON line.
 """
 
 from __future__ import annotations
@@ -187,9 +191,10 @@ def run_reference(args):
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
-        "ms_per_step": 1e3 * total / len(times), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
+        "scaling": "strong" if args.gpus > 1 and args.ep_schedule in ("c6", "c8") else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": config_block(T, args.gpus),
+        "config": config_block(T, args.gpus, args.ep_schedule, args.tp),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -200,14 +205,24 @@ def run_reference(args):
 # ----------------------------------------------------------------------------- GPU arm
 
 
-def config_block(T: int, n: int) -> dict:
+def config_block(T: int, n: int, schedule: str = "c7", tp: int = 1) -> dict:
+    per_rank = T
     if n == 1:
         wl = f"single-B200 fused MoE layer (C5/C9 path), T={T} tokens"
         par = "single"
+    elif schedule == "c6":
+        wl = (f"expert-parallel replicated-input MoE layer with one all_reduce (C6 path), "
+              f"{T} tokens replicated on every rank, E/{n} experts per rank")
+        par = f"ep{n} (replicated input)"
+    elif schedule == "c8":
+        per_rank = T // n
+        wl = (f"hybrid TP x EP MoE layer (C8 path), {T} tokens in all, tp={tp} x dp={n // tp}, "
+              f"a stripe of {per_rank} tokens per rank, E/{n} experts per rank, closing all_gather")
+        par = f"tp{tp}xdp{n // tp}=ep{n}"
     else:
         wl = f"expert-parallel all_to_all MoE layer (C7 path), {T} tokens per rank, E/{n} experts per rank"
         par = f"ep{n}"
-    return {"workload": wl, "tokens_per_rank": T, "hidden": H, "intermediate": I, "experts": E,
+    return {"workload": wl, "tokens_per_rank": per_rank, "hidden": H, "intermediate": I, "experts": E,
             "top_k": K_TOP, "routing": "uniform (router N(0,0.02), no bias)", "parallelism": par,
             "l2": "inputs larger than L2: 1.21 GB of expert weights streamed per step; "
                   "sweep: L2 flushed (512 MB write) before each timed replay"}
@@ -517,16 +532,28 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens per step: 16384 (N=1; per rank for c7; in all for c8), "
+                         "4096 replicated for c6")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="N>1: peer-store exchange over NVLink, or NCCL all_to_alls")
+    ap.add_argument("--ep-schedule", choices=["c7", "c6", "c8"], default="c7",
+                    help="N>1: all_to_all (c7), replicated + all_reduce (c6), hybrid TP x EP (c8)")
+    ap.add_argument("--tp", type=int, default=2, help="c8: tensor-parallel group size")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--sweep", default="1,16,128,1024,4096",
                     help="comma-separated token counts for the graph-captured sweep ('' = none)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    multi = int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.gpus > 1
+    if args.tokens is None:
+        args.tokens = 4096 if multi and args.ep_schedule == "c6" else 16384
+    if multi and args.ep_schedule == "c8":
+        n = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+        if args.tp < 1 or n % args.tp != 0 or args.tokens % n != 0:
+            ap.error(f"c8 needs tp dividing N={n} and tokens divisible by N")
     if args.impl == "reference":
         run_reference(args)
         return

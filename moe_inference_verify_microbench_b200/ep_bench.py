@@ -1,11 +1,21 @@
-"""Multi-GPU leg of ``bench.py``: the C7 expert-parallel schedule
-(``EPSparseMoE`` pure, all_to_all dispatch/combine; the peer-store exchange
-over NVLink by default, NCCL all_to_alls with ``--ep-transport nccl``) with T
-tokens per rank and E/N experts per rank, one process per GPU (weak scaling).
+"""Multi-GPU leg of ``bench.py``: one of the three expert-parallel schedules
+on N GPUs, one process per GPU, E/N experts per rank.
+
+* ``c7`` (default): ``EPSparseMoE`` pure (C7/python/solution.py:65-269),
+  all_to_all dispatch/combine with T tokens per rank (weak scaling); the
+  peer-store exchange over NVLink by default, NCCL all_to_alls with
+  ``--ep-transport nccl``.  ``value`` = N·T / step time.
+* ``c6``: ``EPSparseMoE`` lean (C6/python/solution.py:57-182), the same T
+  tokens replicated on every rank, local experts only, one NCCL all_reduce
+  of [T, H] (strong scaling).  ``value`` = T / step time.
+* ``c8``: ``HybridMoE`` (C8/python/solution.py:59-230) with tp × dp = N:
+  every TP group holds T/dp tokens, each rank runs the C7 core on its 1/tp
+  stripe (T/N tokens) and the TP group all_gathers the stripes (strong
+  scaling).  ``value`` = T / step time.
 
 Timing: W warm-up steps, then K steps bracketed by a barrier and a device
 synchronise on both sides, CUDA events on each rank's stream, the maximum
-over ranks.  ``value`` = N·T / that time.
+over ranks.
 """
 
 from __future__ import annotations
@@ -22,12 +32,29 @@ import torch.distributed as dist
 H, I, E, K_TOP = 2048, 768, 128, 8
 
 
-def _build(rank: int, world: int, dev: torch.device, T: int, transport: str):
-    from .ep_pure import EPSparseMoE
+def _build(rank: int, world: int, dev: torch.device, T: int, transport: str,
+           schedule: str = "c7", tp: int = 1):
+    """The schedule's module with seeded weights (the same global expert e gets
+    the same weights on every rank and in every schedule) and this rank's
+    input: T own tokens (c7), the T replicated tokens (c6), or the T/dp tokens
+    of its TP group (c8)."""
+    from .ep import EPSparseMoELean, EPSparseMoEPure, HybridMoE
 
+    x_rows, x_seed = T, 10 + rank
     with torch.device(dev):
-        mod = EPSparseMoE(H, I, E, K_TOP, world, rank, group=None, transport=transport,
-                          max_tokens_per_rank=T).to(torch.bfloat16)
+        if schedule == "c6":
+            mod = EPSparseMoELean(H, I, E, K_TOP, world, rank, group=None)
+            x_seed = 10  # replicated input
+        elif schedule == "c8":
+            # Every rank creates every TP group, in the same order.
+            groups = [dist.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(world // tp)]
+            mod = HybridMoE(H, I, E, K_TOP, tp, rank % tp, groups[rank // tp], world, rank, None,
+                            transport=transport, max_tokens_per_rank=T // world)
+            x_rows, x_seed = T // (world // tp), 10 + rank // tp  # replicated within TP
+        else:
+            mod = EPSparseMoEPure(H, I, E, K_TOP, world, rank, group=None, transport=transport,
+                                  max_tokens_per_rank=T)
+        mod = mod.to(torch.bfloat16)
     wg, wu, wd = mod.pack()
     g = torch.Generator(device=dev)
     with torch.no_grad():
@@ -37,8 +64,8 @@ def _build(rank: int, world: int, dev: torch.device, T: int, transport: str):
             for e in range(t.shape[0]):
                 g.manual_seed(1000 + 3 * (mod.expert_start + e) + (0 if t is wg else 1 if t is wu else 2))
                 t[e].copy_((torch.randn(t.shape[1:], generator=g, device=dev) * 0.02).to(torch.bfloat16))
-        g.manual_seed(10 + rank)  # distinct tokens per rank
-        x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
+        g.manual_seed(x_seed)
+        x = torch.randn(x_rows, H, generator=g, device=dev).to(torch.bfloat16)
     return mod, x
 
 
@@ -91,7 +118,9 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
 
     T = args.tokens
     transport = getattr(args, "ep_transport", "nccl")
-    mod, x = _build(rank, world, dev, T, transport)
+    schedule = getattr(args, "ep_schedule", "c7")
+    tp = getattr(args, "tp", 1) if schedule == "c8" else 1
+    mod, x = _build(rank, world, dev, T, transport, schedule, tp)
     stream = torch.cuda.current_stream(dev)
     with torch.no_grad():
         for _ in range(args.warmup):
@@ -117,11 +146,32 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
         ms_e2e = _timed(e2e_step, n_e2e, stream)
         clk = clocks.stop() if clocks is not None else None
         ops.check_status(dev)
-    mod.close()
+    close = getattr(mod, "close", None)
+    if close is not None:
+        close()
     ms_step = ms / args.steps
     if rank != 0:
         return
-    flop_rank = T * (2 * H * E + K_TOP * 6 * H * I)
+    # Expected FLOP per rank and tokens per step of the whole job.
+    if schedule == "c6":
+        # replicated router over all T tokens, 1/N of the expert records
+        flop_rank = T * 2 * H * E + T * K_TOP * 6 * H * I / world
+        job_tokens, scaling = T, "strong"
+        api = "EPSparseMoE.forward (C6 lean schedule, NCCL all_reduce)"
+        exchange = "NCCL all_reduce"
+        launches = 7  # router, sort (3), gate/up, down, masked combine
+    else:
+        rows = T if schedule == "c7" else T // world
+        flop_rank = rows * (2 * H * E + K_TOP * 6 * H * I)
+        job_tokens = world * T if schedule == "c7" else T
+        scaling = "weak" if schedule == "c7" else "strong"
+        api = (f"EPSparseMoE.forward (C7 schedule, transport={transport})" if schedule == "c7" else
+               f"HybridMoE.forward (C8 schedule, tp={tp}, transport={transport})")
+        exchange = f"{transport} exchange" + (" + NCCL all_gather" if schedule == "c8" else "")
+        # router, ep_keys, plan sort, local sort (3), gate/up, down, combine
+        # + (nccl) ep_meta, gather, partial combine
+        # + (peer) publish, dispatch, recv wait, return, return wait
+        launches = 14 if transport == "peer" else 12
     peaks = {}
     try:
         with open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
@@ -133,25 +183,26 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
         src = "fallback"
     peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
     achieved = flop_rank / (ms_step * 1e-3) / 1e12
+    config = config_block(T, world, schedule, tp)
+    if schedule != "c6":
+        config["ep_transport"] = transport
     line = {
-        "metric": metric, "value": world * T / (ms_step * 1e-3), "unit": "tokens/s",
+        "metric": metric, "value": job_tokens / (ms_step * 1e-3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded x~N(0,1) per rank, weights~N(0,0.02))",
-        "config": {**config_block(T, world), "ep_transport": transport},
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded x~N(0,1), weights~N(0,0.02))",
+        "config": config,
         "roofline": {"bound": "tensor",
-                     "kernel": f"whole EP layer per rank (compute + {transport} exchange)",
+                     "kernel": f"whole EP layer per rank (compute + {exchange})",
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                     "traffic": None, "peak_source": f"{src} bf16_tflops_sustained"},
-        "e2e": {"value": world * T * n_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": T * H * 2, "d2h_bytes_per_step": T * H * 2,
-                "api": f"EPSparseMoE.forward (C7 schedule, transport={transport})",
-                "steps": n_e2e, "copies": "pinned host, upload / forward / download in "
-                                          "turn on the compute stream; max over ranks"},
-        # our kernels per forward: router, ep_keys, plan sort, local sort (3),
-        # w13, w2, combine + (nccl) ep_meta, gather, partial combine
-        #                   + (peer) publish, dispatch, recv wait, return, return wait
-        "gpu_launches": (14 if transport == "peer" else 12) * args.steps,
+                     "traffic": None, "peak_source": f"{src} bf16_tflops_sustained",
+                     "algorithmic_per_launch": f"expected FLOP per rank per step = {flop_rank:.4g}"},
+        "e2e": {"value": job_tokens * n_e2e / (ms_e2e * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
+                "api": api, "steps": n_e2e,
+                "copies": "pinned host, upload / forward / download in turn on the compute "
+                          "stream; max over ranks; bytes per rank"},
+        "gpu_launches": launches * args.steps,
         "clocks": clk,
     }
     print(json.dumps(line), flush=True)
