@@ -10,7 +10,10 @@
  *   - writes device-side failures (expert id out of range, a bounded wait that
  *     ran out) into the caller's device status word `status` (int32, may be
  *     NULL); the first failure wins, 0 means none.  Read it after the stream
- *     has finished; moe_error_string() names both kinds of code.
+ *     has finished; moe_error_string() names both kinds of code;
+ *   - accepts an empty batch (T, M or R = 0): it returns 0 and launches
+ *     nothing, and the per-token / per-record buffers may then be NULL (an
+ *     empty torch tensor has no storage); weights and tile tables may not.
  * The caller owns all memory.  Scratch space is passed in as `workspace`, with
  * its size given by the matching *_workspace_bytes() query.
  *

@@ -339,14 +339,14 @@ int moe_layer_forward_ex(const void* x, const void* router_weight, const float* 
                          cudaStream_t stream) {
   if (combine_mode != MOE_COMBINE_SLOTS && combine_mode != MOE_COMBINE_ATOMIC)
     return kRcBadArgument;
-  if (x == nullptr || router_weight == nullptr || w_gate == nullptr || w_up == nullptr ||
-      w_down == nullptr || y == nullptr || workspace == nullptr || T < 0 || H <= 0 || I <= 0 ||
-      E <= 0 || top_k <= 0 || top_k > E)
+  if (router_weight == nullptr || w_gate == nullptr || w_up == nullptr || w_down == nullptr ||
+      T < 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0 || top_k > E)
     return kRcBadArgument;
+  if (T == 0) return kRcOk;  // empty batch: nothing to read or write, x and y may be NULL
+  if (x == nullptr || y == nullptr || workspace == nullptr) return kRcBadArgument;
   if (static_cast<long long>(T) * top_k > 0x7fffffffLL) return kRcUnsupported;
   if (workspace_bytes < moe_layer_workspace_bytes_ex(T, H, I, E, top_k, combine_mode))
     return kRcWorkspace;
-  if (T == 0) return kRcOk;
   int rc = kRcOk;
   layer_layout(T, H, I, E, top_k, combine_mode, workspace,
                [&](const LayerPlan& p, int* ids, float* w, void* sort_ws, int* counts,

@@ -165,7 +165,8 @@ int device_sm_count() { return device_sms(); }
 int launch_router(const void* x, const void* wr, const float* bias, int T, int H, int E, int k,
                   int norm_topk_prob, int* ids_out, float* w_out, void* logits_out, int* status,
                   cudaStream_t stream) {
-  if (x == nullptr || wr == nullptr || ids_out == nullptr || w_out == nullptr || T < 0 || H <= 0)
+  if ((T > 0 && (x == nullptr || ids_out == nullptr || w_out == nullptr)) || wr == nullptr ||
+      T < 0 || H <= 0)
     return kRcBadArgument;
   if ((H % kBK) != 0 || (E % 16) != 0 || E < 16 || E > 256 || k < 1 || k > kRouterMaxK || k > E)
     return kRcUnsupported;
@@ -199,8 +200,8 @@ int launch_router(const void* x, const void* wr, const float* bias, int T, int H
 int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_tiles, int max_tiles,
                       const void* w_gate, const void* w_up, int E, int H, int I, void* h_out,
                       int* status, cudaStream_t stream, int tile_rows) {
-  if (a == nullptr || tiles == nullptr || num_tiles == nullptr || w_gate == nullptr ||
-      w_up == nullptr || h_out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0)
+  if ((M > 0 && (a == nullptr || h_out == nullptr)) || tiles == nullptr || num_tiles == nullptr ||
+      w_gate == nullptr || w_up == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0)
     return kRcBadArgument;
   if (M == 0 || max_tiles == 0) return kRcOk;
   if (use_gemv_w13(M) && gemv_ok(I, H, true))
@@ -259,9 +260,9 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
                              const void* w_gate, const void* w_up, int E, int H, int I,
                              void* h_out, int* status, cudaStream_t stream, int tile_rows,
                              const void* w_down_prefetch) {
-  if (src == nullptr || tiles == nullptr || num_tiles == nullptr || w_gate == nullptr ||
-      w_up == nullptr || h_out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 ||
-      max_tiles < 0 || src_rows < 0 || index_div <= 0)
+  if ((M > 0 && (src == nullptr || h_out == nullptr)) || tiles == nullptr ||
+      num_tiles == nullptr || w_gate == nullptr || w_up == nullptr || M < 0 || E <= 0 || H <= 0 ||
+      I <= 0 || max_tiles < 0 || src_rows < 0 || index_div <= 0)
     return kRcBadArgument;
   if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0) return kRcBadArgument;
   if (M == 0 || max_tiles == 0) return kRcOk;
@@ -377,8 +378,8 @@ static int launch_w2_gemm(const void* h, int M, const int4* tiles, const int* nu
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
               void* out, int out_rows, int* status, cudaStream_t stream, int tile_rows) {
-  if (h == nullptr || tiles == nullptr || num_tiles == nullptr || w_down == nullptr ||
-      out == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0 || out_rows < 0)
+  if ((M > 0 && (h == nullptr || out == nullptr)) || tiles == nullptr || num_tiles == nullptr ||
+      w_down == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0 || out_rows < 0)
     return kRcBadArgument;
   if (M == 0 || max_tiles == 0) return kRcOk;
   if (use_gemv_w2(M) && gemv_ok(H, I, false))
@@ -392,9 +393,9 @@ int launch_w2_atomic(const void* h, int M, const int4* tiles, const int* num_til
                      int max_tiles, const void* w_down, int E, int H, int I, const int* row_map,
                      const float* row_scale, int n_slots, int red_div, float* out_f32,
                      int* status, cudaStream_t stream, int tile_rows) {
-  if (h == nullptr || tiles == nullptr || num_tiles == nullptr || w_down == nullptr ||
-      out_f32 == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0 ||
-      n_slots < 0 || red_div <= 0)
+  if ((M > 0 && (h == nullptr || out_f32 == nullptr)) || tiles == nullptr ||
+      num_tiles == nullptr || w_down == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 ||
+      max_tiles < 0 || n_slots < 0 || red_div <= 0)
     return kRcBadArgument;
   if ((reinterpret_cast<uintptr_t>(out_f32) & 15u) != 0) return kRcBadArgument;
   if (M == 0 || max_tiles == 0) return kRcOk;

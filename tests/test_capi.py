@@ -71,6 +71,32 @@ def test_null_arguments_rejected_without_launch():
                               None, None, None) == -1
 
 
+def test_empty_batch_accepted_without_launch():
+    """T, M or R = 0: every entry point returns 0 before any CUDA call, and the
+    per-token buffers may be NULL (an empty torch tensor has no storage), as
+    the reference's C5 forward accepts an empty batch; weights stay required
+    and a positive count with a NULL buffer is still refused."""
+    lib = _native.load()
+    w = ctypes.c_void_p(256)  # stand-in weight / table address, never dereferenced
+    H, I, E, k = 256, 128, 16, 4
+    assert lib.moe_layer_forward(None, w, None, w, w, w, 0, H, I, E, k, 1, None, 0, None,
+                                 None, None) == 0
+    assert lib.moe_layer_forward_ex(None, w, None, w, w, w, 0, H, I, E, k, 1, 1, None, 0, None,
+                                    None, None) == 0
+    assert lib.moe_layer_forward(None, None, None, w, w, w, 0, H, I, E, k, 1, None, 0, None,
+                                 None, None) == -1
+    assert lib.moe_router_topk(None, w, None, 0, H, E, k, 1, None, None, None, None, None) == 0
+    assert lib.moe_router_topk(None, w, None, 3, H, E, k, 1, None, None, None, None, None) == -1
+    assert lib.moe_grouped_w13_swiglu(None, 0, w, w, E, w, w, E, H, I, None, None, None) == 0
+    assert lib.moe_grouped_w13_swiglu(None, 5, w, w, E, w, w, E, H, I, None, None, None) == -1
+    assert lib.moe_grouped_w13_swiglu_gather(None, 0, None, k, 0, w, w, E, w, w, E, H, I, None,
+                                             None, None) == 0
+    assert lib.moe_grouped_w2(None, 0, w, w, E, w, E, H, I, None, None, None, 0, None,
+                              None) == 0
+    assert lib.moe_grouped_w2(None, 0, w, w, E, None, E, H, I, None, None, None, 0, None,
+                              None) == -1
+
+
 def test_index_add_mode_is_validated():
     import torch
     from moe_inference_verify_microbench_b200 import PermutedSparseMoE, ops

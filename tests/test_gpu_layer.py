@@ -271,3 +271,27 @@ def test_grouped_w2_atomic_op(cuda):
         ref = sl.float().reshape(T, k, H).sum(1)
         assert mo.rel_err(acc.cpu().numpy(), ref.cpu().numpy()) <= 1e-2, rows
         assert mo.rel_err(to_f32(y_at), to_f32(y_det)) <= 1e-2, rows
+
+
+def test_empty_batch(cuda):
+    """T = 0 through every drop-in: empty CUDA tensors (no storage, NULL data
+    pointer) give empty results and no device error, as the reference's C5
+    forward does for an empty batch."""
+    H, I, E, k = 256, 128, 16, 4
+    d = mo.make_inputs(1, H, I, E, seed=3)
+    wr, wg, wu, wd = (to_t(d[n], cuda) for n in ("wr", "w_gate", "w_up", "w_down"))
+    x0 = torch.empty((0, H), dtype=torch.bfloat16, device=cuda)
+    assert ops.moe_layer(x0, wr, wg, wu, wd, top_k=k).shape == (0, H)
+    assert ops.moe_layer(x0, wr, wg, wu, wd, top_k=k, index_add="atomic").shape == (0, H)
+    ids, w = ops.router_topk(x0, wr, k)[:2]
+    assert ids.shape == (0, k) and w.shape == (0, k)
+    s = ops.sort_align(ids, E, want_inv=True)
+    torch.cuda.synchronize()
+    assert int(s.num_tiles.item()) == 0
+    assert not s.counts.any() and not s.offsets.any()
+    mod = PermutedSparseMoE(H, I, E, k).to(device=cuda, dtype=torch.bfloat16)
+    with torch.no_grad():
+        assert mod(torch.empty((2, 0, H), dtype=torch.bfloat16, device=cuda)).shape == (2, 0, H)
+    y = fused_moe_forward(x0, torch.zeros(E + 1, dtype=torch.int64, device=cuda), wg, wu, wd)
+    assert y.shape == (0, H)
+    ops.check_status(cuda)
