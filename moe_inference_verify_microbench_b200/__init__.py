@@ -4,8 +4,8 @@ reference's components: ``PermutedSparseMoE`` (C5), ``fused_moe_forward``
 all_to_all) and ``HybridMoE`` (C8).  The kernels live in ``libmoe_b200.so``
 behind the C ABI of ``include/moe_b200.h``."""
 
-from .experts import SwiGLU_MLP
+from .experts import SwiGLU_MLP, load_qwen3_moe_layer
 from .fused_moe import fused_moe_forward
 from .permuted_moe import PermutedSparseMoE
 
-__all__ = ["PermutedSparseMoE", "SwiGLU_MLP", "fused_moe_forward"]
+__all__ = ["PermutedSparseMoE", "SwiGLU_MLP", "fused_moe_forward", "load_qwen3_moe_layer"]

@@ -81,3 +81,59 @@ def router_bias_of(gate: nn.Linear) -> torch.Tensor | None:
     workload swaps in an ``nn.Linear(bias=True)``); the reference gate has none."""
     b = getattr(gate, "bias", None)
     return None if b is None else b.detach().float().contiguous()
+
+
+def qwen3_moe_layer_weights(state_dict, layer: int, num_experts: int,
+                            prefix: str = "model.layers."):
+    """One MoE layer's tensors from a Hugging Face Qwen3-MoE-style state dict
+    (``{prefix}{layer}.mlp.gate.weight`` [E, H] and
+    ``{prefix}{layer}.mlp.experts.{e}.{gate,up,down}_proj.weight``), returned as
+    the argument lists of the reference's ``weight_loader``
+    (C6/python/solution.py:98-110): ``(router, gate_list, up_list, down_list)``.
+    ``state_dict`` only needs ``__getitem__`` (a dict, or a lazy mapping over
+    checkpoint shards); nothing is copied here."""
+    base = f"{prefix}{layer}.mlp."
+
+    def get(name):
+        try:
+            return state_dict[base + name]
+        except KeyError:
+            raise KeyError(f"the state dict has no {base + name!r}") from None
+
+    router = get("gate.weight")
+    gate = [get(f"experts.{e}.gate_proj.weight") for e in range(num_experts)]
+    up = [get(f"experts.{e}.up_proj.weight") for e in range(num_experts)]
+    down = [get(f"experts.{e}.down_proj.weight") for e in range(num_experts)]
+    return router, gate, up, down
+
+
+@torch.no_grad()
+def load_qwen3_moe_layer(module: nn.Module, state_dict, layer: int,
+                         prefix: str = "model.layers.") -> None:
+    """Copy one Qwen3-MoE layer of a checkpoint into a drop-in MoE module:
+    ``PermutedSparseMoE`` (all experts), or an expert-parallel module
+    (``EPSparseMoE`` lean / pure, ``HybridMoE``: the replicated router and this
+    rank's expert shard, through its ``weight_loader``).  The expert weights
+    land in the module's stacked [E, I, H] / [E, H, I] tensors, the layout the
+    grouped GEMMs read, with no second copy.  Shapes are checked against the
+    module before anything is copied."""
+    E, H, I = module.num_experts, module.hidden, module.intermediate
+    router, gate, up, down = qwen3_moe_layer_weights(state_dict, layer, E, prefix)
+    want = [("gate.weight", router, (E, H))]
+    for e in range(E):
+        want += [(f"experts.{e}.gate_proj.weight", gate[e], (I, H)),
+                 (f"experts.{e}.up_proj.weight", up[e], (I, H)),
+                 (f"experts.{e}.down_proj.weight", down[e], (H, I))]
+    for name, t, shape in want:
+        if tuple(t.shape) != shape:
+            raise ValueError(f"{prefix}{layer}.mlp.{name} has shape {tuple(t.shape)}, "
+                             f"the module expects {shape}")
+    if hasattr(module, "weight_loader"):
+        module.weight_loader(router, gate, up, down)
+        return
+    module.gate.weight.copy_(router)
+    wg, wu, wd = module.pack()
+    for e in range(E):
+        wg[e].copy_(gate[e])
+        wu[e].copy_(up[e])
+        wd[e].copy_(down[e])
