@@ -81,7 +81,7 @@ def run_ep(args, metric, config_block, clock_sampler_cls) -> None:
     saved = os.dup(1)
     os.dup2(2, 1)
     try:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
         dist.barrier()
         torch.cuda.synchronize()
     finally:
