@@ -11,9 +11,11 @@
  *     ran out) into the caller's device status word `status` (int32, may be
  *     NULL); the first failure wins, 0 means none.  Read it after the stream
  *     has finished; moe_error_string() names both kinds of code;
- *   - accepts an empty batch (T, M or R = 0): it returns 0 and launches
- *     nothing, and the per-token / per-record buffers may then be NULL (an
- *     empty torch tensor has no storage); weights and tile tables may not.
+ *   - accepts an empty batch (T, M or R = 0) and returns 0; the per-token /
+ *     per-record buffers may then be NULL (an empty torch tensor has no
+ *     storage), weights and tile tables may not.  Nothing is launched,
+ *     except where fixed-size outputs remain to be written (the sort still
+ *     writes zero counts, offsets and tile count).
  * The caller owns all memory.  Scratch space is passed in as `workspace`, with
  * its size given by the matching *_workspace_bytes() query.
  *
