@@ -97,6 +97,18 @@ def test_empty_batch_accepted_without_launch():
                               None) == -1
 
 
+def test_record_count_beyond_int32_is_refused_without_launch():
+    """T * k routing records must fit the kernels' 32-bit record indices: a
+    larger layer call returns MOE_RC_UNSUPPORTED before any pointer is used."""
+    lib = _native.load()
+    p = ctypes.c_void_p(256)  # stand-in addresses, never dereferenced
+    T = (1 << 31) // 8        # T * 8 = 2^31 records: one past the int32 range
+    assert lib.moe_layer_forward(p, p, None, p, p, p, T, 2048, 768, 128, 8, 1, p, 1 << 62, p,
+                                 None, None) == -2
+    assert lib.moe_layer_forward(p, p, None, p, p, p, T - 1, 2048, 768, 128, 8, 1, p, 0, p,
+                                 None, None) == -5  # fits: then the workspace size is checked
+
+
 def test_index_add_mode_is_validated():
     import torch
     from moe_inference_verify_microbench_b200 import PermutedSparseMoE, ops
