@@ -97,6 +97,20 @@ def run_ep(args, metric, config_block, clock_sampler_cls) -> None:
         dist.destroy_process_group()
 
 
+def schedule_work(schedule: str, T: int, world: int):
+    """(expected FLOP per rank, tokens of the whole job, scaling kind) of one
+    step.  c7: every rank routes and computes its own T tokens (a rank's
+    experts receive T·k records on average); c6: every rank routes all T
+    replicated tokens and computes 1/N of their records; c8: every rank routes
+    and computes its stripe of T/N tokens."""
+    per_token = 2 * H * E + K_TOP * 6 * H * I
+    if schedule == "c6":
+        return T * 2 * H * E + T * K_TOP * 6 * H * I / world, T, "strong"
+    if schedule == "c8":
+        return (T // world) * per_token, T, "strong"
+    return T * per_token, world * T, "weak"
+
+
 def _timed(fn, steps, stream):
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
@@ -152,19 +166,12 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
     ms_step = ms / args.steps
     if rank != 0:
         return
-    # Expected FLOP per rank and tokens per step of the whole job.
+    flop_rank, job_tokens, scaling = schedule_work(schedule, T, world)
     if schedule == "c6":
-        # replicated router over all T tokens, 1/N of the expert records
-        flop_rank = T * 2 * H * E + T * K_TOP * 6 * H * I / world
-        job_tokens, scaling = T, "strong"
         api = "EPSparseMoE.forward (C6 lean schedule, NCCL all_reduce)"
         exchange = "NCCL all_reduce"
         launches = 7  # router, sort (3), gate/up, down, masked combine
     else:
-        rows = T if schedule == "c7" else T // world
-        flop_rank = rows * (2 * H * E + K_TOP * 6 * H * I)
-        job_tokens = world * T if schedule == "c7" else T
-        scaling = "weak" if schedule == "c7" else "strong"
         api = (f"EPSparseMoE.forward (C7 schedule, transport={transport})" if schedule == "c7" else
                f"HybridMoE.forward (C8 schedule, tp={tp}, transport={transport})")
         exchange = f"{transport} exchange" + (" + NCCL all_gather" if schedule == "c8" else "")

@@ -91,3 +91,21 @@ def test_bench_config_names_the_schedule(sched, tp, per_rank, par):
     c = bench.config_block(T, 4, sched, tp)
     assert c["tokens_per_rank"] == per_rank and c["parallelism"] == par
     assert sched.upper() in c["workload"]
+
+
+def test_roofline_arithmetic_matches_the_per_token_figures():
+    """The FLOP counts behind every bench line's roofline: 76,021,760 FLOP per
+    token for the layer (2·H·E router + 8 × 6·H·I experts), bytes = 9,437,184
+    per active expert + the router weights + x read and y written."""
+    sys.path.insert(0, os.path.dirname(HERE))
+    import bench
+    from moe_inference_verify_microbench_b200.ep_bench import schedule_work
+    assert bench.layer_flops(1) == 76_021_760
+    assert bench.layer_flops(16384) == 16384 * 76_021_760
+    assert bench.layer_bytes(128, 16384) == 128 * 9_437_184 + 524_288 + 4 * 16384 * 2048
+    assert bench.layer_launches(16384, 256) == 7 and bench.layer_launches(64, 128) == 5
+    assert schedule_work("c7", 16384, 4) == (16384 * 76_021_760, 4 * 16384, "weak")
+    f6, t6, s6 = schedule_work("c6", 4096, 4)
+    assert (t6, s6) == (4096, "strong")
+    assert f6 == 4096 * 2 * 2048 * 128 + 4096 * 8 * 6 * 2048 * 768 / 4
+    assert schedule_work("c8", 16384, 4) == (4096 * 76_021_760, 16384, "strong")
