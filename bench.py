@@ -245,10 +245,14 @@ class Timer:
         return self.a.elapsed_time(self.b)
 
 
-# DRAM bytes (read + write) of one launch of the gate/up GEMM at the bench
-# workload, from the one-pass ncu capture summarised in
-# profiles/w13_pair_gather_t16384.md.
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# the gate/up GEMM at T=16384, taken from an ncu capture of that kernel on
+# B200 (not measured by this script: CUDA events cannot count DRAM bytes).
+# The weight bytes do not grow with T, so no other size is scaled from it.
 W13_TRAFFIC = {(16384, 256): 1211178240 + 192313344}
+W13_TRAFFIC_SOURCE = ("ncu capture of the same kernel at T=16384 "
+                      "(dram__bytes_read.sum + dram__bytes_write.sum, one launch); "
+                      "a recorded constant, not measured in this run")
 
 
 def w13_kernel_name(tile_rows):
@@ -257,12 +261,31 @@ def w13_kernel_name(tile_rows):
     return "grouped_gemm_kernel<BN,SwiGLU,stages,gather> (w13)"
 
 
-def layer_launches(T, tile_rows):
-    """Kernels moe_layer_forward launches for T tokens (large-batch path):
-    router, sort (one kernel up to 2048 records, else three), gate/up with the
-    gather fused, down, combine."""
+SORT_CHUNK, SORT_THREADS, CLUSTER_SORT_MAX, CLUSTER_CHUNK = 2048, 256, 8, 4096
+GEMV_W13_MAX_ROWS, ROUTER_SMALL_MAX_T = 128, 16
+
+
+def sort_launches(R: int, e_local: int = E) -> int:
+    """Kernels launch_sort_align issues for R records: one (single-CTA sort up
+    to one 2048-record chunk, or one cluster of <= 8 CTAs of <= 4096 records
+    each, i.e. R <= 32768) or three (histogram, scan, scatter)."""
+    if R <= SORT_CHUNK and e_local <= SORT_THREADS:
+        return 1
+    chunk = -(-R // CLUSTER_SORT_MAX)
+    chunk = -(-chunk // SORT_THREADS) * SORT_THREADS
+    return 1 if chunk <= CLUSTER_CHUNK and e_local <= SORT_THREADS else 3
+
+
+def layer_launches(T, tile_rows=None):
+    """Kernels moe_layer_forward launches for T tokens.  Decode (T*k <= 128
+    records): router and sort fused in one kernel for T <= 16, the gate/up
+    weight-streaming kernel, the down GEMV or GEMM, the combine.  Otherwise:
+    router, sort (``sort_launches``), gate/up GEMM with the row gather fused,
+    down GEMM, combine."""
     R = T * K_TOP
-    return 1 + (1 if R <= 2048 else 3) + 1 + 1 + 1
+    if 0 < R <= GEMV_W13_MAX_ROWS:
+        return (1 if T <= ROUTER_SMALL_MAX_T else 1 + sort_launches(R)) + 3
+    return 1 + sort_launches(R) + 3
 
 
 def e2e_pipelined(mod, x_host, dev, n_steps):
@@ -383,6 +406,8 @@ def run_ours_single(args):
         "roofline": {"bound": "tensor", "kernel": w13_kernel_name(tile_rows),
                      "achieved": w13_tflops, "peak": peak_tc, "unit": "TFLOP/s",
                      "frac": w13_tflops / peak_tc, "traffic": W13_TRAFFIC.get((T, tile_rows)),
+                     "traffic_source": (W13_TRAFFIC_SOURCE if (T, tile_rows) in W13_TRAFFIC
+                                        else "no ncu capture at this size"),
                      "peak_source": f"{peak_kind} bf16_tflops_sustained",
                      "algorithmic_per_launch": f"2*T*k*(2I)*H = {w13_flop:.4g} FLOP"},
         "layer_roofline": {"t_roof_ms": t_roof * 1e3, "frac": t_roof * 1e3 / ms_step,

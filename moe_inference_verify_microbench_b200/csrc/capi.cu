@@ -241,6 +241,8 @@ size_t moe_layer_workspace_bytes(int T, int H, int I, int E, int top_k) {
 size_t moe_layer_workspace_bytes_ex(int T, int H, int I, int E, int top_k, int combine_mode) {
   if (T < 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0) return 0;
   if (combine_mode != MOE_COMBINE_SLOTS && combine_mode != MOE_COMBINE_ATOMIC) return 0;
+  // The layer refuses more than 2^31 - 1 routing records; so does its size query.
+  if (static_cast<long long>(T) * top_k > 0x7fffffffLL) return 0;
   return layer_layout(T, H, I, E, top_k, combine_mode, nullptr, [](auto&&...) {});
 }
 

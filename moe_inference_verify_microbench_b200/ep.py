@@ -20,6 +20,18 @@ variable all_to_all, whose split sizes the host must read (the reference's
 ``.tolist()``, C7:199-200); with ``transport="peer"`` (C7 and C8) the ranks
 write into each other's buffers over NVLink with the split sizes negotiated on
 the device (``peer.PeerExchange``): no host synchronisation in the forward.
+
+Errors.  With the keyword extra ``check_errors=True`` every forward
+synchronises and raises ``ops.MoEKernelError`` when a kernel reported a
+failure in the device status word (an expert id out of range, a peer that did
+not signal in time); otherwise failures are only recorded there
+(``ops.check_status``).  A peer timeout seen that way marks the exchange
+unusable: its ranks' epochs may no longer agree, so later forwards raise
+until ``close()`` (collective) and a new forward rebuild it.  A forward whose
+batch exceeds the peer capacity (``max_tokens_per_rank``, or the largest
+per-rank batch of the first forward) still takes its part in the exchange
+step, with an empty batch, so the other ranks' results stay correct and every
+rank stays in step, and then raises ``ValueError``.
 """
 
 from __future__ import annotations
@@ -117,9 +129,10 @@ class EPSparseMoELean(_EPBase):
 
     def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int, ep_size: int,
                  ep_rank: int, group: dist.ProcessGroup | None = None,
-                 norm_topk_prob: bool = True) -> None:
+                 norm_topk_prob: bool = True, *, check_errors: bool = False) -> None:
         super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
         self.group = group
+        self.check_errors = check_errors
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         K = self._kernels
@@ -138,6 +151,8 @@ class EPSparseMoELean(_EPBase):
         partial = K.combine(slots, N, k, ids=ids.reshape(-1),          # (C6:175-176)
                             e_range=(self.expert_start, self.expert_end))
         dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)  # (C6:180)
+        if self.check_errors:
+            ops.check_status(partial.device)
         return partial.reshape(shape)
 
 
@@ -214,11 +229,13 @@ def dispatch_combine_peer(mod: _EPBase, local_x: torch.Tensor, px: PeerExchange)
 class _A2ABase(_EPBase):
     """Transport selection shared by the all_to_all schedules."""
 
-    def _init_transport(self, transport: str, max_tokens_per_rank: int | None) -> None:
+    def _init_transport(self, transport: str, max_tokens_per_rank: int | None,
+                        check_errors: bool) -> None:
         if transport not in TRANSPORTS:
             raise ValueError(f"transport must be one of {TRANSPORTS}, got {transport!r}")
         self.transport = transport
         self.max_tokens_per_rank = max_tokens_per_rank
+        self.check_errors = check_errors
         self._peer: PeerExchange | None = None
 
     def _exchange(self, local_x: torch.Tensor, group) -> torch.Tensor:
@@ -232,7 +249,31 @@ class _A2ABase(_EPBase):
                 n_max = max(_all_gather(local_x.shape[0], group))
             self._peer = PeerExchange(group, self.ep_size * int(n_max), self.hidden, self.top_k,
                                       local_x.device)
-        return dispatch_combine_peer(self, local_x, self._peer)
+        px = self._peer
+        if getattr(px, "broken", False):
+            raise RuntimeError("the peer exchange timed out in an earlier forward and its ranks "
+                               "may be out of step; call close() on every rank to rebuild it")
+        if local_x.shape[0] * self.ep_size > px.cap_rows:
+            # Refusing before the exchange would leave the peers waiting for this
+            # rank's step until they time out, and this rank one epoch behind them
+            # for good.  Take part with an empty batch instead, then refuse.
+            dispatch_combine_peer(self, local_x[:0], px)
+            raise ValueError(f"{local_x.shape[0]} tokens on this rank exceed the peer exchange "
+                             f"capacity of {px.cap_rows // self.ep_size} tokens per rank; this "
+                             "rank sent nothing in this step (the other ranks' results are "
+                             "complete); pass max_tokens_per_rank to size the exchange")
+        return dispatch_combine_peer(self, local_x, px)
+
+    def _checked(self, y: torch.Tensor) -> torch.Tensor:
+        if not self.check_errors:
+            return y
+        try:
+            ops.check_status(y.device)
+        except ops.MoEKernelError as err:
+            if err.code == ops.ERR_PEER_TIMEOUT and self._peer is not None:
+                self._peer.broken = True
+            raise
+        return y
 
     def close(self) -> None:
         """Collective with the peer transport: unmap and free the peer buffers."""
@@ -250,15 +291,15 @@ class EPSparseMoEPure(_A2ABase):
     def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int, ep_size: int,
                  ep_rank: int, group: dist.ProcessGroup | None = None,
                  norm_topk_prob: bool = True, *, transport: str = "nccl",
-                 max_tokens_per_rank: int | None = None) -> None:
+                 max_tokens_per_rank: int | None = None, check_errors: bool = False) -> None:
         super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
         self.ep_group = group
-        self._init_transport(transport, max_tokens_per_rank)
+        self._init_transport(transport, max_tokens_per_rank, check_errors)
 
     def forward(self, local_x: torch.Tensor) -> torch.Tensor:
         shape = local_x.shape
         x_flat = local_x.reshape(-1, self.hidden).contiguous()
-        return self._exchange(x_flat, self.ep_group).reshape(shape)
+        return self._checked(self._exchange(x_flat, self.ep_group)).reshape(shape)
 
 
 class HybridMoE(_A2ABase):
@@ -268,13 +309,14 @@ class HybridMoE(_A2ABase):
     def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int, tp_size: int,
                  tp_rank: int, tp_group: dist.ProcessGroup | None, ep_size: int, ep_rank: int,
                  ep_group: dist.ProcessGroup | None, norm_topk_prob: bool = True, *,
-                 transport: str = "nccl", max_tokens_per_rank: int | None = None) -> None:
+                 transport: str = "nccl", max_tokens_per_rank: int | None = None,
+                 check_errors: bool = False) -> None:
         super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
         self.tp_size = tp_size
         self.tp_rank = tp_rank
         self.tp_group = tp_group
         self.ep_group = ep_group
-        self._init_transport(transport, max_tokens_per_rank)
+        self._init_transport(transport, max_tokens_per_rank, check_errors)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape
@@ -283,7 +325,7 @@ class HybridMoE(_A2ABase):
         assert N_tp % self.tp_size == 0
         local_N = N_tp // self.tp_size
         local_x = x_flat[self.tp_rank * local_N:(self.tp_rank + 1) * local_N].contiguous()  # (C8:160)
-        local_y = self._exchange(local_x, self.ep_group)
+        local_y = self._checked(self._exchange(local_x, self.ep_group))
         y_flat = torch.empty((N_tp, self.hidden), dtype=local_y.dtype, device=local_y.device)
         dist.all_gather_into_tensor(y_flat, local_y, group=self.tp_group)            # (C8:227)
         return y_flat.reshape(shape)

@@ -19,7 +19,16 @@ BLOCK_M = 128
 
 
 class MoEKernelError(RuntimeError):
-    pass
+    """A C-ABI call refused its arguments (``code`` < 0, a MOE_RC_* value) or a
+    kernel reported a failure in the device status word (``code`` > 0, a
+    MOE_ERR_* value)."""
+
+    def __init__(self, message: str, code: int = 0) -> None:
+        super().__init__(message)
+        self.code = code
+
+
+ERR_PEER_TIMEOUT = 0x105  # MOE_ERR_PEER_TIMEOUT
 
 
 _status: dict[int, torch.Tensor] = {}
@@ -36,14 +45,19 @@ def status_word(device: torch.device) -> torch.Tensor:
 
 
 def check_status(device: torch.device | None = None, reset: bool = True) -> None:
-    """Synchronise and raise if any kernel on ``device`` reported an error."""
+    """Synchronise and raise ``MoEKernelError`` if any kernel on ``device``
+    reported an error (then the word is cleared unless ``reset`` is False).
+    The modules call this after every forward when built with
+    ``check_errors=True``; otherwise a device-side failure (an expert id out of
+    range, a bounded wait that ran out) is only recorded, and the forward's
+    output is not to be trusted until the caller has checked."""
     device = device or torch.device("cuda", torch.cuda.current_device())
     st = status_word(device)
     code = int(st.item())
     if reset and code:
         st.zero_()
     if code:
-        raise MoEKernelError(f"device status 0x{code:x}: {_native.error_string(code)}")
+        raise MoEKernelError(f"device status 0x{code:x}: {_native.error_string(code)}", code)
 
 
 def _p(t: torch.Tensor | None) -> ctypes.c_void_p | None:
@@ -69,7 +83,7 @@ def _need(t: torch.Tensor, name: str, dtype: torch.dtype, ndim: int | None = Non
 
 def _rc(rc: int, what: str) -> None:
     if rc != 0:
-        raise MoEKernelError(f"{what}: {_native.error_string(rc)} (rc={rc})")
+        raise MoEKernelError(f"{what}: {_native.error_string(rc)} (rc={rc})", rc)
 
 
 # --------------------------------------------------------------------------- router

@@ -77,6 +77,9 @@ class PeerExchange:
         self.cap_rows, self.hidden, self.top_k = int(cap_rows), int(hidden), int(top_k)
         self.device = torch.device(device)
         self.group = group
+        # Set by the expert-parallel modules when a forward saw a peer timeout:
+        # the ranks' epochs may disagree from then on, so the exchange is not reused.
+        self.broken = False
         lib = _native.load()
         self._lib = lib
         nbytes = int(lib.moe_ep_peer_buffer_bytes(self.ep, self.cap_rows, hidden, top_k))

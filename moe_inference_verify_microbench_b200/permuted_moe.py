@@ -8,7 +8,11 @@ GEMM with the top-k weight fused, and a deterministic k-way combine.  It
 issues no host synchronisation (the reference syncs once per expert on
 ``.item()``, C5:144).  The keyword extra ``index_add="atomic"`` switches the
 un-permute to the reference's own semantics (index_add_, C5:160: fp32 atomic
-accumulation per token, fused into the down GEMM).
+accumulation per token, fused into the down GEMM).  With the keyword extra
+``check_errors=True`` every forward synchronises and raises
+``ops.MoEKernelError`` if a kernel reported a failure in the device status
+word; by default the forward never synchronises and a failure is only
+recorded there (``ops.check_status`` reads it).
 
 The module must be bf16 on a CUDA device: there is no CPU path.
 """
@@ -28,10 +32,12 @@ class PermutedSparseMoE(nn.Module):
     """Single-GPU sparse MoE with permutation + grouped compute (C5:82-161)."""
 
     def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int,
-                 norm_topk_prob: bool = True, *, index_add: str = "deterministic") -> None:
+                 norm_topk_prob: bool = True, *, index_add: str = "deterministic",
+                 check_errors: bool = False) -> None:
         super().__init__()
         ops._combine_mode(index_add)  # validate
         self.index_add = index_add
+        self.check_errors = check_errors
         self.hidden = hidden
         self.intermediate = intermediate
         self.num_experts = num_experts
@@ -58,4 +64,6 @@ class PermutedSparseMoE(nn.Module):
         wg, wu, wd = self.pack()
         y = ops.moe_layer(x_flat, self.gate.weight, wg, wu, wd, self.top_k, self.norm_topk_prob,
                           bias=router_bias_of(self.gate), index_add=self.index_add)
+        if self.check_errors:
+            ops.check_status(y.device)
         return y.reshape(shape)

@@ -108,7 +108,7 @@ class CpuContractKernels:
             e = ids.reshape(-1).long()
             valid &= (e >= e_range[0]) & (e < e_range[1])
         contrib = rows.float()[s.clamp(min=0)] * (w * valid)[:, None]
-        return contrib.reshape(T, k, -1).sum(1).to(torch.bfloat16)
+        return contrib.reshape(T, k, rows.shape[1]).sum(1).to(torch.bfloat16)
 
 
 class CpuPeerExchange:
@@ -124,6 +124,7 @@ class CpuPeerExchange:
         self.ep = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.cap_rows, self.hidden, self.top_k = cap_rows, hidden, top_k
+        self.broken = False
         self.recv_ids = torch.zeros((cap_rows, top_k), dtype=torch.int32)
         self.recv_w = torch.zeros((cap_rows, top_k), dtype=torch.float32)
         self.recv_rows = torch.zeros((cap_rows, hidden), dtype=torch.bfloat16)

@@ -3,7 +3,7 @@ suite itself (weidotwisc/moe_inference_verify_microbench) on CPU.
 
 Run in a container that has the reference checkout:
 
-    REFERENCE_ROOT=/root/reference python tests/golden/make_golden.py
+    REFERENCE_ROOT=<path of the reference checkout> python tests/golden/make_golden.py
 
 The reference imports helper modules it does not ship; ``_stubs/bootcamp``
 provides them, restated from their call sites.  Inputs come from
@@ -32,8 +32,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
-os.environ["REFERENCE_ROOT"] = REF
+REF = os.environ.get("REFERENCE_ROOT")
+if not REF or not os.path.isdir(REF):
+    sys.exit("set REFERENCE_ROOT to the reference checkout (the directory holding C5/ ... C9/)")
 sys.path.insert(0, os.path.join(HERE, "_stubs"))
 sys.path.insert(0, REPO)
 

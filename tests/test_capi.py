@@ -107,6 +107,11 @@ def test_record_count_beyond_int32_is_refused_without_launch():
                                  None, None) == -2
     assert lib.moe_layer_forward(p, p, None, p, p, p, T - 1, 2048, 768, 128, 8, 1, p, 0, p,
                                  None, None) == -5  # fits: then the workspace size is checked
+    # the size query refuses the same shapes (0) instead of a wrapped size
+    for mode in (0, 1):
+        assert lib.moe_layer_workspace_bytes_ex(T, 2048, 768, 128, 8, mode) == 0
+        assert lib.moe_layer_workspace_bytes_ex(T - 1, 2048, 768, 128, 8, mode) > 0
+    assert lib.moe_layer_workspace_bytes(T, 2048, 768, 128, 8) == 0
 
 
 def test_index_add_mode_is_validated():

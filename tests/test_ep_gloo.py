@@ -105,3 +105,72 @@ def test_peer_exchange_rejects_bad_shapes_before_touching_the_gpu():
     for hidden, k, cap in ((100, 8, 64), (2048, 9, 64), (2048, 8, -1)):
         with pytest.raises(ValueError):
             PeerExchange(None, cap, hidden, k, torch.device("cpu"))
+
+
+def _overcap_worker(rank, world, port, q):
+    """Rank 1 passes twice the tokens the peer exchange was sized for; rank 0
+    a batch within it.  Rank 1 must raise after taking part in the step (so
+    rank 0's result is complete and both ranks stay in step), and a second
+    forward within the capacity must then be correct on both ranks."""
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
+    from cpu_contract import CpuContractKernels, CpuPeerExchange
+    from helpers import load_golden, to_t
+    from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
+    from oracle import moe_oracle as mo
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        g = load_golden("ep_c7_w2.npz")
+        T, H, I, E, k = (int(g[n]) for n in ("T", "H", "I", "E", "k"))
+        d = mo.make_inputs(T * world, H, I, E, int(g["seed"]))
+        xall = to_t(d["x"])
+        mod = Pure(H, I, E, k, world, rank, group=None, transport="peer",
+                   max_tokens_per_rank=T).to(torch.bfloat16)
+        mod._kernels = CpuContractKernels
+        mod._peer = CpuPeerExchange(None, world * T, H, k)
+        mod.weight_loader(to_t(d["wr"]), [to_t(d["w_gate"][e]) for e in range(E)],
+                          [to_t(d["w_up"][e]) for e in range(E)],
+                          [to_t(d["w_down"][e]) for e in range(E)])
+        x = xall[rank * T:(rank + 1) * T]
+        yref = mo.f32_from_bf16_bits(g[f"y_rank{rank}"])
+        _, _, lg = CpuContractKernels.router_topk(x, mod.gate.weight, k)
+        srt = torch.sort(lg.float(), dim=-1, descending=True).values
+        keep = ~(srt[:, k - 1] == srt[:, k]).numpy()
+        out = {}
+        with torch.no_grad():
+            if rank == 1:
+                try:
+                    mod(torch.cat([x, x]))
+                    out["raised"] = False
+                except ValueError:
+                    out["raised"] = True
+            else:
+                y = mod(x)
+                out["err_first"] = mo.rel_err(y.float().numpy()[keep], yref[keep])
+            y = mod(x)
+            out["err_second"] = mo.rel_err(y.float().numpy()[keep], yref[keep])
+        q.put((rank, out))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_peer_batch_over_capacity_keeps_ranks_in_step():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29950
+    procs = [ctx.Process(target=_overcap_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[1]["raised"] is True
+    assert res[0]["err_first"] <= 2e-2
+    assert res[0]["err_second"] <= 2e-2 and res[1]["err_second"] <= 2e-2
