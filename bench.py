@@ -1,7 +1,7 @@
 """Benchmark of the MoE-layer hot path (H=2048, I=768, E=128, top-8, bf16).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T] [--impl ours|reference]
-                    [--ep-schedule c7|c6|c8] [--ep-transport peer|nccl] [--tp TP]
+                    [--ep-schedule c7|c6|c8] [--ep-transport peer|nccl] [--tp TP] [--zipf]
 
 One step = one MoE-layer forward over T tokens.  At N=1 the workload is the
 single-B200 fused MoE layer at T=16384 (router, sort, gather, w13+SwiGLU, w2,
@@ -194,7 +194,7 @@ def run_reference(args):
         "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
         "scaling": "strong" if args.gpus > 1 and args.ep_schedule in ("c6", "c8") else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": config_block(T, args.gpus, args.ep_schedule, args.tp),
+        "config": config_block(T, args.gpus, args.ep_schedule, args.tp, args.zipf),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -205,7 +205,7 @@ def run_reference(args):
 # ----------------------------------------------------------------------------- GPU arm
 
 
-def config_block(T: int, n: int, schedule: str = "c7", tp: int = 1) -> dict:
+def config_block(T: int, n: int, schedule: str = "c7", tp: int = 1, zipf: bool = False) -> dict:
     per_rank = T
     if n == 1:
         wl = f"single-B200 fused MoE layer (C5/C9 path), T={T} tokens"
@@ -223,7 +223,10 @@ def config_block(T: int, n: int, schedule: str = "c7", tp: int = 1) -> dict:
         wl = f"expert-parallel all_to_all MoE layer (C7 path), {T} tokens per rank, E/{n} experts per rank"
         par = f"ep{n}"
     return {"workload": wl, "tokens_per_rank": per_rank, "hidden": H, "intermediate": I, "experts": E,
-            "top_k": K_TOP, "routing": "uniform (router N(0,0.02), no bias)", "parallelism": par,
+            "top_k": K_TOP,
+            "routing": ("Zipf(1.2) skew: router N(0,0.02) + fp32 bias -1.2*ln(e+1)" if zipf
+                        else "uniform (router N(0,0.02), no bias)"),
+            "parallelism": par,
             "l2": "inputs larger than L2: 1.21 GB of expert weights streamed per step; "
                   "sweep: L2 flushed (512 MB write) before each timed replay"}
 
@@ -566,6 +569,8 @@ def main():
     ap.add_argument("--ep-schedule", choices=["c7", "c6", "c8"], default="c7",
                     help="N>1: all_to_all (c7), replicated + all_reduce (c6), hybrid TP x EP (c8)")
     ap.add_argument("--tp", type=int, default=2, help="c8: tensor-parallel group size")
+    ap.add_argument("--zipf", action="store_true",
+                    help="N>1: Zipf(1.2) router bias (the skewed-routing C7 configuration)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--sweep", default="1,16,128,1024,4096",
                     help="comma-separated token counts for the graph-captured sweep ('' = none)")

@@ -4,7 +4,9 @@ on N GPUs, one process per GPU, E/N experts per rank.
 * ``c7`` (default): ``EPSparseMoE`` pure (C7/python/solution.py:65-269),
   all_to_all dispatch/combine with T tokens per rank (weak scaling); the
   peer-store exchange over NVLink by default, NCCL all_to_alls with
-  ``--ep-transport nccl``.  ``value`` = N·T / step time.
+  ``--ep-transport nccl``; ``--zipf`` adds the Zipf(1.2) router bias of the
+  skewed configuration (2048 tokens per rank: ``--tokens 2048 --zipf``).
+  ``value`` = N·T / step time.
 * ``c6``: ``EPSparseMoE`` lean (C6/python/solution.py:57-182), the same T
   tokens replicated on every rank, local experts only, one NCCL all_reduce
   of [T, H] (strong scaling).  ``value`` = T / step time.
@@ -32,12 +34,21 @@ import torch.distributed as dist
 H, I, E, K_TOP = 2048, 768, 128, 8
 
 
+def zipf_router_bias(num_experts: int, s: float = 1.2) -> torch.Tensor:
+    """The skewed-routing workload's router bias b_e = -s * ln(e + 1) (fp32,
+    added to the logits before their bf16 rounding): expert e is picked with
+    Zipf(s)-like frequency, so the ranks owning the low expert ids receive
+    most of the rows."""
+    e = torch.arange(num_experts, dtype=torch.float64)
+    return (-s * torch.log(e + 1.0)).to(torch.float32)
+
+
 def _build(rank: int, world: int, dev: torch.device, T: int, transport: str,
-           schedule: str = "c7", tp: int = 1):
+           schedule: str = "c7", tp: int = 1, zipf: bool = False):
     """The schedule's module with seeded weights (the same global expert e gets
     the same weights on every rank and in every schedule) and this rank's
     input: T own tokens (c7), the T replicated tokens (c6), or the T/dp tokens
-    of its TP group (c8)."""
+    of its TP group (c8).  ``zipf``: the router carries the Zipf(1.2) bias."""
     from .ep import EPSparseMoELean, EPSparseMoEPure, HybridMoE
 
     x_rows, x_seed = T, 10 + rank
@@ -66,6 +77,11 @@ def _build(rank: int, world: int, dev: torch.device, T: int, transport: str,
                 t[e].copy_((torch.randn(t.shape[1:], generator=g, device=dev) * 0.02).to(torch.bfloat16))
         g.manual_seed(x_seed)
         x = torch.randn(x_rows, H, generator=g, device=dev).to(torch.bfloat16)
+        if zipf:
+            lin = torch.nn.Linear(H, E, bias=True, device=dev, dtype=torch.bfloat16)
+            lin.weight.copy_(mod.gate.weight)
+            lin.bias.copy_(zipf_router_bias(E).to(torch.bfloat16))
+            mod.gate = lin
     return mod, x
 
 
@@ -134,7 +150,8 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
     transport = getattr(args, "ep_transport", "nccl")
     schedule = getattr(args, "ep_schedule", "c7")
     tp = getattr(args, "tp", 1) if schedule == "c8" else 1
-    mod, x = _build(rank, world, dev, T, transport, schedule, tp)
+    zipf = bool(getattr(args, "zipf", False))
+    mod, x = _build(rank, world, dev, T, transport, schedule, tp, zipf)
     stream = torch.cuda.current_stream(dev)
     with torch.no_grad():
         for _ in range(args.warmup):
@@ -190,7 +207,7 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
         src = "fallback"
     peak = peaks.get("bf16_tflops_sustained") or peaks.get("bf16_tflops")
     achieved = flop_rank / (ms_step * 1e-3) / 1e12
-    config = config_block(T, world, schedule, tp)
+    config = config_block(T, world, schedule, tp, zipf)
     if schedule != "c6":
         config["ep_transport"] = transport
     line = {

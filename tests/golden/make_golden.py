@@ -18,7 +18,8 @@ Fixtures written:
 * ``c9_fp32.npz``           C9 fused_moe_forward under the Triton CPU interpreter in
                             fp32 (bf16 is wrong under the interpreter), ragged and
                             empty experts
-* ``ep_{c6,c7,c8}_*.npz``   C6 / C7 / C8-HybridMoE on gloo ranks; per-rank outputs
+* ``ep_{c6,c7,c8}_*.npz``   C6 / C7 / C8-HybridMoE on 2, 4 and 8 gloo ranks (C7 also with
+                            the Zipf router skew, C8 at tp=2 and tp=4); per-rank outputs
 """
 
 from __future__ import annotations
@@ -175,20 +176,39 @@ def run_ep(kind, world, tp=1, seed=0, zipf=False, port=29611):
     return out
 
 
+FIXTURES = {
+    "c5_small_s0.npz": lambda: run_c5(64, 128, 64, 16, 4, seed=0),
+    "c5_small_s1.npz": lambda: run_c5(64, 128, 64, 16, 4, seed=1),
+    "c5_small_nonorm.npz": lambda: run_c5(64, 128, 64, 16, 4, seed=2, norm=False),
+    "c5_full_t256.npz": lambda: run_c5(256, 2048, 768, 128, 8, seed=0, store_inputs=False),
+    "c9_fp32.npz": run_c9_fp32,
+    "ep_c6_w2.npz": lambda: run_ep("c6", 2, port=29611),
+    "ep_c6_w4.npz": lambda: run_ep("c6", 4, port=29612),
+    "ep_c7_w2.npz": lambda: run_ep("c7", 2, port=29613),
+    "ep_c7_w4_zipf.npz": lambda: run_ep("c7", 4, zipf=True, port=29614),
+    "ep_c8_w4_tp2.npz": lambda: run_ep("c8", 4, tp=2, port=29615),
+    # eight ranks: the expert-parallel configurations at their own world size
+    # (C6 ep=8; C7 dp=ep=8 with the Zipf router skew; C8 tp=2 x dp=4 and tp=4 x dp=2)
+    "ep_c6_w8.npz": lambda: run_ep("c6", 8, port=29616),
+    "ep_c7_w8_zipf.npz": lambda: run_ep("c7", 8, zipf=True, port=29617),
+    "ep_c8_w8_tp2.npz": lambda: run_ep("c8", 8, tp=2, port=29618),
+    "ep_c8_w8_tp4.npz": lambda: run_ep("c8", 8, tp=4, port=29619),
+}
+
+
 def main():
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="fixture file names to (re)write; default: all")
+    names = ap.parse_args().only or list(FIXTURES)
+    unknown = sorted(set(names) - set(FIXTURES))
+    if unknown:
+        sys.exit(f"unknown fixtures {unknown}; known: {sorted(FIXTURES)}")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
-    save = lambda name, d: np.savez_compressed(os.path.join(HERE, name), **d)  # noqa: E731
-    save("c5_small_s0.npz", run_c5(64, 128, 64, 16, 4, seed=0))
-    save("c5_small_s1.npz", run_c5(64, 128, 64, 16, 4, seed=1))
-    save("c5_small_nonorm.npz", run_c5(64, 128, 64, 16, 4, seed=2, norm=False))
-    save("c5_full_t256.npz", run_c5(256, 2048, 768, 128, 8, seed=0, store_inputs=False))
-    save("c9_fp32.npz", run_c9_fp32())
-    save("ep_c6_w2.npz", run_ep("c6", 2, port=29611))
-    save("ep_c6_w4.npz", run_ep("c6", 4, port=29612))
-    save("ep_c7_w2.npz", run_ep("c7", 2, port=29613))
-    save("ep_c7_w4_zipf.npz", run_ep("c7", 4, zipf=True, port=29614))
-    save("ep_c8_w4_tp2.npz", run_ep("c8", 4, tp=2, port=29615))
-    print("fixtures written to", HERE)
+    for name in names:
+        np.savez_compressed(os.path.join(HERE, name), **FIXTURES[name]())
+        print("wrote", name, flush=True)
 
 
 if __name__ == "__main__":

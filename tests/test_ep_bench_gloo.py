@@ -47,6 +47,14 @@ def _worker(rank, world, port, q):
             "err_c7": mo.rel_err(out["c7"][1], out["c6"][1]) if rank == 0 else 0.0,
             "err_c8": mo.rel_err(out["c8"][1], out["c6"][1]),
         }
+        # The skewed-routing C7 configuration: the router carries the Zipf bias,
+        # so the first rank's experts take most of the records.
+        mz, xz = eb._build(rank, world, dev, T_SMALL, "nccl", "c7", zipf=True)
+        bias = mz.gate.bias.float()
+        res["zipf_bias_ok"] = bool(torch.allclose(
+            bias, eb.zipf_router_bias(E_SMALL).to(torch.bfloat16).float()))
+        ids, _, _ = CpuContractKernels.router_topk(xz, mz.gate.weight, 4, bias=mz.gate.bias)
+        res["zipf_low_share"] = float((ids < E_SMALL // world).float().mean())
         gathered = [None] * world
         dist.all_gather_object(gathered, [xs["c6"], xs["c7"]])
         res["c6_replicated"] = bool((gathered[0][0] == gathered[1][0]).all())
@@ -79,6 +87,7 @@ def test_bench_schedules_build_consistent_inputs_and_agree():
         assert all(v == rank * E_SMALL // world for v in r["start"].values()), r["start"]
         assert r["c6_replicated"] and r["c7_distinct"], r
         assert r["err_c7"] <= 2e-2 and r["err_c8"] <= 2e-2, (rank, r["err_c7"], r["err_c8"])
+        assert r["zipf_bias_ok"] and r["zipf_low_share"] > 0.7, r["zipf_low_share"]
 
 
 @pytest.mark.parametrize("sched,tp,per_rank,par", [
@@ -90,6 +99,8 @@ def test_bench_config_names_the_schedule(sched, tp, per_rank, par):
     T = 4096 if sched == "c6" else 16384
     c = bench.config_block(T, 4, sched, tp)
     assert c["tokens_per_rank"] == per_rank and c["parallelism"] == par
+    assert c["routing"].startswith("uniform")
+    assert bench.config_block(2048, 8, "c7", 1, True)["routing"].startswith("Zipf(1.2)")
     assert sched.upper() in c["workload"]
 
 

@@ -74,7 +74,11 @@ def _worker(rank, world, port, name, transport, q):
     ("ep_c6_w2.npz", 2, "nccl"), ("ep_c6_w4.npz", 4, "nccl"), ("ep_c7_w2.npz", 2, "nccl"),
     ("ep_c7_w4_zipf.npz", 4, "nccl"), ("ep_c8_w4_tp2.npz", 4, "nccl"),
     ("ep_c7_w2.npz", 2, "peer"), ("ep_c7_w4_zipf.npz", 4, "peer"),
-    ("ep_c8_w4_tp2.npz", 4, "peer")])
+    ("ep_c8_w4_tp2.npz", 4, "peer"),
+    # eight ranks: C6 ep=8, C7 dp=ep=8 with the Zipf skew, C8 tp=4 x dp=2 and tp=2 x dp=4
+    ("ep_c6_w8.npz", 8, "nccl"), ("ep_c7_w8_zipf.npz", 8, "nccl"),
+    ("ep_c7_w8_zipf.npz", 8, "peer"), ("ep_c8_w8_tp4.npz", 8, "nccl"),
+    ("ep_c8_w8_tp4.npz", 8, "peer"), ("ep_c8_w8_tp2.npz", 8, "peer")])
 def test_ep_schedule_matches_reference(name, world, transport):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
@@ -174,3 +178,57 @@ def test_peer_batch_over_capacity_keeps_ranks_in_step():
     assert res[1]["raised"] is True
     assert res[0]["err_first"] <= 2e-2
     assert res[0]["err_second"] <= 2e-2 and res[1]["err_second"] <= 2e-2
+
+
+@pytest.mark.parametrize("name,world", [("ep_c6_w8.npz", 8), ("ep_c7_w8_zipf.npz", 8),
+                                        ("ep_c8_w8_tp4.npz", 8), ("ep_c8_w4_tp2.npz", 4)])
+def test_loopback_harness_on_cpu(name, world):
+    """The thread-per-rank collective stand-in that the one-GPU expert-parallel
+    test uses (tests/loopback.py), driven here with the CPU stand-in kernels:
+    it must reproduce the reference's own per-rank outputs."""
+    sys.path.insert(0, HERE)
+    from cpu_contract import CpuContractKernels
+    from helpers import load_golden, to_t
+    from loopback import LoopbackWorld
+    from moe_inference_verify_microbench_b200.ep_lean import EPSparseMoE as Lean
+    from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
+    from moe_inference_verify_microbench_b200.hybrid import HybridMoE
+    from oracle import moe_oracle as mo
+    import torch.distributed as dist
+
+    g = load_golden(name)
+    T, H, I, E, k, tp = (int(g[n]) for n in ("T", "H", "I", "E", "k", "tp"))
+    kind = str(g["kind"])
+    d = mo.make_inputs(T * world, H, I, E, int(g["seed"]))
+    xall, wr = to_t(d["x"]), to_t(d["wr"])
+    wg, wu, wd = (to_t(d[n]) for n in ("w_gate", "w_up", "w_down"))
+    lw = LoopbackWorld(world, torch.device("cpu"))
+
+    def rank_fn(rank):
+        if kind == "c6":
+            mod, x = Lean(H, I, E, k, world, rank, group=None), xall[:T]
+        elif kind == "c7":
+            mod, x = Pure(H, I, E, k, world, rank, group=None), xall[rank * T:(rank + 1) * T]
+        else:
+            groups = [dist.new_group(list(range(i * tp, (i + 1) * tp))) for i in range(world // tp)]
+            mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None)
+            x = xall[(rank // tp) * T:(rank // tp + 1) * T]
+        mod = mod.to(torch.bfloat16)
+        mod._kernels = CpuContractKernels
+        mod.weight_loader(wr, wg, wu, wd)
+        if int(g["zipf"]):
+            lin = torch.nn.Linear(H, E, bias=True).to(torch.bfloat16)
+            lin.weight.data.copy_(wr)
+            lin.bias.data.copy_(torch.from_numpy(mo.zipf_bias(E)).to(torch.bfloat16))
+            mod.gate = lin
+        with torch.no_grad():
+            y = mod(x)
+        _, _, lg = CpuContractKernels.router_topk(x, mod.gate.weight, k,
+                                                  bias=getattr(mod.gate, "bias", None))
+        srt = torch.sort(lg.float(), dim=-1, descending=True).values
+        return y, (srt[:, k - 1] == srt[:, k]).numpy()
+
+    for rank, (y, tie) in enumerate(lw.run(rank_fn)):
+        yref = mo.f32_from_bf16_bits(g[f"y_rank{rank}"])
+        assert tie.mean() <= 0.2
+        assert mo.rel_err(y.float().numpy()[~tie], yref[~tie]) <= 2e-2, (name, rank)

@@ -108,7 +108,11 @@ def _spawn(target, world, args):
     ("ep_c6_w2.npz", 2, "nccl"), ("ep_c7_w2.npz", 2, "nccl"), ("ep_c7_w2.npz", 2, "peer"),
     ("ep_c6_w4.npz", 4, "nccl"), ("ep_c7_w4_zipf.npz", 4, "nccl"),
     ("ep_c7_w4_zipf.npz", 4, "peer"), ("ep_c8_w4_tp2.npz", 4, "nccl"),
-    ("ep_c8_w4_tp2.npz", 4, "peer")])
+    ("ep_c8_w4_tp2.npz", 4, "peer"),
+    ("ep_c6_w8.npz", 8, "nccl"), ("ep_c7_w8_zipf.npz", 8, "nccl"),
+    ("ep_c7_w8_zipf.npz", 8, "peer"), ("ep_c8_w8_tp2.npz", 8, "nccl"),
+    ("ep_c8_w8_tp2.npz", 8, "peer"), ("ep_c8_w8_tp4.npz", 8, "nccl"),
+    ("ep_c8_w8_tp4.npz", 8, "peer")])
 def test_ep_schedule_on_gpus_matches_reference(name, world, transport):
     _need(world)
     res = _spawn(_fixture_worker, world, (29800 + world + 10 * (transport == "peer"), name,
