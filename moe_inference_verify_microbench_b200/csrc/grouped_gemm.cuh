@@ -23,11 +23,13 @@
 // row index[p] / index_div: the token of routing record perm[p]).  Warps 8..11
 // load them with 16-byte cp.async into the same 128-byte-swizzled layout TMA
 // would write; eight consecutive lanes cover one row's 128 bytes, so every
-// warp instruction moves four whole 128-byte lines.  A loader publishes stage i
-// two stages later: it waits for that stage's copies, fences the generic->async
-// proxy (the MMA reads shared memory through the async proxy), and its warp's
-// lane 0 arrives on the stage barrier.  Warp 0 then loads only B.  This fuses
-// the permutation gather (C5/python/solution.py:137) into the GEMM.
+// warp instruction moves four whole 128-byte lines.  The loaders do not wait
+// for their copies: every loader thread arms the stage's gather barrier with
+// cp.async.mbarrier.arrive.noinc, which completes once all of their copies of
+// the stage have landed; lane 0 of warp 3 (the forwarder) waits for it,
+// fences the generic->async proxy (the MMA reads shared memory through the
+// async proxy) and arrives on the stage barrier.  Warp 0 then loads only B.
+// This fuses the permutation gather (C5/python/solution.py:137) into the GEMM.
 #pragma once
 
 #include "ptx.cuh"
@@ -279,7 +281,7 @@ __device__ __forceinline__ void epilogue_tile_atomic(const GemmArgs& args, uint3
 
 constexpr int kGatherWarp0 = 8;    // first of the four A-loader warps
 constexpr int kGatherWarps = 4;
-constexpr int kGatherLag = 2;      // a stage is published this many stages after its copies
+constexpr int kForwardWarp = 3;    // publishes the loaders' stages
 
 // Epilogue warps: 4..7 read TMEM lane quarters 0..3; without GATHER_A, warps
 // 8..11 take the second half of the accumulator columns (two warps per lane
@@ -320,7 +322,8 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* gat = drain + 1;  // GATHER_A: the loaders' copies of a stage have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gat + STAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -328,8 +331,9 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], GATHER_A ? 1 + kGatherWarps : 1);  // TMA (+ each loader warp)
+      mbar_init(&full[s], GATHER_A ? 2 : 1);  // TMA (+ the forwarder)
       mbar_init(&empty[s], 1);
+      mbar_init(&gat[s], kGatherWarps * 32);  // the copies of every loader thread
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -462,10 +466,8 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
     const uint32_t chunk = static_cast<uint32_t>(g & 7);
     const int row0 = g >> 3;  // 0..15
     const int K = args.num_kb * kBK;
-    static_assert(kGatherLag < STAGES - 1, "a loader must publish before it needs the stage back");
     int s = 0;
     uint32_t ph = 0;
-    uint32_t it = 0;  // stages issued by this loader
     bool ok = true;
     for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
       const int mt = w / args.n_tiles;
@@ -501,27 +503,37 @@ __global__ void __launch_bounds__(gemm_threads<GATHER_A>(), 1)
           const bool have = (nbytes >> j) & 1u;
           cp_async_16(dst, have ? src[j] + kb * kBK : src[j], have ? 16u : 0u);
         }
-        cp_async_commit();
-        if (it >= static_cast<uint32_t>(kGatherLag)) {
-          cp_async_wait_group<kGatherLag>();
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&full[(it - kGatherLag) % STAGES]);
-        }
-        ++it;
+        cp_async_arrive_noinc(&gat[s]);
         if (++s == STAGES) {
           s = 0;
           ph ^= 1u;
         }
       }
     }
-    // Publish the stages still in flight (also on abort), then let every copy land.
-    cp_async_wait_all();
-    fence_proxy_async_smem();
-    __syncwarp();
+    cp_async_wait_all();  // every copy lands before the CTA can exit
+  } else if (GATHER_A && warp == kForwardWarp) {
     if (lane == 0) {
-      const uint32_t first = it > static_cast<uint32_t>(kGatherLag) ? it - kGatherLag : 0u;
-      for (uint32_t i = first; i < it; ++i) mbar_arrive(&full[i % STAGES]);
+      // -------------------------------------------------------- forwarder
+      // A stage's A rows are complete once every loader thread's copies have
+      // landed (gat); the proxy fence then makes them visible to the tensor
+      // core's async proxy and the stage barrier hears of it.
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < total; w += gridDim.x) {
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(&gat[s], ph, abort_flag, args.status, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&full[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
     }
   } else if (warp >= 4 && warp < 4 + epi_warps<GATHER_A>()) {
     // -------------------------------------------------------------- epilogue

@@ -23,9 +23,14 @@
 //
 // GATHER_A (512 threads): warps 12..15 of each CTA gather its 128 A rows from
 // the source matrix through the index with 16-byte cp.async, as in the
-// single-CTA kernel, and publish a stage kPairGatherLag stages later by
-// arriving on the even CTA's stage barrier; the TMA producer then loads only
-// B.  This fuses the permutation gather (C5/python/solution.py:137) into the
+// single-CTA kernel; the TMA producer then loads only B.  The loaders never
+// wait for their copies: each thread arms a CTA-local barrier with
+// cp.async.mbarrier.arrive.noinc, which completes once every loader thread's
+// copies of the stage have landed, and lane 0 of warp 3 (the forwarder) waits
+// for it, fences the generic->async proxy and publishes the stage on the even
+// CTA's stage barrier.  (Publishing from the loaders themselves after
+// cp.async.wait_group serialised them on their oldest copies: 3 % slower.)
+// This fuses the permutation gather (C5/python/solution.py:137) into the
 // gate/up GEMM and removes the gathered copy's round trip through HBM.
 #pragma once
 
@@ -36,7 +41,7 @@ namespace moe {
 constexpr int kPairBM = 2 * kBM;  // rows of a pair tile (M of the pair MMA)
 constexpr int kPairBN = 256;
 constexpr int kPairGatherWarp0 = 12;  // first of the four A-loader warps (GATHER_A)
-constexpr int kPairGatherLag = 2;     // a stage is published this many stages after its copies
+constexpr int kPairForwardWarp = 3;   // publishes the loaders' stages (GATHER_A)
 
 template <bool GATHER_A>
 constexpr int pair_threads() {
@@ -59,8 +64,6 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
                              const __grid_constant__ CUtensorMap tmB1, const GemmArgs args) {
   static_assert(EPI == kEpiSwiGLU || EPI == kEpiStore || EPI == kEpiAtomic,
                 "pair kernel: SwiGLU, store or atomic epilogue");
-  static_assert(!GATHER_A || kPairGatherLag < STAGES - 1,
-                "a loader must publish before it needs the stage back");
   using L = PairSmem<STAGES>;
   constexpr int BN = kPairBN;
   constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
@@ -78,7 +81,8 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* gat = drain + 1;  // GATHER_A: this CTA's loader copies of a stage have landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gat + STAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -89,9 +93,10 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       // The even CTA's producer (+ the bytes of both CTAs), and with GATHER_A
-      // every loader warp of both CTAs.
-      mbar_init(&full[s], GATHER_A ? 1 + 2 * 4 : 1);
+      // the forwarder of each CTA.
+      mbar_init(&full[s], GATHER_A ? 1 + 2 : 1);
       mbar_init(&empty[s], 1);  // one MMA commit
+      mbar_init(&gat[s], 4 * 32);  // the copies of every loader thread of this CTA
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -234,7 +239,6 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
     const int K = args.num_kb * kBK;
     int s = 0;
     uint32_t ph = 0;
-    uint32_t it = 0;
     bool ok = true;
     for (int w = pair; ok && w < total; w += npairs) {
       const int mt = w / args.n_tiles;
@@ -271,29 +275,37 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
           const bool have = (present >> j) & 1u;
           cp_async_16(dst, have ? src[j] + kb * kBK : src[j], have ? 16u : 0u);
         }
-        cp_async_commit();
-        if (it >= static_cast<uint32_t>(kPairGatherLag)) {
-          cp_async_wait_group<kPairGatherLag>();
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0)
-            mbar_arrive_cluster(cluster_addr(&full[(it - kPairGatherLag) % STAGES], 0));
-        }
-        ++it;
+        cp_async_arrive_noinc(&gat[s]);
         if (++s == STAGES) {
           s = 0;
           ph ^= 1u;
         }
       }
     }
-    // Publish the stages still in flight (also on abort), then let every copy land.
-    cp_async_wait_all();
-    fence_proxy_async_smem();
-    __syncwarp();
+    cp_async_wait_all();  // every copy lands before the CTA can exit
+  } else if (GATHER_A && warp == kPairForwardWarp) {
     if (lane == 0) {
-      const uint32_t first = it > static_cast<uint32_t>(kPairGatherLag) ? it - kPairGatherLag : 0u;
-      for (uint32_t i = first; i < it; ++i)
-        mbar_arrive_cluster(cluster_addr(&full[i % STAGES], 0));
+      // -------------------------------------------------------- forwarder
+      // A stage's A rows are complete once every loader thread's copies have
+      // landed (gat); then the proxy fence makes them visible to the tensor
+      // core's async proxy and the stage is published on the even CTA's barrier.
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int w = pair; ok && w < total; w += npairs) {
+        for (int kb = 0; kb < args.num_kb; ++kb) {
+          if (!mbar_wait(&gat[s], ph, abort_flag, args.status, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_smem();
+          mbar_arrive_cluster(cluster_addr(&full[s], 0));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
     }
   } else if (warp >= 4 && warp < 4 + kEpiWarps) {
     // -------------------------------------------------------------- epilogue
