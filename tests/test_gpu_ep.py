@@ -206,12 +206,13 @@ def _peer_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_ep_peer_transport_bit_identical_to_nccl():
+@pytest.mark.parametrize("world", [2, 8])
+def test_ep_peer_transport_bit_identical_to_nccl(world):
     """The peer-store exchange and the NCCL all_to_alls sum the same rows in
     the same order: outputs must be bit-identical, over several forwards
     with different per-rank token counts."""
-    _need(2)
-    res = _spawn(_peer_worker, 2, (29950,))  # both transports pick the same tile height here
+    _need(world)
+    res = _spawn(_peer_worker, world, (29950 + world,))  # both transports: same tile height
     for rank, same in res:
         assert all(same), (rank, same)
 
