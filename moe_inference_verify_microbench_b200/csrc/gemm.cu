@@ -210,10 +210,11 @@ int launch_w13_swiglu(const void* a, int M, const int4* tiles, const int* num_ti
   if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   if (tile_rows == kPairTileRows) {
     if ((I % (kPairBN / 2)) != 0) return kRcUnsupported;
+    // Each CTA loads 64 gate rows and the 64 matching up rows per stage.
     CUtensorMap ma, mg, mu;
     int rc = map_2d(&ma, a, M, H, kBM);
-    if (rc == kRcOk) rc = map_3d(&mg, w_gate, E, I, H, kPairBN / 2);
-    if (rc == kRcOk) rc = map_3d(&mu, w_up, E, I, H, kPairBN / 2);
+    if (rc == kRcOk) rc = map_3d(&mg, w_gate, E, I, H, kPairBN / 4);
+    if (rc == kRcOk) rc = map_3d(&mu, w_up, E, I, H, kPairBN / 4);
     if (rc != kRcOk) return rc;
     GemmArgs g = blank_args(status);
     g.tiles = tiles;
@@ -273,9 +274,10 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
   if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   if (tile_rows == kPairTileRows) {
     if ((I % (kPairBN / 2)) != 0) return kRcUnsupported;
+    // Each CTA loads 64 gate rows and the 64 matching up rows per stage.
     CUtensorMap mg, mu;
-    int rc = map_3d(&mg, w_gate, E, I, H, kPairBN / 2);
-    if (rc == kRcOk) rc = map_3d(&mu, w_up, E, I, H, kPairBN / 2);
+    int rc = map_3d(&mg, w_gate, E, I, H, kPairBN / 4);
+    if (rc == kRcOk) rc = map_3d(&mu, w_up, E, I, H, kPairBN / 4);
     if (rc != kRcOk) return rc;
     GemmArgs g = blank_args(status);
     g.tiles = tiles;

@@ -146,44 +146,35 @@ __device__ __forceinline__ uint32_t stage_slot(int r, int j) {
   else return static_cast<uint32_t>(r * 64 + ((j ^ ((r >> 1) & 3)) << 4));
 }
 
-// Epilogue of one accumulator tile for this thread's row: TMEM columns ->
-// bf16 -> this warp's staging rows -> global.  SwiGLU: out[row, nt*BN/2 + c] =
-// silu(acc[c]) * acc[BN/2 + c]; store: out[orow, nt*BN + c] = scale * acc[c].
-// `half` selects this warp's share of the columns when kHalves warps serve one
-// TMEM lane quarter.  Output is written in chunks of CW columns: every lane
-// stages its row, then each store instruction writes CW*2-byte row segments of
-// 256/CW rows (whole 128-byte lines for CW = 64), with the row's destination
-// and store flag taken from the lane that owns it.
-template <int BN, int EPI, int kHalves>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tb, int row,
-                                              bool valid, bool st, int orow_idx, float scale,
-                                              int nt, int half, uint8_t* stage, int lane) {
-  constexpr int kOut = EPI == kEpiSwiGLU ? BN / 2 : BN;  // output columns of the tile
-  constexpr int kSplit = (kOut / kHalves >= 32) ? kHalves : 1;
-  constexpr int kCols = kOut / kSplit;                   // this warp's output columns
-  constexpr int CW = (kCols % 64 == 0) ? 64 : 32;
-  static_assert(kCols % 32 == 0, "epilogue works in 32-column chunks");
+// Epilogue core: `ncols` output columns of this thread's row, in chunks of CW
+// (32 or 64) columns: TMEM -> bf16 -> this warp's staging rows -> global.
+// Output column ocol0 + c comes from TMEM column tcol0 + c of this warp's lane
+// window `tb`; SwiGLU: out = silu(acc[tcol0 + c]) * acc[tcol0 + ucol + c];
+// store: out = scale * acc[tcol0 + c].  Every lane stages its row, then each
+// store instruction writes CW*2-byte row segments of 256/CW rows (whole
+// 128-byte lines for CW = 64), with the row's destination and store flag
+// taken from the lane that owns it.
+template <int EPI, int CW>
+__device__ __forceinline__ void epilogue_cols(const GemmArgs& args, uint32_t tb, bool st,
+                                              int orow_idx, float scale, int tcol0, int ucol,
+                                              int ocol0, int ncols, uint8_t* stage, int lane) {
+  static_assert(CW == 32 || CW == 64, "epilogue chunks are 32 or 64 columns");
   constexpr int kRowBytes = 2 * CW;
   constexpr int kLanesPerRow = CW / 8;
   constexpr int kRowsPerStore = 32 / kLanesPerRow;
-  if (half >= kSplit) return;
-  if constexpr (EPI == kEpiSwiGLU) {
-    orow_idx = row;
-    st = valid && row < args.out_rows;
-  }
   const uint32_t my_stage = smem_u32(stage);
   const int j = lane % kLanesPerRow;
   const int rsub = lane / kLanesPerRow;
-  __nv_bfloat16* const out_base = args.out + static_cast<size_t>(nt) * kOut;
+  __nv_bfloat16* const out_base = args.out + ocol0;
 #pragma unroll 1
-  for (int c0 = half * kCols; c0 < (half + 1) * kCols; c0 += CW) {
+  for (int c0 = 0; c0 < ncols; c0 += CW) {
     uint32_t pk[CW / 2];
 #pragma unroll
     for (int sub = 0; sub < CW / 32; ++sub) {
       if constexpr (EPI == kEpiSwiGLU) {
         uint32_t g[32], u[32];
-        tmem_ld32(tb + c0 + 32 * sub, g);
-        tmem_ld32(tb + BN / 2 + c0 + 32 * sub, u);
+        tmem_ld32(tb + tcol0 + c0 + 32 * sub, g);
+        tmem_ld32(tb + tcol0 + ucol + c0 + 32 * sub, u);
         tc_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -193,7 +184,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tb,
         }
       } else {
         uint32_t r[32];
-        tmem_ld32(tb + c0 + 32 * sub, r);
+        tmem_ld32(tb + tcol0 + c0 + 32 * sub, r);
         tc_wait_ld();
 #pragma unroll
         for (int i = 0; i < 16; ++i)
@@ -226,29 +217,50 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tb,
   }
 }
 
-// Atomic-combine epilogue (the reference's index_add_ on CUDA, C5:160): each
-// row's scaled fp32 results are added into its token's accumulation row with
-// 16-byte fp32 vector atomics.  Rows are staged through this warp's shared
-// memory so that eight lanes cover one 128-byte segment of a row and each
-// instruction touches four whole segments.  The order in which the k records
-// of a token land is not fixed, so the sums are not bitwise reproducible.
-template <int BN, int kHalves>
-__device__ __forceinline__ void epilogue_tile_atomic(const GemmArgs& args, uint32_t tb, bool st,
-                                                     int orow_idx, float scale, int nt, int half,
-                                                     uint8_t* stage, int lane) {
-  constexpr int kSplit = (BN / kHalves >= 32) ? kHalves : 1;
-  constexpr int kCols = BN / kSplit;
+// Epilogue of one accumulator tile of the single-CTA kernel for this thread's
+// row: the accumulator holds [gate BN/2 | up BN/2] (SwiGLU) or BN output
+// columns (store); SwiGLU: out[row, nt*BN/2 + c] = silu(acc[c]) *
+// acc[BN/2 + c]; store: out[orow, nt*BN + c] = scale * acc[c].  `half`
+// selects this warp's share of the columns when kHalves warps serve one TMEM
+// lane quarter.
+template <int BN, int EPI, int kHalves>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tb, int row,
+                                              bool valid, bool st, int orow_idx, float scale,
+                                              int nt, int half, uint8_t* stage, int lane) {
+  constexpr int kOut = EPI == kEpiSwiGLU ? BN / 2 : BN;  // output columns of the tile
+  constexpr int kSplit = (kOut / kHalves >= 32) ? kHalves : 1;
+  constexpr int kCols = kOut / kSplit;                   // this warp's output columns
+  constexpr int CW = (kCols % 64 == 0) ? 64 : 32;
   static_assert(kCols % 32 == 0, "epilogue works in 32-column chunks");
   if (half >= kSplit) return;
+  if constexpr (EPI == kEpiSwiGLU) {
+    orow_idx = row;
+    st = valid && row < args.out_rows;
+  }
+  epilogue_cols<EPI, CW>(args, tb, st, orow_idx, scale, half * kCols, BN / 2,
+                         nt * kOut + half * kCols, kCols, stage, lane);
+}
+
+// Atomic-combine epilogue core (the reference's index_add_ on CUDA, C5:160):
+// this row's scaled fp32 results of TMEM columns tcol0 .. tcol0 + ncols are
+// added into its token's accumulation row at columns ocol0 .. with 16-byte
+// fp32 vector atomics.  Rows are staged through this warp's shared memory so
+// that eight lanes cover one 128-byte segment of a row and each instruction
+// touches four whole segments.  The order in which the k records of a token
+// land is not fixed, so the sums are not bitwise reproducible.
+__device__ __forceinline__ void epilogue_cols_atomic(const GemmArgs& args, uint32_t tb, bool st,
+                                                     int orow_idx, float scale, int tcol0,
+                                                     int ocol0, int ncols, uint8_t* stage,
+                                                     int lane) {
   const uint32_t my_stage = smem_u32(stage);
   const int j = lane & 7;
   const int rsub = lane >> 3;
   const int tok = st ? orow_idx / args.red_div : 0;
-  float* const out_base = args.out_f32 + static_cast<size_t>(nt) * BN;
+  float* const out_base = args.out_f32 + ocol0;
 #pragma unroll 1
-  for (int c0 = half * kCols; c0 < (half + 1) * kCols; c0 += 32) {
+  for (int c0 = 0; c0 < ncols; c0 += 32) {
     uint32_t r[32];
-    tmem_ld32(tb + c0, r);
+    tmem_ld32(tb + tcol0 + c0, r);
     tc_wait_ld();
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -277,6 +289,18 @@ __device__ __forceinline__ void epilogue_tile_atomic(const GemmArgs& args, uint3
     }
     __syncwarp();
   }
+}
+
+template <int BN, int kHalves>
+__device__ __forceinline__ void epilogue_tile_atomic(const GemmArgs& args, uint32_t tb, bool st,
+                                                     int orow_idx, float scale, int nt, int half,
+                                                     uint8_t* stage, int lane) {
+  constexpr int kSplit = (BN / kHalves >= 32) ? kHalves : 1;
+  constexpr int kCols = BN / kSplit;
+  static_assert(kCols % 32 == 0, "epilogue works in 32-column chunks");
+  if (half >= kSplit) return;
+  epilogue_cols_atomic(args, tb, st, orow_idx, scale, half * kCols, nt * BN + half * kCols, kCols,
+                       stage, lane);
 }
 
 constexpr int kGatherWarp0 = 8;    // first of the four A-loader warps

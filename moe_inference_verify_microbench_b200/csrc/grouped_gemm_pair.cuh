@@ -5,12 +5,24 @@
 // Work unit: one (pair tile, N-tile).  A pair tile is up to 256 consecutive
 // rows of one expert (tile table built with 256-row blocks); CTA r of the pair
 // owns rows row_begin + 128 r .. +127 of it and loads those A rows plus half of
-// the B tile (gate rows for r = 0 and up rows for r = 1 in the SwiGLU GEMM;
-// B rows n*256 + 128 r .. +127 for the store GEMM).  Each CTA's tensor memory
-// receives the 128 x 256 accumulator of its own rows, so the epilogue is the
-// one of the single-CTA kernel.  Per CTA and K-block the operands are 32 KB
-// for 4.2 MFLOP, against 48 KB for the single-CTA 128 x 256 tile: the pair
-// halves the B traffic from L2 and leaves room for six stages.
+// the B tile (the store GEMM: B rows n*256 + 128 r .. +127; the SwiGLU GEMM:
+// gate rows n*128 + 64 r .. +63 followed by the up rows of the same indices,
+// so that the accumulator holds [gate | up] of the same output columns in
+// each 128-column half: [g 0..63 | u 0..63 | g 64..127 | u 64..127]).  Each
+// CTA's tensor memory receives the 128 x 256 accumulator of its own rows.
+// Per CTA and K-block the operands are 32 KB for 4.2 MFLOP, against 48 KB for
+// the single-CTA 128 x 256 tile: the pair halves the B traffic from L2 and
+// leaves room for six stages.
+//
+// Half tiles.  The last block of an expert often holds few rows (with ~1024
+// rows per expert about half the experts end in a block of <= 64 rows); a
+// tile of <= 128 rows runs M = 128 MMAs instead, with 64 A rows per CTA, at
+// half the tensor work.  Their accumulator (the tcgen05 data-path layout of
+// cta_group::2 at M = 128) keeps the CTA's 64 rows twice over: columns
+// 0..127 of the tile in TMEM lanes 0..63 and columns 128..255 in lanes
+// 64..127, both at TMEM columns 0..127; the epilogue maps lane quarters to
+// rows and columns accordingly.  The gate/up column order above keeps gate
+// and up of an output column in the same lane in both layouts.
 //
 // Roles per CTA (384 threads): warp 0 TMA producer (both CTAs; the copies of
 // both count on the even CTA's stage barrier), warp 1 MMA issuer (even CTA
@@ -68,7 +80,6 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
   constexpr int BN = kPairBN;
   constexpr uint32_t kTmemCols = 2 * BN;  // two accumulators
   constexpr int kEpiWarps = 8;
-  constexpr int kHalves = kEpiWarps / 4;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -147,7 +158,9 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
           *abort_flag = 1;
           break;
         }
-        const int arow = t.y + kBM * static_cast<int>(rank);
+        // A rows of this CTA: 128 (64 in a half tile); the box always holds
+        // 128 rows, of which a half tile's MMA reads the first 64.
+        const int arow = t.y + (t.z - t.y <= kBM ? kBM / 2 : kBM) * static_cast<int>(rank);
         for (int kb = 0; kb < args.num_kb; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, args.status, kErrTimeoutEmpty)) {
             ok = false;
@@ -158,7 +171,10 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
           if (!GATHER_A) tma_load_2d_pair(sA + s * L::kABytes, &tmA, fb, kb * kBK, arow);
           uint8_t* b = sB + s * L::kBBytes;
           if (EPI == kEpiSwiGLU) {
-            tma_load_3d_pair(b, leader ? &tmB0 : &tmB1, fb, kb * kBK, nt * (BN / 2), t.x);
+            // gate rows nt*128 + 64 rank .. +63, then the up rows of the same indices
+            const int brow = nt * (BN / 2) + (BN / 4) * static_cast<int>(rank);
+            tma_load_3d_pair(b, &tmB0, fb, kb * kBK, brow, t.x);
+            tma_load_3d_pair(b + L::kBBytes / 2, &tmB1, fb, kb * kBK, brow, t.x);
           } else {
             tma_load_3d_pair(b, &tmB0, fb, kb * kBK, nt * BN + (BN / 2) * static_cast<int>(rank),
                              t.x);
@@ -184,12 +200,18 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ------------------------------------------------------------ MMA issuer
-      const uint32_t idesc = idesc_bf16_f32(kPairBM, BN);
+      const uint32_t idesc_full = idesc_bf16_f32(kPairBM, BN);
+      const uint32_t idesc_half = idesc_bf16_f32(kBM, BN);  // half tile: 64 rows per CTA
       int s = 0;
       uint32_t ph = 0;
       int it = 0;
       bool ok = true;
+      // Tile entries are read one work unit ahead, so the load is not waited on.
+      int4 t_next = pair < total ? load_tile(args, pair / args.n_tiles) : make_int4(0, 0, 0, 0);
       for (int w = pair; ok && w < total; w += npairs, ++it) {
+        const int4 t = t_next;
+        if (w + npairs < total) t_next = load_tile(args, (w + npairs) / args.n_tiles);
+        const uint32_t idesc = t.z - t.y <= kBM ? idesc_half : idesc_full;
         const int acc = it & 1;
         const uint32_t acc_ph = (it >> 1) & 1;
         if (!mbar_wait(&acc_empty[acc], acc_ph ^ 1u, abort_flag, args.status,
@@ -243,14 +265,16 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
     for (int w = pair; ok && w < total; w += npairs) {
       const int mt = w / args.n_tiles;
       const int4 t = load_tile(args, mt);
-      const int base = t.y + kBM * static_cast<int>(rank);
+      const bool half_tile = t.z - t.y <= kBM;
+      const int base = t.y + (half_tile ? kBM / 2 : kBM) * static_cast<int>(rank);
+      const int nrows = half_tile ? 4 : 8;  // rows row0 + 16 j, j < nrows (64 or 128 rows)
       const __nv_bfloat16* src[8];
       uint32_t present = 0;  // bit j: row j of this thread exists
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int p = base + row0 + 16 * j;
         src[j] = args.a_src;  // any valid address when the row is absent (zero-filled)
-        if (p < t.z) {
+        if (j < nrows && p < t.z) {
           const int i = args.a_index != nullptr ? args.a_index[p] / args.a_index_div : p;
           if (i >= 0 && i < args.a_src_rows) {
             src[j] = args.a_src + static_cast<size_t>(i) * K + chunk * 8;
@@ -270,6 +294,7 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
         const uint32_t sbase = smem_u32(sA + s * L::kABytes);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
+          if (j >= nrows) break;  // a half tile's MMA reads rows 0..63 only
           const uint32_t r = static_cast<uint32_t>(row0 + 16 * j);
           const uint32_t dst = sbase + r * 128u + ((chunk ^ (r & 7u)) << 4);
           const bool have = (present >> j) & 1u;
@@ -309,8 +334,8 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
     }
   } else if (warp >= 4 && warp < 4 + kEpiWarps) {
     // -------------------------------------------------------------- epilogue
-    const int q = warp & 3;
-    const int half = (warp - 4) >> 2;
+    const int q = warp & 3;                 // TMEM lane quarter of this warp
+    const int part = (warp - 4) >> 2;       // which of the two column shares
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t release0 = cluster_addr(&acc_empty[0], 0);
     const uint32_t release1 = cluster_addr(&acc_empty[1], 0);
@@ -321,7 +346,9 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
       const int mt = w / args.n_tiles;
       const int nt = w - mt * args.n_tiles;
       const int4 t = load_tile(args, mt);
-      const int row = t.y + kBM * static_cast<int>(rank) + q * 32 + lane;
+      const bool half_tile = t.z - t.y <= kBM;
+      const int row = half_tile ? t.y + (kBM / 2) * static_cast<int>(rank) + (q & 1) * 32 + lane
+                                : t.y + kBM * static_cast<int>(rank) + q * 32 + lane;
       const bool valid = row < t.z;
       int orow_idx = row;
       float scale = 1.0f;
@@ -336,6 +363,8 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
             scale = args.row_scale[orow_idx];
           }
         }
+      } else {
+        st = valid && row < args.out_rows;
       }
       bool ok = mbar_wait(&acc_full[acc], acc_ph, abort_flag, args.status,
                                   kErrTimeoutAccFull);
@@ -343,12 +372,35 @@ __global__ void __launch_bounds__(pair_threads<GATHER_A>(), 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t tb = tmem_base + static_cast<uint32_t>(acc * BN) + lane_off;
-      if constexpr (EPI == kEpiAtomic)
-        epilogue_tile_atomic<BN, kHalves>(args, tb, st, orow_idx, scale, nt, half,
-                                          sOut + (warp - 4) * kEpiStageBytes, lane);
-      else
-        epilogue_tile<BN, EPI, kHalves>(args, tb, row, valid, st, orow_idx, scale, nt, half,
-                                        sOut + (warp - 4) * kEpiStageBytes, lane);
+      uint8_t* const stage = sOut + (warp - 4) * kEpiStageBytes;
+      // Columns of this warp.  Full tile: its share `part` of its lane quarter's
+      // 256 columns.  Half tile: lane quarter q holds rows (q & 1) * 32 .. and
+      // tile columns 128 (q >> 1) .. + 127 at TMEM columns 0..127.
+      const int blk = q >> 1;
+      if constexpr (EPI == kEpiSwiGLU) {
+        // [g | u] pairs of 64 columns: output column nt*128 + 64 b + i has its
+        // gate value at accumulator column 128 b + i and up at 128 b + 64 + i.
+        if (!half_tile)
+          epilogue_cols<kEpiSwiGLU, 64>(args, tb, st, row, 1.0f, 128 * part, 64,
+                                        nt * (BN / 2) + 64 * part, 64, stage, lane);
+        else
+          epilogue_cols<kEpiSwiGLU, 32>(args, tb, st, row, 1.0f, 32 * part, 64,
+                                        nt * (BN / 2) + 64 * blk + 32 * part, 32, stage, lane);
+      } else if constexpr (EPI == kEpiStore) {
+        if (!half_tile)
+          epilogue_cols<kEpiStore, 64>(args, tb, st, orow_idx, scale, 128 * part, 0,
+                                       nt * BN + 128 * part, 128, stage, lane);
+        else
+          epilogue_cols<kEpiStore, 64>(args, tb, st, orow_idx, scale, 64 * part, 0,
+                                       nt * BN + 128 * blk + 64 * part, 64, stage, lane);
+      } else {
+        if (!half_tile)
+          epilogue_cols_atomic(args, tb, st, orow_idx, scale, 128 * part, nt * BN + 128 * part,
+                               128, stage, lane);
+        else
+          epilogue_cols_atomic(args, tb, st, orow_idx, scale, 64 * part,
+                               nt * BN + 128 * blk + 64 * part, 64, stage, lane);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc ? release1 : release0);

@@ -219,6 +219,61 @@ def test_w2_scatter(cuda, counts, H, I, mapped):
     assert mo.rel_err(to_f32(out), ref) <= 1e-2
 
 
+def _pair_table(offs, cuda):
+    """256-row tile table of the CTA-pair GEMMs: every expert's rows cut into
+    blocks of 256; a last block of <= 128 rows is a half tile."""
+    t = []
+    for e in range(len(offs) - 1):
+        for b in range(int(offs[e]), int(offs[e + 1]), 256):
+            t.append((e, b, min(b + 256, int(offs[e + 1])), 0))
+    tiles = torch.tensor(t, dtype=torch.int32, device=cuda).reshape(-1, 4)
+    n = torch.tensor([len(t)], dtype=torch.int32, device=cuda)
+    return tiles, n, len(t)
+
+
+@pytest.mark.parametrize("counts,H,I", [
+    # half tiles of 1, 64, 65, 127 and 128 rows (M = 128 MMAs) next to full ones
+    ([1, 64, 65, 127, 128, 129, 0, 200, 256, 257, 383, 384, 385, 513], 256, 128),
+    ([1050, 1000, 1024, 1088, 64, 0, 130], 2048, 768),  # production widths
+])
+def test_pair_gemms_half_and_full_tiles(cuda, counts, H, I):
+    """CTA-pair GEMMs on 256-row tile tables whose last block of an expert may
+    hold <= 128 rows (then the pair runs M = 128 MMAs, 64 rows per CTA, with
+    the accumulator split over the lane halves): gate/up + SwiGLU with the A
+    rows by TMA and gathered by the loader warps (bitwise equal), and the down
+    GEMM with the weighted scatter and with the atomic combine, against fp32."""
+    offs, M, tb, fb, _, _, _ = _grouped_setup(cuda, counts, H, I, 31 + sum(counts))
+    tiles, nt, mt = _pair_table(offs, cuda)
+    a = tb["a"].to(cuda)
+    wg, wu, wd = (tb[n].to(cuda) for n in ("wg", "wu", "wd"))
+    h = ops.grouped_w13_swiglu(a, tiles, nt, mt, wg, wu, tile_rows=256)
+    idx = torch.arange(M, dtype=torch.int32, device=cuda)
+    h2 = ops.grouped_w13_swiglu_gather(a, idx, 1, M, tiles, nt, mt, wg, wu, tile_rows=256)
+    rng = np.random.default_rng(5)
+    rmap = rng.permutation(M).astype(np.int32)
+    scale = rng.random(M).astype(np.float32)
+    rmap_t, scale_t = torch.from_numpy(rmap).to(cuda), torch.from_numpy(scale).to(cuda)
+    out = ops.grouped_w2(h, tiles, nt, mt, wd, row_map=rmap_t, slot_scale=scale_t, tile_rows=256)
+    acc = torch.zeros(M, H, dtype=torch.float32, device=cuda)
+    ops.grouped_w2_atomic(h, tiles, nt, mt, wd, rmap_t, scale_t, M, 1, acc, tile_rows=256)
+    ops.check_status(cuda)
+    assert torch.equal(h, h2)
+    href = np.zeros((M, I), dtype=np.float32)
+    oref = np.zeros((M, H), dtype=np.float32)
+    hf = to_f32(h)
+    for e in range(len(counts)):
+        s, t = offs[e], offs[e + 1]
+        if s == t:
+            continue
+        g = fb["a"][s:t] @ fb["wg"][e].T
+        u = fb["a"][s:t] @ fb["wu"][e].T
+        href[s:t] = mo.silu_f32(g) * u
+        oref[rmap[s:t]] = (hf[s:t] @ fb["wd"][e].T) * scale[rmap[s:t]][:, None]
+    assert mo.rel_err(hf, href) <= 1e-2
+    assert mo.rel_err(to_f32(out), oref) <= 1e-2
+    assert mo.rel_err(acc.cpu().numpy(), oref) <= 1e-2
+
+
 @pytest.mark.parametrize("T,k,H,I,E", [(300, 8, 256, 128, 16), (77, 4, 128, 64, 8), (2048, 8, 2048, 768, 128)])
 def test_w13_gather_fused_equals_gather_then_gemm(cuda, T, k, H, I, E):
     """The fused-gather A operand (cp.async, swizzled by hand) must reproduce the
