@@ -55,6 +55,7 @@ extern "C" {
 #define MOE_ERR_TIMEOUT_ACC_FULL 0x103
 #define MOE_ERR_TIMEOUT_ACC_EMPTY 0x104
 #define MOE_ERR_PEER_TIMEOUT 0x105
+#define MOE_ERR_TIMEOUT_GRID 0x106
 #define MOE_ERR_BAD_EXPERT 0x201
 #define MOE_ERR_BAD_ROW 0x202
 

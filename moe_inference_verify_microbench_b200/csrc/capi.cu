@@ -79,7 +79,11 @@ size_t layer_layout(int T, int H, int I, int E, int k, int mode, void* ws, Body&
   void* slots = use_atomic_combine(mode, lp)
                     ? static_cast<void*>(c.take<float>(static_cast<size_t>(T) * H))
                     : static_cast<void*>(c.take<__nv_bfloat16>(p.R * H));
-  body(p, ids, w, sort_ws, counts, offsets, perm, tiles, num_tiles, sorted_x, h, slots);
+  // single-launch decode layer: router logits and its grid-barrier counters
+  void* fused = lp.small && fused_decode_ok(T, H, I, E, k)
+                    ? static_cast<void*>(c.take<uint8_t>(fused_decode_scratch_bytes(T, E)))
+                    : nullptr;
+  body(p, ids, w, sort_ws, counts, offsets, perm, tiles, num_tiles, sorted_x, h, slots, fused);
   return c.used;
 }
 
@@ -102,6 +106,7 @@ const char* moe_error_string(int code) {
     case kErrTimeoutAccFull: return "device: epilogue timed out waiting for the accumulator";
     case kErrTimeoutAccEmpty: return "device: MMA warp timed out waiting for the epilogue";
     case kErrPeerTimeout: return "device: timed out waiting for a peer rank of the expert-parallel group";
+    case kErrTimeoutGrid: return "device: timed out in a grid-wide barrier of the single-launch decode layer";
     case kErrBadExpert: return "device: expert id out of range";
     case kErrBadRow: return "device: row index out of range";
     default: return "unknown code";
@@ -353,8 +358,19 @@ int moe_layer_forward_ex(const void* x, const void* router_weight, const float* 
   layer_layout(T, H, I, E, top_k, combine_mode, workspace,
                [&](const LayerPlan& p, int* ids, float* w, void* sort_ws, int* counts,
                    int* offsets, int* perm, int4* tiles, int* num_tiles, void* sorted_x, void* h,
-                   void* slots) {
+                   void* slots, void* fused) {
                  const int R = static_cast<int>(p.R);
+                 if (fused != nullptr) {
+                   // T * k <= 32 records: the whole layer in one launch (bitwise
+                   // the result of the four-launch decode path below, which runs
+                   // instead if the cooperative launch is refused).
+                   rc = launch_decode_fused(x, router_weight, router_bias, T, H, I, E, top_k,
+                                            norm_topk_prob, w_gate, w_up, w_down, fused, h,
+                                            slots, y, status, stream);
+                   if (rc == kRcOk) return;
+                   (void)cudaGetLastError();  // a refused launch leaves no sticky error
+                   rc = kRcOk;
+                 }
                  const LayerPath lp = layer_path(R, H, I, E);
                  const bool small = lp.small;  // decode: weight-streaming kernels
                  const int tile_rows = lp.tile_rows;  // 256: CTA-pair GEMMs

@@ -239,7 +239,12 @@ constexpr int kPrefetchRows = 32;                    // down rows per prefetch r
 // One warp's pass over ROWS weight rows of a stage (row j at w + j * rstride,
 // in uint4 units) for n <= NR records whose A rows are act[rows[r]], over CH
 // dependency chains per (row, record).
-template <int ROWS, int NR, int CH>
+// How the consumers read the A rows: the read-only path (inputs of the
+// launch), through L2 (rows written earlier in the same launch by other
+// CTAs), or a plain load (rows staged in this CTA's shared memory).
+enum ActLoad : int { kActLdg = 0, kActL2 = 1, kActPlain = 2 };
+
+template <int ROWS, int NR, int CH, int ACT = kActLdg>
 __device__ __forceinline__ void stage_dots(const uint4* w, int rstride,
                                            const uint4* __restrict__ act, const int* rows, int n,
                                            int vec, int lane, float (&acc)[ROWS][NR][CH]) {
@@ -258,7 +263,8 @@ __device__ __forceinline__ void stage_dots(const uint4* w, int rstride,
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
       if (r < n) {
-        const uint4 xv = __ldg(act + static_cast<size_t>(rows[r]) * vec + v);
+        const uint4* xp = act + static_cast<size_t>(rows[r]) * vec + v;
+        const uint4 xv = ACT == kActLdg ? __ldg(xp) : ACT == kActL2 ? __ldcg(xp) : *xp;
 #pragma unroll
         for (int j = 0; j < ROWS; ++j) {
           float* c = acc[j][r];
@@ -313,14 +319,14 @@ __device__ __forceinline__ void reduce_records(float (&v)[ROWS][NR], int lane) {
 // Gate/up: rows 0 and 1 are the gate and up rows of output row `row`; down:
 // rows j = 0..ROWS-1 are output rows row + j * kGemvConsumerWarps.  Both sit
 // kGemvConsumerWarps rows apart in the stage.
-template <bool SWIGLU, int NR>
+template <bool SWIGLU, int NR, int ACT = kActLdg>
 __device__ __forceinline__ void gemv_pass(const StreamArgs& a, const uint4* w, int p0, int n,
                                           int row, const int* rows, int my_out, float my_scale,
                                           int bad, int vec, int lane) {
   constexpr int ROWS = SWIGLU ? 2 : gemv_rows_per_warp<false>();
   constexpr int CH = ROWS * NR >= 16 ? 2 : 4;
   float acc[ROWS][NR][CH];
-  stage_dots<ROWS, NR, CH>(w, kGemvConsumerWarps * vec, a.act, rows, n, vec, lane, acc);
+  stage_dots<ROWS, NR, CH, ACT>(w, kGemvConsumerWarps * vec, a.act, rows, n, vec, lane, acc);
   float v[ROWS][NR];
 #pragma unroll
   for (int j = 0; j < ROWS; ++j)
@@ -388,7 +394,7 @@ __device__ __forceinline__ long long block_scan_ll(long long v, long long* sh, l
 // This CTA's contiguous item range [*lo, *hi): items are ordered (tile, row
 // block) and the ranges split the summed item cost evenly over the grid, so a
 // CTA that meets tiles with many records gets fewer items.
-__device__ void balanced_range(const StreamArgs& a, int nt, int blocks, long long* lo,
+__device__ __forceinline__ void balanced_range(const StreamArgs& a, int nt, int blocks, long long* lo,
                                long long* hi) {
   __shared__ long long sh_scan[32];
   __shared__ long long sh_range[2];
@@ -425,33 +431,21 @@ __device__ void balanced_range(const StreamArgs& a, int nt, int blocks, long lon
   *hi = sh_range[1];
 }
 
-template <bool SWIGLU>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs a) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];
+// The work items [lo, hi) of a streamed GEMV on this CTA: the producer warp's
+// lane 0 copies each item's weight rows into the ring `smem_raw` (a.stages
+// stages, barriers full/empty, each used from phase 0), the consumer warps
+// apply them.  Every thread of the CTA calls it; `nt` is the tile count.
+// ACT: how the consumers read the A rows (ActLoad).
+template <bool SWIGLU, int ACT = kActLdg>
+__device__ __forceinline__ void stream_items(const StreamArgs& a, uint8_t* smem_raw, uint64_t* full,
+                             uint64_t* empty, volatile int* abort_flag, int nt, long long lo,
+                             long long hi) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int vec = a.K / 8;
   constexpr int kRB = gemv_row_block<SWIGLU>();
   const uint32_t mat_bytes = static_cast<uint32_t>(kRB) * a.K * 2;  // one matrix's rows
   const uint32_t stage_bytes = (SWIGLU ? 2u : 1u) * mat_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + a.stages * stage_bytes);
-  uint64_t* empty = full + kGemvMaxStages;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kGemvMaxStages);
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < a.stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kGemvConsumerWarps);
-    }
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
-  pdl_wait();
-  pdl_trigger();
-
-  const int nt = max(0, min(*a.num_tiles, a.max_tiles));
   const int blocks = a.N / kRB;
-  long long lo, hi;
-  balanced_range(a, nt, blocks, &lo, &hi);
 
   if (warp == kGemvConsumerWarps) {
     // ------------------------------------------------------------ producer
@@ -477,7 +471,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
       }
       if (SWIGLU && a.next_w != nullptr && !*abort_flag) {
         // This CTA's share of the next GEMM's weights, in kPrefetchRows-row
-        // requests, so the down projection streams from L2.
+        // requests, so the down projection streams from L2.  Issued after
+        // this GEMM's own copies, which are on the critical path (issuing the
+        // prefetch first measured slower at T=1 and 2).
         const int nblk = a.next_N / kPrefetchRows;
         const long long bytes_all =
             static_cast<long long>(nt) * a.next_N * a.next_K * static_cast<long long>(2);
@@ -508,7 +504,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
         }
       }
     }
-    return;
+    return;  // the producer warp has no consumer work
   }
 
   // -------------------------------------------------------------- consumers
@@ -550,7 +546,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
       fetch(t.y, min(kGemvMaxRecs, t.z - t.y));
       cached_ti = single ? ti : -1;
     }
-    if (!mbar_wait(&full[s], ph, abort_flag, a.status, kErrTimeoutFull)) return;
+    if (!mbar_wait(&full[s], ph, abort_flag, a.status, kErrTimeoutFull)) break;
     const uint4* w0 = reinterpret_cast<const uint4*>(smem_raw + s * stage_bytes) + warp * vec;
     const int row = rb * kRB + warp;  // this warp's (first) output row
     for (int p0 = t.y; p0 < t.z; p0 += kGemvMaxRecs) {
@@ -559,10 +555,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
       int rows[kGemvMaxRecs];
 #pragma unroll
       for (int r = 0; r < kGemvMaxRecs; ++r) rows[r] = __shfl_sync(0xffffffffu, my_row, r);
-      if (n == 1) gemv_pass<SWIGLU, 1>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
-      else if (n == 2) gemv_pass<SWIGLU, 2>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
-      else if (n <= 4) gemv_pass<SWIGLU, 4>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
-      else gemv_pass<SWIGLU, 8>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
+      if (n == 1)
+        gemv_pass<SWIGLU, 1, ACT>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
+      else if (n == 2)
+        gemv_pass<SWIGLU, 2, ACT>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
+      else if (n <= 4)
+        gemv_pass<SWIGLU, 4, ACT>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
+      else
+        gemv_pass<SWIGLU, 8, ACT>(a, w0, p0, n, row, rows, my_out, my_scale, bad, vec, lane);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
@@ -570,6 +570,296 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
       s = 0;
       ph ^= 1u;
     }
+  }
+}
+
+template <bool SWIGLU>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  constexpr int kRB = gemv_row_block<SWIGLU>();
+  const uint32_t stage_bytes = (SWIGLU ? 2u : 1u) * static_cast<uint32_t>(kRB) * a.K * 2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + a.stages * stage_bytes);
+  uint64_t* empty = full + kGemvMaxStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kGemvMaxStages);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGemvConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+
+  const int nt = max(0, min(*a.num_tiles, a.max_tiles));
+  long long lo, hi;
+  balanced_range(a, nt, a.N / kRB, &lo, &hi);
+  stream_items<SWIGLU>(a, smem_raw, full, empty, abort_flag, nt, lo, hi);
+}
+
+// ------------------------------------------------------------------ single-launch decode layer
+//
+// decode_layer_fused: the whole MoE layer for at most kFusedMaxRecs routing
+// records (T * k <= 32: T <= 4 tokens at top-8) in one cooperative launch of
+// one CTA per SM, the phases separated by grid-wide barriers:
+//   1  router logits, one expert per CTA (the arithmetic of router_sort_small)
+//   -  barrier
+//   2  every CTA takes the top-k of every token from the logits and sorts the
+//      records by expert (stable; one tile per expert) in its shared memory
+//   3  gate/up + SwiGLU as gemv_stream<true>, the down weights of the routed
+//      experts prefetched into L2 behind this CTA's own copies
+//   -  barrier
+//   4  down projection with the routing weights as gemv_stream<false>, to the
+//      slot rows n*k + j
+//   -  barrier
+//   5  y[n] = sum_j slots[n*k + j] in fp32 in slot order (combine_rows)
+// Four launches (router + sort, two GEMVs, combine) become one: no launch
+// gaps, no kernel start-up or tail between the steps, the router spread over
+// 128 SMs instead of one 8-CTA cluster.  Every phase does the arithmetic of
+// the kernel it replaces, so the output is bitwise that of the four-launch
+// path.  The grid barriers count arrivals on counters the launcher zeroes;
+// every wait is bounded (kErrTimeoutGrid), and a CTA that gives up skips the
+// rest of the layer.
+
+constexpr int kFusedMaxRecs = kGemvW2MaxRows;
+
+struct DecodeArgs {
+  const uint4* x;          // [T][H]
+  const uint4* wr;         // [E][H]
+  const float* bias;       // [E] or null
+  int T, H, I, E, k, norm_topk_prob;
+  const __nv_bfloat16* w_gate;
+  const __nv_bfloat16* w_up;
+  const __nv_bfloat16* w_down;
+  float* logits;           // scratch [T][E]
+  __nv_bfloat16* h;        // scratch [T*k][I]
+  __nv_bfloat16* slots;    // scratch [T*k][H]
+  unsigned int* bar;       // three counters, zero at launch
+  uint4* y;                // [T][H]
+  int stages3, stages4;
+  int* status;
+};
+
+// All CTAs of the grid arrive on *ctr and wait until gridDim.x have arrived.
+// False (and the CTA's abort flag raised) once the bounded wait gives up or
+// the CTA has aborted before.
+__device__ bool grid_barrier(unsigned int* ctr, volatile int* abort_flag, int* status) {
+  __syncthreads();
+  if (threadIdx.x == 0 && !*abort_flag) {
+    __threadfence();
+    atomicAdd(ctr, 1u);
+    const unsigned long long t0 = globaltimer_ns();
+    for (;;) {
+      unsigned int v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+      if (v >= gridDim.x) break;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_status(status, kErrTimeoutGrid);
+        *abort_flag = 1;
+        break;
+      }
+      __nanosleep(32);
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  return *abort_flag == 0;
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 1) decode_layer_fused(const DecodeArgs d) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];  // ring, then both phases' barriers
+  __shared__ int s_ids[kFusedMaxRecs];
+  __shared__ float s_w[kFusedMaxRecs];   // routing weight of slot n*k + j
+  __shared__ int s_perm[kFusedMaxRecs];  // slot of the p-th record in expert order
+  __shared__ int4 s_tiles[kFusedMaxRecs];
+  __shared__ int s_nt;
+  uint64_t* full3 = reinterpret_cast<uint64_t*>(smem_raw + kGemvRingBytes);
+  uint64_t* empty3 = full3 + kGemvMaxStages;
+  uint64_t* full4 = empty3 + kGemvMaxStages;
+  uint64_t* empty4 = full4 + kGemvMaxStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty4 + kGemvMaxStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < d.stages3; ++s) {
+      mbar_init(&full3[s], 1);
+      mbar_init(&empty3[s], kGemvConsumerWarps);
+    }
+    for (int s = 0; s < d.stages4; ++s) {
+      mbar_init(&full4[s], 1);
+      mbar_init(&empty4[s], kGemvConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int vec = d.H / 8, R = d.T * d.k;
+
+  // ---------------------------------------------------------- 1: router logits
+  if (warp == 0) {
+    for (int e = blockIdx.x; e < d.E; e += gridDim.x) {
+      const uint4* row = d.wr + static_cast<size_t>(e) * vec;
+      const float be = d.bias != nullptr ? d.bias[e] : 0.0f;
+      for (int t = 0; t < d.T; ++t) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const uint4* xr = d.x + static_cast<size_t>(t) * vec;
+#pragma unroll
+        for (int j = 0; j < kRouterMaxVecPerLane; ++j) {
+          const int v = lane + 32 * j;
+          if (v < vec) dot8_acc(__ldg(row + v), __ldg(xr + v), acc);
+        }
+        const float sum = warp_sum(acc_sum(acc));
+        if (lane == 0) d.logits[t * d.E + e] = bf16_round_f(sum + be);
+      }
+    }
+  }
+  if (!grid_barrier(d.bar + 0, abort_flag, d.status)) return;
+
+  // ------------------------------------------------- 2: top-k and the record sort
+  for (int t = warp; t < d.T; t += kGemvThreads / 32) {  // one warp per token
+    const float* lg = d.logits + t * d.E;
+    uint32_t top[kRouterMaxK];
+#pragma unroll
+    for (int i = 0; i < kRouterMaxK; ++i) top[i] = 0u;
+    for (int c = lane; c < d.E; c += 32) topk_insert(top, topk_key(__ldcg(lg + c), c));
+    uint32_t sel[kRouterMaxK];
+#pragma unroll
+    for (int i = 0; i < kRouterMaxK; ++i) {
+      const uint32_t m = __reduce_max_sync(0xffffffffu, top[0]);
+      sel[i] = m;
+      if (top[0] == m) {
+#pragma unroll
+        for (int j = 0; j + 1 < kRouterMaxK; ++j) top[j] = top[j + 1];
+        top[kRouterMaxK - 1] = 0u;
+      }
+    }
+    const float ref = topk_key_value(sel[0]);
+    float den = 0.0f;
+    if (d.norm_topk_prob) {
+#pragma unroll
+      for (int i = 0; i < kRouterMaxK; ++i)
+        if (i < d.k) den += expf(topk_key_value(sel[i]) - ref);
+    } else {
+      for (int c = lane; c < d.E; c += 32) den += expf(__ldcg(lg + c) - ref);
+      den = warp_sum(den);
+    }
+    const float inv = 1.0f / den;
+#pragma unroll
+    for (int i = 0; i < kRouterMaxK; ++i) {
+      if (i < d.k && lane == i) {
+        s_ids[t * d.k + i] = topk_key_id(sel[i]);
+        s_w[t * d.k + i] = expf(topk_key_value(sel[i]) - ref) * inv;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // Stable sort of the R <= 32 records by expert, lane r = slot r, over
+    // shuffles: a record's position counts the records with a smaller id or
+    // the same id and a lower slot; one tile per expert, ascending ids.
+    const int my = lane < R ? s_ids[lane] : 0x7fffffff;
+    int pos = 0, before = 0, same = 0;
+    bool first = lane < R;
+    for (int j = 0; j < R; ++j) {
+      const int o = __shfl_sync(0xffffffffu, my, j);
+      pos += (o < my || (o == my && j < lane)) ? 1 : 0;
+      before += o < my ? 1 : 0;
+      same += o == my ? 1 : 0;
+      if (o == my && j < lane) first = false;
+    }
+    int tile = 0;
+    for (int j = 0; j < R; ++j) {
+      const int o = __shfl_sync(0xffffffffu, my, j);
+      const bool f = __shfl_sync(0xffffffffu, first ? 1 : 0, j) != 0;
+      tile += (f && o < my) ? 1 : 0;
+    }
+    if (lane < R) s_perm[pos] = lane;
+    if (first) s_tiles[tile] = make_int4(my, before, before + same, 0);
+    const int n_tiles = __popc(__ballot_sync(0xffffffffu, first));
+    if (lane == 0) s_nt = n_tiles;
+  }
+  __syncthreads();
+  const int nt = s_nt;
+
+  // ------------------------------------------------------------- 3: gate/up
+  StreamArgs a{};
+  a.act = d.x;
+  a.act_rows = d.T;
+  a.index = s_perm;
+  a.index_div = d.k;
+  a.M = R;
+  a.tiles = s_tiles;
+  a.num_tiles = &s_nt;
+  a.max_tiles = kFusedMaxRecs;
+  a.w0 = d.w_gate;
+  a.w1 = d.w_up;
+  a.E = d.E;
+  a.K = d.H;
+  a.N = d.I;
+  a.out = d.h;
+  a.out_rows = R;
+  a.stages = d.stages3;
+  a.status = d.status;
+  a.next_w = d.w_down;
+  a.next_N = d.H;
+  a.next_K = d.I;
+  // Both phases' item ranges depend only on the tile table: computed here, so
+  // the down phase starts streaming as soon as its barrier opens.
+  const int hvec = d.I / 8;
+  uint4* sh_h = reinterpret_cast<uint4*>(
+      smem_raw + static_cast<size_t>(d.stages4) * gemv_row_block<false>() * d.I * 2);
+  StreamArgs b{};
+  b.act = sh_h;
+  b.act_rows = R;
+  b.index_div = 1;
+  b.M = R;
+  b.tiles = s_tiles;
+  b.num_tiles = &s_nt;
+  b.max_tiles = kFusedMaxRecs;
+  b.w0 = d.w_down;
+  b.E = d.E;
+  b.K = d.I;
+  b.N = d.H;
+  b.out = d.slots;
+  b.row_map = s_perm;
+  b.row_scale = s_w;
+  b.out_rows = R;
+  b.stages = d.stages4;
+  b.status = d.status;
+  long long lo3, hi3, lo4, hi4;
+  balanced_range(a, nt, d.I / gemv_row_block<true>(), &lo3, &hi3);
+  __syncthreads();  // every thread has its range before the shared result is reused
+  balanced_range(b, nt, d.H / gemv_row_block<false>(), &lo4, &hi4);
+  stream_items<true>(a, smem_raw, full3, empty3, abort_flag, nt, lo3, hi3);
+  if (!grid_barrier(d.bar + 1, abort_flag, d.status)) return;
+
+  // ----------------------------------------------------- 4: down, to slot rows
+  // The R rows of h (written by every CTA in phase 3) are staged in shared
+  // memory behind the ring's stages, so the dot products read them at once
+  // instead of waiting on L2 inside every pass.
+  for (int i = threadIdx.x; i < R * hvec; i += blockDim.x)
+    sh_h[i] = __ldcg(reinterpret_cast<const uint4*>(d.h) + i);
+  __syncthreads();
+  stream_items<false, kActPlain>(b, smem_raw, full4, empty4, abort_flag, nt, lo4, hi4);
+  if (!grid_barrier(d.bar + 2, abort_flag, d.status)) return;
+
+  // --------------------------------------------------------------- 5: combine
+  const uint4* sl = reinterpret_cast<const uint4*>(d.slots);
+  const long long total = static_cast<long long>(d.T) * vec;
+  for (long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; g < total;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int n = static_cast<int>(g / vec);
+    const int v = static_cast<int>(g - static_cast<long long>(n) * vec);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < d.k; ++j)
+      acc_bf16x8(acc, __ldcg(sl + static_cast<size_t>(n * d.k + j) * vec + v), 1.0f);
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    d.y[g] = o;
   }
 }
 
@@ -701,6 +991,73 @@ int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles
   a.out_rows = out_rows;
   a.status = status;
   return launch_stream<false>(a, stream);
+}
+
+bool fused_decode_ok(int T, int H, int I, int E, int k) {
+  const long long R = static_cast<long long>(T) * k;
+  // the down phase keeps two ring stages and the R rows of h in shared memory
+  const long long down_smem = 2LL * gemv_row_block<false>() * I * 2 + R * I * 2;
+  return R >= 1 && R <= kFusedMaxRecs && router_small_ok(T, H, E, k) && gemv_ok(I, H, true) &&
+         gemv_ok(H, I, false) && down_smem <= kGemvRingBytes;
+}
+
+size_t fused_decode_scratch_bytes(int T, int E) {
+  return (static_cast<size_t>(T) * E * sizeof(float) + 255) / 256 * 256 + 256;
+}
+
+int launch_decode_fused(const void* x, const void* wr, const float* bias, int T, int H, int I,
+                        int E, int k, int norm_topk_prob, const void* w_gate, const void* w_up,
+                        const void* w_down, void* scratch, void* h, void* slots, void* y,
+                        int* status, cudaStream_t stream) {
+  if (!fused_decode_ok(T, H, I, E, k)) return kRcUnsupported;
+  if (!aligned16(x) || !aligned16(wr) || !aligned16(w_gate) || !aligned16(w_up) ||
+      !aligned16(w_down) || !aligned16(h) || !aligned16(slots) || !aligned16(y) ||
+      scratch == nullptr)
+    return kRcBadArgument;
+  DecodeArgs d{};
+  d.x = static_cast<const uint4*>(x);
+  d.wr = static_cast<const uint4*>(wr);
+  d.bias = bias;
+  d.T = T;
+  d.H = H;
+  d.I = I;
+  d.E = E;
+  d.k = k;
+  d.norm_topk_prob = norm_topk_prob;
+  d.w_gate = static_cast<const __nv_bfloat16*>(w_gate);
+  d.w_up = static_cast<const __nv_bfloat16*>(w_up);
+  d.w_down = static_cast<const __nv_bfloat16*>(w_down);
+  d.logits = static_cast<float*>(scratch);
+  d.bar = reinterpret_cast<unsigned int*>(
+      static_cast<uint8_t*>(scratch) + fused_decode_scratch_bytes(T, E) - 256);
+  d.h = static_cast<__nv_bfloat16*>(h);
+  d.slots = static_cast<__nv_bfloat16*>(slots);
+  d.y = static_cast<uint4*>(y);
+  d.stages3 = gemv_stages(H, true);
+  // phase 4 leaves room behind its stages for the T*k rows of h
+  const long long stage4 = static_cast<long long>(gemv_row_block<false>()) * I * 2;
+  const long long h_bytes = static_cast<long long>(T) * k * I * 2;
+  d.stages4 = static_cast<int>(
+      std::min<long long>(gemv_stages(I, false), (kGemvRingBytes - h_bytes) / stage4));
+  if (d.stages4 < 2) return kRcUnsupported;
+  d.status = status;
+  const size_t sh = kGemvRingBytes + 4 * kGemvMaxStages * sizeof(uint64_t) + 16;
+  static std::atomic<uint64_t> attr{0};
+  if (!allow_smem(decode_layer_fused, static_cast<int>(sh), attr)) return kRcCudaError;
+  if (cudaMemsetAsync(d.bar, 0, 3 * sizeof(unsigned int), stream) != cudaSuccess)
+    return kRcCudaError;
+  // Cooperative: every CTA is resident at once, as the grid barriers need.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(device_sm_count());
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = sh;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeCooperative;
+  attrs[0].val.cooperative = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_layer_fused, d) == cudaSuccess ? kRcOk : kRcCudaError;
 }
 
 }  // namespace moe

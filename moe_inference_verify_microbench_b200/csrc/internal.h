@@ -132,6 +132,17 @@ int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles
                    const float* row_scale, void* out, int out_rows, int* status,
                    cudaStream_t stream);
 
+// Whole decode layer in one cooperative launch (T * k <= kGemvW2MaxRows records):
+// router, top-k, sort, gate/up and down GEMVs and the k-way combine, bitwise
+// equal to the four-launch decode path.  `scratch` holds
+// fused_decode_scratch_bytes(T, E) bytes; h [T*k, I] and slots [T*k, H] bf16.
+bool fused_decode_ok(int T, int H, int I, int E, int k);
+size_t fused_decode_scratch_bytes(int T, int E);
+int launch_decode_fused(const void* x, const void* wr, const float* bias, int T, int H, int I,
+                        int E, int k, int norm_topk_prob, const void* w_gate, const void* w_up,
+                        const void* w_down, void* scratch, void* h, void* slots, void* y,
+                        int* status, cudaStream_t stream);
+
 // Down GEMM with the atomic combine: out_f32[row_map[p] / red_div] +=
 // row_scale[row_map[p]] * (h[p] @ w_down[e]^T) in fp32 (row_map[p] < n_slots).
 int launch_w2_atomic(const void* h, int M, const int4* tiles, const int* num_tiles,

@@ -22,6 +22,7 @@ enum StatusCode : int {
   kErrTimeoutAccFull = 0x103,  // epilogue: accumulator never committed
   kErrTimeoutAccEmpty = 0x104, // MMA warp: accumulator never drained
   kErrPeerTimeout = 0x105,     // expert-parallel exchange: a peer rank never signalled
+  kErrTimeoutGrid = 0x106,     // a grid-wide barrier of a single-launch layer never completed
   kErrBadExpert = 0x201,       // an expert id outside [0, E)
   kErrBadRow = 0x202,          // a tile row range outside the A operand
 };
@@ -380,6 +381,17 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t M, uint32_t N) {
 
 __device__ __forceinline__ float bf16_round_f(float v) {
   return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// acc[i] += w * v[i] for the eight bf16 values of v, in fp32 (fmaf).
+__device__ __forceinline__ void acc_bf16x8(float (&acc)[8], const uint4& v, float w) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    acc[2 * i] = fmaf(w, f.x, acc[2 * i]);
+    acc[2 * i + 1] = fmaf(w, f.y, acc[2 * i + 1]);
+  }
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -55,16 +55,6 @@ __global__ void __launch_bounds__(kRowsThreads) gather_rows(const uint4* __restr
   }
 }
 
-__device__ __forceinline__ void acc_bf16x8(float (&acc)[8], const uint4& v, float w) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h[i]);
-    acc[2 * i] = fmaf(w, f.x, acc[2 * i]);
-    acc[2 * i + 1] = fmaf(w, f.y, acc[2 * i + 1]);
-  }
-}
-
 constexpr int kCombineMaxK = 8;  // the router selects at most 8 experts
 
 // One thread per (token, 16-byte column vector): the k source rows' vectors are

@@ -31,9 +31,10 @@ def _init(rank, world, port):
     return dev
 
 
-def _fixture_worker(rank, world, port, name, transport, q):
-    sys.path.insert(0, HERE)
-    sys.path.insert(0, os.path.dirname(HERE))
+def _check_fixture(rank, world, dev, name, transport):
+    """One rank's forward of the fixture's schedule on its transport: (relative
+    error against the reference's own output on tokens without a top-k
+    boundary tie, fraction of tied tokens)."""
     import torch.distributed as dist
     from helpers import load_golden, to_t
     from moe_inference_verify_microbench_b200 import ops
@@ -42,50 +43,58 @@ def _fixture_worker(rank, world, port, name, transport, q):
     from moe_inference_verify_microbench_b200.hybrid import HybridMoE
     from oracle import moe_oracle as mo
 
+    g = load_golden(name)
+    T, H, I, E, k, tp = (int(g[n]) for n in ("T", "H", "I", "E", "k", "tp"))
+    d = mo.make_inputs(T * world, H, I, E, int(g["seed"]))
+    xall = to_t(d["x"], dev)
+    wr = to_t(d["wr"], dev)
+    wg = [to_t(d["w_gate"][e], dev) for e in range(E)]
+    wu = [to_t(d["w_up"][e], dev) for e in range(E)]
+    wd = [to_t(d["w_down"][e], dev) for e in range(E)]
+    kind = str(g["kind"])
+    with torch.device(dev):
+        if kind == "c6":
+            mod = Lean(H, I, E, k, world, rank, group=None)
+            x = xall[:T]
+        elif kind == "c7":
+            mod = Pure(H, I, E, k, world, rank, group=None, transport=transport)
+            x = xall[rank * T:(rank + 1) * T]
+        else:
+            groups = [dist.new_group(list(range(i * tp, (i + 1) * tp))) for i in range(world // tp)]
+            mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None,
+                            transport=transport)
+            x = xall[(rank // tp) * T:(rank // tp + 1) * T]
+        mod = mod.to(torch.bfloat16)
+    mod.weight_loader(wr, wg, wu, wd)
+    bias = None
+    if int(g["zipf"]):
+        lin = torch.nn.Linear(H, E, bias=True).to(torch.bfloat16).to(dev)
+        lin.weight.data.copy_(wr)
+        lin.bias.data.copy_(torch.from_numpy(mo.zipf_bias(E)).to(torch.bfloat16))
+        mod.gate = lin
+        bias = lin.bias.float()
+    with torch.no_grad():
+        y = mod(x.contiguous())
+        _, _, lg = ops.router_topk(x.contiguous(), mod.gate.weight, k, bias=bias, return_logits=True)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    srt = torch.sort(lg.float(), dim=-1, descending=True).values
+    tie = (srt[:, k - 1] == srt[:, k]).cpu().numpy()
+    yref = mo.f32_from_bf16_bits(g[f"y_rank{rank}"])
+    if hasattr(mod, "close"):
+        mod.close()
+    dist.barrier()
+    return mo.rel_err(y.float().cpu().numpy()[~tie], yref[~tie]), float(tie.mean())
+
+
+def _fixture_worker(rank, world, port, name, transport, q):
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
     dev = _init(rank, world, port)
     try:
-        g = load_golden(name)
-        T, H, I, E, k, tp = (int(g[n]) for n in ("T", "H", "I", "E", "k", "tp"))
-        d = mo.make_inputs(T * world, H, I, E, int(g["seed"]))
-        xall = to_t(d["x"], dev)
-        wr = to_t(d["wr"], dev)
-        wg = [to_t(d["w_gate"][e], dev) for e in range(E)]
-        wu = [to_t(d["w_up"][e], dev) for e in range(E)]
-        wd = [to_t(d["w_down"][e], dev) for e in range(E)]
-        kind = str(g["kind"])
-        with torch.device(dev):
-            if kind == "c6":
-                mod = Lean(H, I, E, k, world, rank, group=None)
-                x = xall[:T]
-            elif kind == "c7":
-                mod = Pure(H, I, E, k, world, rank, group=None, transport=transport)
-                x = xall[rank * T:(rank + 1) * T]
-            else:
-                groups = [dist.new_group(list(range(i * tp, (i + 1) * tp))) for i in range(world // tp)]
-                mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None,
-                                transport=transport)
-                x = xall[(rank // tp) * T:(rank // tp + 1) * T]
-            mod = mod.to(torch.bfloat16)
-        mod.weight_loader(wr, wg, wu, wd)
-        bias = None
-        if int(g["zipf"]):
-            lin = torch.nn.Linear(H, E, bias=True).to(torch.bfloat16).to(dev)
-            lin.weight.data.copy_(wr)
-            lin.bias.data.copy_(torch.from_numpy(mo.zipf_bias(E)).to(torch.bfloat16))
-            mod.gate = lin
-            bias = lin.bias.float()
-        with torch.no_grad():
-            y = mod(x.contiguous())
-            _, _, lg = ops.router_topk(x.contiguous(), mod.gate.weight, k, bias=bias, return_logits=True)
-        torch.cuda.synchronize()
-        ops.check_status(dev)
-        srt = torch.sort(lg.float(), dim=-1, descending=True).values
-        tie = (srt[:, k - 1] == srt[:, k]).cpu().numpy()
-        yref = mo.f32_from_bf16_bits(g[f"y_rank{rank}"])
-        q.put((rank, mo.rel_err(y.float().cpu().numpy()[~tie], yref[~tie]), float(tie.mean())))
-        if hasattr(mod, "close"):
-            mod.close()
-        dist.barrier()
+        err, tie = _check_fixture(rank, world, dev, name, transport)
+        q.put((rank, err, tie))
     finally:
         dist.destroy_process_group()
 
@@ -166,44 +175,90 @@ def test_ep_full_shapes_match_single_gpu_layer(kind):
         assert err <= 1e-2, (rank, err)
 
 
-def _peer_worker(rank, world, port, q):
-    sys.path.insert(0, HERE)
-    sys.path.insert(0, os.path.dirname(HERE))
+def _check_peer_vs_nccl(rank, world, dev):
+    """Four forwards with ragged per-rank token counts on both transports:
+    whether each pair of outputs is bit-identical."""
     import torch.distributed as dist
     from moe_inference_verify_microbench_b200 import ops
     from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
 
+    H, I, E, k, T = 2048, 768, 128, 8, 2048
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wg = (torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wu = (torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    wd = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    mods = {}
+    for tr in ("nccl", "peer"):
+        with torch.device(dev):
+            mods[tr] = Pure(H, I, E, k, world, rank, group=None, transport=tr).to(torch.bfloat16)
+        mods[tr].weight_loader(wr, list(wg), list(wu), list(wd))
+    same = []
+    g.manual_seed(100 + rank)
+    with torch.no_grad():
+        for step in range(4):  # epochs; ragged token counts per step and rank
+            n = T - 97 * ((step + rank) % 3)
+            x = torch.randn(n, H, generator=g, device=dev).to(torch.bfloat16)
+            dist.barrier()
+            y_peer = mods["peer"](x)
+            y_nccl = mods["nccl"](x)
+            same.append(bool(torch.equal(y_peer, y_nccl)))
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    mods["peer"].close()
+    dist.barrier()
+    return same
+
+
+def _peer_worker(rank, world, port, q):
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
     dev = _init(rank, world, port)
     try:
-        H, I, E, k, T = 2048, 768, 128, 8, 2048
-        g = torch.Generator(device=dev)
-        g.manual_seed(11)
-        wr = (torch.randn(E, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        wg = (torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        wu = (torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        wd = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        mods = {}
-        for tr in ("nccl", "peer"):
-            with torch.device(dev):
-                mods[tr] = Pure(H, I, E, k, world, rank, group=None, transport=tr).to(torch.bfloat16)
-            mods[tr].weight_loader(wr, list(wg), list(wu), list(wd))
-        same = []
-        g.manual_seed(100 + rank)
-        with torch.no_grad():
-            for step in range(4):  # epochs; ragged token counts per step and rank
-                n = T - 97 * ((step + rank) % 3)
-                x = torch.randn(n, H, generator=g, device=dev).to(torch.bfloat16)
-                dist.barrier()
-                y_peer = mods["peer"](x)
-                y_nccl = mods["nccl"](x)
-                same.append(bool(torch.equal(y_peer, y_nccl)))
-        torch.cuda.synchronize()
-        ops.check_status(dev)
-        mods["peer"].close()
-        q.put((rank, same))
-        dist.barrier()
+        q.put((rank, _check_peer_vs_nccl(rank, world, dev)))
     finally:
         dist.destroy_process_group()
+
+
+EP_FIXTURES = {2: ["ep_c6_w2.npz", "ep_c7_w2.npz"],
+               4: ["ep_c6_w4.npz", "ep_c7_w4_zipf.npz", "ep_c8_w4_tp2.npz"],
+               8: ["ep_c6_w8.npz", "ep_c7_w8_zipf.npz", "ep_c8_w8_tp2.npz", "ep_c8_w8_tp4.npz"]}
+
+
+def _all_worker(rank, world, port, q):
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
+    dev = _init(rank, world, port)
+    try:
+        res = {}
+        for name in EP_FIXTURES[world]:
+            for tr in (("nccl",) if "_c6_" in name else ("nccl", "peer")):
+                res[f"{name}/{tr}"] = _check_fixture(rank, world, dev, name, tr)
+        res["peer_bits_equal_nccl"] = _check_peer_vs_nccl(rank, world, dev)
+        q.put((rank, res))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_all_schedules_in_one_process_group(world):
+    """Every expert-parallel fixture of this world size (C6; C7 and C8 on both
+    transports) against the reference's own per-rank outputs, and the peer
+    transport bit-identical to NCCL, in ONE process group: the same checks
+    as the per-fixture tests, for a fraction of their start-up cost."""
+    _need(world)
+    res = _spawn(_all_worker, world, (29700 + world,))
+    for rank, r in res:
+        for key, v in r.items():
+            if key == "peer_bits_equal_nccl":
+                assert all(v), (rank, v)
+            else:
+                err, tie = v
+                assert tie <= 0.2, (rank, key, tie)
+                assert err <= 2e-2, (rank, key, err)
 
 
 @pytest.mark.parametrize("world", [2, 8])

@@ -360,6 +360,37 @@ def test_gemv_w13_w2_small_batches(cuda, counts, H, I):
     assert mo.rel_err(to_f32(out), ref_o) <= 1e-2
 
 
+@pytest.mark.parametrize("T,norm,with_bias", [(1, True, False), (2, False, False), (4, True, True)])
+def test_single_launch_decode_layer_bitwise(cuda, T, norm, with_bias):
+    """Up to 32 routing records (T <= 4 at top-8) run the whole layer as one
+    cooperative launch (router, top-k, sort, both GEMVs and the combine, with
+    grid barriers between them).  Its output must equal the four-launch
+    decode pipeline, op by op through the C ABI, bit for bit, at the full
+    shapes (H=2048 I=768 E=128 k=8)."""
+    H, I, E, k = 2048, 768, 128, 8
+    g = torch.Generator(device=cuda)
+    g.manual_seed(500 + T)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=g, device=cuda).to(bf)
+    wr = (torch.randn(E, H, generator=g, device=cuda) * 0.02).to(bf)
+    wg = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wu = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wd = (torch.randn(E, H, I, generator=g, device=cuda) * 0.02).to(bf)
+    bias = torch.randn(E, generator=g, device=cuda) * 0.1 if with_bias else None
+    y = ops.moe_layer(x, wr, wg, wu, wd, k, norm_topk_prob=norm, bias=bias)
+    y_again = ops.moe_layer(x, wr, wg, wu, wd, k, norm_topk_prob=norm, bias=bias)
+    ids, w, _ = ops.router_topk(x, wr, k, norm_topk_prob=norm, bias=bias)
+    s = ops.sort_align(ids, E)
+    h = ops.grouped_w13_swiglu_gather(x, s.perm, k, T * k, s.tiles, s.num_tiles, s.max_tiles,
+                                      wg, wu)
+    sl = ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, wd, row_map=s.perm,
+                        slot_scale=w.reshape(-1))
+    y2 = ops.combine(sl, T, k)
+    ops.check_status(cuda)
+    assert torch.equal(y, y2)
+    assert torch.equal(y, y_again)
+
+
 @pytest.mark.parametrize("T,k,E", [(1, 4, 16), (3, 8, 64), (16, 8, 128), (17, 4, 32)])
 def test_layer_decode_equals_op_by_op(cuda, T, k, E):
     """moe_layer_forward at decode sizes (fused router + sort, GEMV experts)
