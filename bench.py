@@ -269,6 +269,7 @@ def w13_kernel_name(tile_rows):
 
 SORT_CHUNK, SORT_THREADS, CLUSTER_SORT_MAX, CLUSTER_CHUNK = 2048, 256, 8, 4096
 GEMV_W13_MAX_ROWS, ROUTER_SMALL_MAX_T = 128, 16
+FUSED_DECODE_MAX_T, FUSED_DECODE_MAX_RECS = 4, 32
 
 
 def sort_launches(R: int, e_local: int = E) -> int:
@@ -283,12 +284,15 @@ def sort_launches(R: int, e_local: int = E) -> int:
 
 
 def layer_launches(T, tile_rows=None):
-    """Kernels moe_layer_forward launches for T tokens.  Decode (T*k <= 128
-    records): router and sort fused in one kernel for T <= 16, the gate/up
+    """Kernels moe_layer_forward launches for T tokens.  Up to 4 tokens and 32
+    records: the single-launch decode layer.  Decode (T*k <= 128 records):
+    router and sort fused in one kernel for T <= 16, the gate/up
     weight-streaming kernel, the down GEMV or GEMM, the combine.  Otherwise:
     router, sort (``sort_launches``), gate/up GEMM with the row gather fused,
     down GEMM, combine."""
     R = T * K_TOP
+    if 0 < T <= FUSED_DECODE_MAX_T and R <= FUSED_DECODE_MAX_RECS:
+        return 1
     if 0 < R <= GEMV_W13_MAX_ROWS:
         return (1 if T <= ROUTER_SMALL_MAX_T else 1 + sort_launches(R)) + 3
     return 1 + sort_launches(R) + 3
@@ -575,6 +579,12 @@ def main():
     ap.add_argument("--tp", type=int, default=2, help="c8: tensor-parallel group size")
     ap.add_argument("--zipf", action="store_true",
                     help="N>1: Zipf(1.2) router bias (the skewed-routing C7 configuration)")
+    ap.add_argument("--ep-overlap", dest="ep_overlap", type=int, nargs="?", const=2, default=0,
+                    metavar="CHUNKS",
+                    help="N>1, peer transport: CHUNKS (default 2) token chunks, each chunk's "
+                         "exchange overlapping the other chunks' GEMMs")
+    ap.add_argument("--exchange-sms", type=int, default=16,
+                    help="--ep-overlap: SMs the GEMMs leave to the exchange kernels")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--sweep", default="1,16,128,1024,4096",
                     help="comma-separated token counts for the graph-captured sweep ('' = none)")

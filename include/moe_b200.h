@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define MOE_B200_ABI_VERSION 4
+#define MOE_B200_ABI_VERSION 5
 
 #define MOE_RC_OK 0
 #define MOE_RC_BAD_ARGUMENT (-1)
@@ -288,6 +288,56 @@ MOE_API int moe_grouped_w2_atomic_rows(const void* h, int M, const int32_t* tile
                                        int n_slots, int red_div, float* out_f32, int tile_rows,
                                        int32_t* status, cudaStream_t stream);
 MOE_API int moe_cast_f32_to_bf16(const float* src, long long n, void* y, cudaStream_t stream);
+
+/*
+ * ABI 5: an SM budget for the grouped GEMMs.  The persistent GEMMs take one
+ * CTA per SM on every SM; these variants of moe_grouped_w13_swiglu_gather_rows
+ * and moe_grouped_w2_rows use at most `max_sms` SMs (<= 0: all), leaving the
+ * others to work the caller runs at the same time on another stream -- the
+ * expert-parallel exchange of the next token chunk while this chunk's expert
+ * GEMMs run (the pipelined form of C7/python/solution.py:186-261).  Results
+ * are bitwise those of the unbudgeted calls.  moe_device_sm_count() is the
+ * current device's SM count.
+ */
+MOE_API int moe_device_sm_count(void);
+MOE_API int moe_grouped_w13_swiglu_gather_ex(const void* src, int src_rows, const int32_t* index,
+                                             int index_div, int M, const int32_t* tiles,
+                                             const int32_t* num_tiles, int max_tiles,
+                                             const void* w_gate, const void* w_up, int E, int H,
+                                             int I, void* h, int tile_rows, int max_sms,
+                                             int32_t* status, cudaStream_t stream);
+MOE_API int moe_grouped_w2_ex(const void* h, int M, const int32_t* tiles,
+                              const int32_t* num_tiles, int max_tiles, const void* w_down, int E,
+                              int H, int I, const int32_t* row_map, const float* slot_scale,
+                              void* out, int out_rows, int tile_rows, int max_sms,
+                              int32_t* status, cudaStream_t stream);
+
+/*
+ * ABI 5: the decode layer in one launch and one pass over the weights, for a
+ * caller that also keeps the down weights transposed: w_down_t [E][I][H] bf16
+ * (w_down_t[e][i][h] = w_down[e][h][i], built once next to the weights).
+ * T <= 4 tokens and T * top_k <= 32 records (C5/python/solution.py:108-161
+ * for a decode batch).  Router, top-k and sort as moe_layer_forward's decode
+ * path; then every CTA streams 8-row slices of gate, up and w_down_t of the
+ * routed experts, forms h for those rows and adds their share of the down
+ * projection to fp32 partials, summed across CTAs after one grid barrier.
+ * The result equals moe_layer_forward's up to fp32 summation order over I.
+ * No fallback: MOE_RC_UNSUPPORTED for a shape outside the bounds (also H > 2048
+ * or I % 8 != 0), MOE_RC_CUDA if the cooperative launch fails.  workspace
+ * holds moe_decode_layer_workspace_bytes(T, H, E) bytes, 16-byte aligned.
+ *
+ * moe_last_cuda_error: the cudaError_t value of the most recent CUDA call
+ * that failed inside this library's launchers on the calling thread (0 when
+ * none has), for diagnosing MOE_RC_CUDA.
+ */
+MOE_API size_t moe_decode_layer_workspace_bytes(int T, int H, int E);
+MOE_API int moe_decode_layer_split(const void* x, const void* router_weight,
+                                   const float* router_bias, const void* w_gate,
+                                   const void* w_up, const void* w_down_t, int T, int H, int I,
+                                   int E, int top_k, int norm_topk_prob, void* workspace,
+                                   size_t workspace_bytes, void* y, int32_t* status,
+                                   cudaStream_t stream);
+MOE_API int moe_last_cuda_error(void);
 
 /*
  * Decoder-block glue around the MoE (C8/python/solution.py:235-325, whose

@@ -82,9 +82,21 @@ SIGNATURES: dict[str, tuple] = {
     "moe_cast_f32_to_bf16": (_c_int, [_ptr, ctypes.c_longlong, _ptr, _ptr]),
     "moe_add_rmsnorm": (_c_int, [_ptr, _ptr, _ptr, _c_int, _c_int, ctypes.c_float, _ptr, _ptr,
                                  _ptr]),
+    # ABI 5: SM budget for the grouped GEMMs
+    "moe_device_sm_count": (_c_int, []),
+    "moe_grouped_w13_swiglu_gather_ex": (_c_int, [_ptr, _c_int, _ptr, _c_int, _c_int, _ptr, _ptr,
+                                                  _c_int, _ptr, _ptr, _c_int, _c_int, _c_int,
+                                                  _ptr, _c_int, _c_int, _ptr, _ptr]),
+    "moe_grouped_w2_ex": (_c_int, [_ptr, _c_int, _ptr, _ptr, _c_int, _ptr, _c_int, _c_int, _c_int,
+                                   _ptr, _ptr, _ptr, _c_int, _c_int, _c_int, _ptr, _ptr]),
+    # ABI 5: the one-pass decode layer on transposed down weights; last CUDA error
+    "moe_decode_layer_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int]),
+    "moe_decode_layer_split": (_c_int, [_ptr, _ptr, _ptr, _ptr, _ptr, _ptr, _c_int, _c_int, _c_int,
+                                        _c_int, _c_int, _c_int, _ptr, _c_size, _ptr, _ptr, _ptr]),
+    "moe_last_cuda_error": (_c_int, []),
 }
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None

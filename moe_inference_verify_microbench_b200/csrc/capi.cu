@@ -214,6 +214,50 @@ int moe_grouped_w13_swiglu_gather_rows(const void* src, int src_rows, const int3
                                   w_gate, w_up, E, H, I, h, status, stream, tile_rows);
 }
 
+int moe_device_sm_count(void) { return device_sm_count(); }
+
+size_t moe_decode_layer_workspace_bytes(int T, int H, int E) {
+  if (T <= 0 || H <= 0 || E <= 0) return 0;
+  return split_decode_scratch_bytes(T, H, E);
+}
+
+int moe_decode_layer_split(const void* x, const void* router_weight, const float* router_bias,
+                           const void* w_gate, const void* w_up, const void* w_down_t, int T,
+                           int H, int I, int E, int top_k, int norm_topk_prob, void* workspace,
+                           size_t workspace_bytes, void* y, int32_t* status, cudaStream_t stream) {
+  if (T <= 0 || H <= 0 || I <= 0 || E <= 0 || top_k <= 0 || w_down_t == nullptr)
+    return kRcBadArgument;
+  if (!split_decode_ok(T, H, I, E, top_k)) return kRcUnsupported;
+  if (workspace == nullptr || workspace_bytes < split_decode_scratch_bytes(T, H, E))
+    return kRcWorkspace;
+  return launch_decode_split(x, router_weight, router_bias, T, H, I, E, top_k, norm_topk_prob,
+                             w_gate, w_up, w_down_t, workspace, y, status, stream);
+}
+
+int moe_last_cuda_error(void) { return last_cuda_error(); }
+
+int moe_grouped_w13_swiglu_gather_ex(const void* src, int src_rows, const int32_t* index,
+                                     int index_div, int M, const int32_t* tiles,
+                                     const int32_t* num_tiles, int max_tiles, const void* w_gate,
+                                     const void* w_up, int E, int H, int I, void* h,
+                                     int tile_rows, int max_sms, int32_t* status,
+                                     cudaStream_t stream) {
+  if (tile_rows != MOE_BLOCK_M && tile_rows != MOE_PAIR_TILE_ROWS) return kRcBadArgument;
+  return launch_w13_swiglu_gather(src, src_rows, index, index_div, M,
+                                  reinterpret_cast<const int4*>(tiles), num_tiles, max_tiles,
+                                  w_gate, w_up, E, H, I, h, status, stream, tile_rows, nullptr,
+                                  max_sms);
+}
+
+int moe_grouped_w2_ex(const void* h, int M, const int32_t* tiles, const int32_t* num_tiles,
+                      int max_tiles, const void* w_down, int E, int H, int I,
+                      const int32_t* row_map, const float* slot_scale, void* out, int out_rows,
+                      int tile_rows, int max_sms, int32_t* status, cudaStream_t stream) {
+  if (tile_rows != MOE_BLOCK_M && tile_rows != MOE_PAIR_TILE_ROWS) return kRcBadArgument;
+  return launch_w2(h, M, reinterpret_cast<const int4*>(tiles), num_tiles, max_tiles, w_down, E, H,
+                   I, row_map, slot_scale, out, out_rows, status, stream, tile_rows, max_sms);
+}
+
 int moe_grouped_w2(const void* h, int M, const int32_t* tiles, const int32_t* num_tiles,
                    int max_tiles, const void* w_down, int E, int H, int I,
                    const int32_t* row_map, const float* slot_scale, void* out, int out_rows,

@@ -436,6 +436,77 @@ __device__ __forceinline__ void balanced_range(const StreamArgs& a, int nt, int 
 // stages, barriers full/empty, each used from phase 0), the consumer warps
 // apply them.  Every thread of the CTA calls it; `nt` is the tile count.
 // ACT: how the consumers read the A rows (ActLoad).
+// The producer side of stream_items: lane 0 of the calling warp copies the
+// weight rows of items [lo, hi) into the ring (a.stages stages, barriers
+// full/empty, each used from phase 0) and, for the gate/up GEMV, prefetches
+// the next GEMM's weights into L2 behind them.
+template <bool SWIGLU>
+__device__ __forceinline__ void produce_items(const StreamArgs& a, uint8_t* smem_raw,
+                                              uint64_t* full, uint64_t* empty,
+                                              volatile int* abort_flag, int nt, long long lo,
+                                              long long hi) {
+  const int lane = threadIdx.x & 31;
+  constexpr int kRB = gemv_row_block<SWIGLU>();
+  const uint32_t mat_bytes = static_cast<uint32_t>(kRB) * a.K * 2;  // one matrix's rows
+  const uint32_t stage_bytes = (SWIGLU ? 2u : 1u) * mat_bytes;
+  const int blocks = a.N / kRB;
+  if (lane == 0) {
+    int s = 0;
+    uint32_t ph = 0, issued = 0;
+    for (long long w = lo; w < hi; ++w) {
+      const int ti = static_cast<int>(w / blocks);
+      const int rb = static_cast<int>(w - static_cast<long long>(ti) * blocks);
+      const int4 t = a.tiles[ti];
+      if (t.x < 0 || t.x >= a.E || t.y < 0 || t.y > t.z || t.z > a.M) break;  // consumers report
+      if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.status, kErrTimeoutEmpty)) break;
+      mbar_arrive_expect_tx(&full[s], stage_bytes);
+      const size_t row0 = (static_cast<size_t>(t.x) * a.N + static_cast<size_t>(rb) * kRB) * a.K;
+      uint8_t* dst = smem_raw + s * stage_bytes;
+      bulk_load(dst, a.w0 + row0, mat_bytes, &full[s]);
+      if (SWIGLU) bulk_load(dst + mat_bytes, a.w1 + row0, mat_bytes, &full[s]);
+      ++issued;
+      if (++s == a.stages) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+    if (SWIGLU && a.next_w != nullptr && !*abort_flag) {
+      // This CTA's share of the next GEMM's weights, in kPrefetchRows-row
+      // requests, so the down projection streams from L2.  Issued after
+      // this GEMM's own copies, which are on the critical path (issuing the
+      // prefetch first measured slower at T=1 and 2).
+      const int nblk = a.next_N / kPrefetchRows;
+      const long long bytes_all =
+          static_cast<long long>(nt) * a.next_N * a.next_K * static_cast<long long>(2);
+      if (nblk > 0 && bytes_all <= kPrefetchMaxBytes) {
+        const long long total2 = static_cast<long long>(nt) * nblk;
+        const long long p_lo = total2 * blockIdx.x / gridDim.x;
+        const long long p_hi = total2 * (blockIdx.x + 1) / gridDim.x;
+        const uint32_t req = static_cast<uint32_t>(kPrefetchRows) * a.next_K * 2;
+        for (long long q = p_lo; q < p_hi; ++q) {
+          const int ti = static_cast<int>(q / nblk);
+          const int rb = static_cast<int>(q - static_cast<long long>(ti) * nblk);
+          const int e = a.tiles[ti].x;
+          if (e < 0 || e >= a.E) continue;
+          prefetch_l2_bulk(a.next_w + (static_cast<size_t>(e) * a.next_N +
+                                       static_cast<size_t>(rb) * kPrefetchRows) * a.next_K,
+                           req);
+        }
+      }
+    }
+    if (*abort_flag) {
+      // Let every copy still in flight land before the CTA exits.
+      const uint32_t first = issued > static_cast<uint32_t>(a.stages) ? issued - a.stages : 0u;
+      for (uint32_t i = first; i < issued; ++i) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[i % a.stages], (i / a.stages) & 1u)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        }
+      }
+    }
+  }
+}
+
 template <bool SWIGLU, int ACT = kActLdg>
 __device__ __forceinline__ void stream_items(const StreamArgs& a, uint8_t* smem_raw, uint64_t* full,
                              uint64_t* empty, volatile int* abort_flag, int nt, long long lo,
@@ -448,62 +519,7 @@ __device__ __forceinline__ void stream_items(const StreamArgs& a, uint8_t* smem_
   const int blocks = a.N / kRB;
 
   if (warp == kGemvConsumerWarps) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int s = 0;
-      uint32_t ph = 0, issued = 0;
-      for (long long w = lo; w < hi; ++w) {
-        const int ti = static_cast<int>(w / blocks);
-        const int rb = static_cast<int>(w - static_cast<long long>(ti) * blocks);
-        const int4 t = a.tiles[ti];
-        if (t.x < 0 || t.x >= a.E || t.y < 0 || t.y > t.z || t.z > a.M) break;  // consumers report
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.status, kErrTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&full[s], stage_bytes);
-        const size_t row0 = (static_cast<size_t>(t.x) * a.N + static_cast<size_t>(rb) * kRB) * a.K;
-        uint8_t* dst = smem_raw + s * stage_bytes;
-        bulk_load(dst, a.w0 + row0, mat_bytes, &full[s]);
-        if (SWIGLU) bulk_load(dst + mat_bytes, a.w1 + row0, mat_bytes, &full[s]);
-        ++issued;
-        if (++s == a.stages) {
-          s = 0;
-          ph ^= 1u;
-        }
-      }
-      if (SWIGLU && a.next_w != nullptr && !*abort_flag) {
-        // This CTA's share of the next GEMM's weights, in kPrefetchRows-row
-        // requests, so the down projection streams from L2.  Issued after
-        // this GEMM's own copies, which are on the critical path (issuing the
-        // prefetch first measured slower at T=1 and 2).
-        const int nblk = a.next_N / kPrefetchRows;
-        const long long bytes_all =
-            static_cast<long long>(nt) * a.next_N * a.next_K * static_cast<long long>(2);
-        if (nblk > 0 && bytes_all <= kPrefetchMaxBytes) {
-          const long long total2 = static_cast<long long>(nt) * nblk;
-          const long long p_lo = total2 * blockIdx.x / gridDim.x;
-          const long long p_hi = total2 * (blockIdx.x + 1) / gridDim.x;
-          const uint32_t req = static_cast<uint32_t>(kPrefetchRows) * a.next_K * 2;
-          for (long long q = p_lo; q < p_hi; ++q) {
-            const int ti = static_cast<int>(q / nblk);
-            const int rb = static_cast<int>(q - static_cast<long long>(ti) * nblk);
-            const int e = a.tiles[ti].x;
-            if (e < 0 || e >= a.E) continue;
-            prefetch_l2_bulk(a.next_w + (static_cast<size_t>(e) * a.next_N +
-                                         static_cast<size_t>(rb) * kPrefetchRows) * a.next_K,
-                             req);
-          }
-        }
-      }
-      if (*abort_flag) {
-        // Let every copy still in flight land before the CTA exits.
-        const uint32_t first = issued > static_cast<uint32_t>(a.stages) ? issued - a.stages : 0u;
-        for (uint32_t i = first; i < issued; ++i) {
-          const unsigned long long t0 = globaltimer_ns();
-          while (!mbar_try_wait(&full[i % a.stages], (i / a.stages) & 1u)) {
-            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-          }
-        }
-      }
-    }
+    produce_items<SWIGLU>(a, smem_raw, full, empty, abort_flag, nt, lo, hi);
     return;  // the producer warp has no consumer work
   }
 
@@ -668,61 +684,56 @@ __device__ bool grid_barrier(unsigned int* ctr, volatile int* abort_flag, int* s
   return *abort_flag == 0;
 }
 
-__global__ void __launch_bounds__(kGemvThreads, 1) decode_layer_fused(const DecodeArgs d) {
-  extern __shared__ __align__(128) uint8_t smem_raw[];  // ring, then both phases' barriers
-  __shared__ int s_ids[kFusedMaxRecs];
-  __shared__ float s_w[kFusedMaxRecs];   // routing weight of slot n*k + j
-  __shared__ int s_perm[kFusedMaxRecs];  // slot of the p-th record in expert order
-  __shared__ int4 s_tiles[kFusedMaxRecs];
-  __shared__ int s_nt;
-  uint64_t* full3 = reinterpret_cast<uint64_t*>(smem_raw + kGemvRingBytes);
-  uint64_t* empty3 = full3 + kGemvMaxStages;
-  uint64_t* full4 = empty3 + kGemvMaxStages;
-  uint64_t* empty4 = full4 + kGemvMaxStages;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty4 + kGemvMaxStages);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < d.stages3; ++s) {
-      mbar_init(&full3[s], 1);
-      mbar_init(&empty3[s], kGemvConsumerWarps);
-    }
-    for (int s = 0; s < d.stages4; ++s) {
-      mbar_init(&full4[s], 1);
-      mbar_init(&empty4[s], kGemvConsumerWarps);
-    }
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  __syncthreads();
-  const int vec = d.H / 8, R = d.T * d.k;
+// Phases 1 and 2 of the single-launch layers, run by every thread of every
+// CTA: the router logits (one expert per CTA, the arithmetic of
+// router_sort_small) to `logits`, a grid barrier on *bar, then in every CTA
+// the top-k of every token and the stable sort of the T * k records by expert
+// (one tile per expert) into rs.  False when the barrier gave up.
+struct RouteSmem {
+  int ids[kFusedMaxRecs];
+  float w[kFusedMaxRecs];      // routing weight of slot n*k + j
+  int perm[kFusedMaxRecs];     // slot of the p-th record in expert order
+  int pos[kFusedMaxRecs];      // position of slot s in expert order
+  int tile_of[kFusedMaxRecs];  // tile of slot s
+  int4 tiles[kFusedMaxRecs];
+  int nt;
+};
 
+__device__ __forceinline__ bool route_and_sort(const uint4* __restrict__ x,
+                                               const uint4* __restrict__ wr,
+                                               const float* __restrict__ bias, int T, int H, int E,
+                                               int k, int norm_topk_prob, float* logits,
+                                               unsigned int* bar, volatile int* abort_flag,
+                                               int* status, RouteSmem& rs) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int vec = H / 8, R = T * k;
   // ---------------------------------------------------------- 1: router logits
   if (warp == 0) {
-    for (int e = blockIdx.x; e < d.E; e += gridDim.x) {
-      const uint4* row = d.wr + static_cast<size_t>(e) * vec;
-      const float be = d.bias != nullptr ? d.bias[e] : 0.0f;
-      for (int t = 0; t < d.T; ++t) {
+    for (int e = blockIdx.x; e < E; e += gridDim.x) {
+      const uint4* row = wr + static_cast<size_t>(e) * vec;
+      const float be = bias != nullptr ? bias[e] : 0.0f;
+      for (int t = 0; t < T; ++t) {
         float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const uint4* xr = d.x + static_cast<size_t>(t) * vec;
+        const uint4* xr = x + static_cast<size_t>(t) * vec;
 #pragma unroll
         for (int j = 0; j < kRouterMaxVecPerLane; ++j) {
           const int v = lane + 32 * j;
           if (v < vec) dot8_acc(__ldg(row + v), __ldg(xr + v), acc);
         }
         const float sum = warp_sum(acc_sum(acc));
-        if (lane == 0) d.logits[t * d.E + e] = bf16_round_f(sum + be);
+        if (lane == 0) logits[t * E + e] = bf16_round_f(sum + be);
       }
     }
   }
-  if (!grid_barrier(d.bar + 0, abort_flag, d.status)) return;
+  if (!grid_barrier(bar, abort_flag, status)) return false;
 
   // ------------------------------------------------- 2: top-k and the record sort
-  for (int t = warp; t < d.T; t += kGemvThreads / 32) {  // one warp per token
-    const float* lg = d.logits + t * d.E;
+  for (int t = warp; t < T; t += static_cast<int>(blockDim.x >> 5)) {  // one warp per token
+    const float* lg = logits + t * E;
     uint32_t top[kRouterMaxK];
 #pragma unroll
     for (int i = 0; i < kRouterMaxK; ++i) top[i] = 0u;
-    for (int c = lane; c < d.E; c += 32) topk_insert(top, topk_key(__ldcg(lg + c), c));
+    for (int c = lane; c < E; c += 32) topk_insert(top, topk_key(__ldcg(lg + c), c));
     uint32_t sel[kRouterMaxK];
 #pragma unroll
     for (int i = 0; i < kRouterMaxK; ++i) {
@@ -736,20 +747,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_layer_fused(const Deco
     }
     const float ref = topk_key_value(sel[0]);
     float den = 0.0f;
-    if (d.norm_topk_prob) {
+    if (norm_topk_prob) {
 #pragma unroll
       for (int i = 0; i < kRouterMaxK; ++i)
-        if (i < d.k) den += expf(topk_key_value(sel[i]) - ref);
+        if (i < k) den += expf(topk_key_value(sel[i]) - ref);
     } else {
-      for (int c = lane; c < d.E; c += 32) den += expf(__ldcg(lg + c) - ref);
+      for (int c = lane; c < E; c += 32) den += expf(__ldcg(lg + c) - ref);
       den = warp_sum(den);
     }
     const float inv = 1.0f / den;
 #pragma unroll
     for (int i = 0; i < kRouterMaxK; ++i) {
-      if (i < d.k && lane == i) {
-        s_ids[t * d.k + i] = topk_key_id(sel[i]);
-        s_w[t * d.k + i] = expf(topk_key_value(sel[i]) - ref) * inv;
+      if (i < k && lane == i) {
+        rs.ids[t * k + i] = topk_key_id(sel[i]);
+        rs.w[t * k + i] = expf(topk_key_value(sel[i]) - ref) * inv;
       }
     }
   }
@@ -758,7 +769,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_layer_fused(const Deco
     // Stable sort of the R <= 32 records by expert, lane r = slot r, over
     // shuffles: a record's position counts the records with a smaller id or
     // the same id and a lower slot; one tile per expert, ascending ids.
-    const int my = lane < R ? s_ids[lane] : 0x7fffffff;
+    const int my = lane < R ? rs.ids[lane] : 0x7fffffff;
     int pos = 0, before = 0, same = 0;
     bool first = lane < R;
     for (int j = 0; j < R; ++j) {
@@ -774,23 +785,56 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_layer_fused(const Deco
       const bool f = __shfl_sync(0xffffffffu, first ? 1 : 0, j) != 0;
       tile += (f && o < my) ? 1 : 0;
     }
-    if (lane < R) s_perm[pos] = lane;
-    if (first) s_tiles[tile] = make_int4(my, before, before + same, 0);
+    if (lane < R) {
+      rs.perm[pos] = lane;
+      rs.pos[lane] = pos;
+      rs.tile_of[lane] = tile;
+    }
+    if (first) rs.tiles[tile] = make_int4(my, before, before + same, 0);
     const int n_tiles = __popc(__ballot_sync(0xffffffffu, first));
-    if (lane == 0) s_nt = n_tiles;
+    if (lane == 0) rs.nt = n_tiles;
   }
   __syncthreads();
-  const int nt = s_nt;
+  return true;
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 1) decode_layer_fused(const DecodeArgs d) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];  // ring, then both phases' barriers
+  __shared__ RouteSmem rs;
+  uint64_t* full3 = reinterpret_cast<uint64_t*>(smem_raw + kGemvRingBytes);
+  uint64_t* empty3 = full3 + kGemvMaxStages;
+  uint64_t* full4 = empty3 + kGemvMaxStages;
+  uint64_t* empty4 = full4 + kGemvMaxStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty4 + kGemvMaxStages);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < d.stages3; ++s) {
+      mbar_init(&full3[s], 1);
+      mbar_init(&empty3[s], kGemvConsumerWarps);
+    }
+    for (int s = 0; s < d.stages4; ++s) {
+      mbar_init(&full4[s], 1);
+      mbar_init(&empty4[s], kGemvConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int vec = d.H / 8, R = d.T * d.k;
+
+  if (!route_and_sort(d.x, d.wr, d.bias, d.T, d.H, d.E, d.k, d.norm_topk_prob, d.logits, d.bar,
+                      abort_flag, d.status, rs))
+    return;
+  const int nt = rs.nt;
 
   // ------------------------------------------------------------- 3: gate/up
   StreamArgs a{};
   a.act = d.x;
   a.act_rows = d.T;
-  a.index = s_perm;
+  a.index = rs.perm;
   a.index_div = d.k;
   a.M = R;
-  a.tiles = s_tiles;
-  a.num_tiles = &s_nt;
+  a.tiles = rs.tiles;
+  a.num_tiles = &rs.nt;
   a.max_tiles = kFusedMaxRecs;
   a.w0 = d.w_gate;
   a.w1 = d.w_up;
@@ -814,16 +858,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_layer_fused(const Deco
   b.act_rows = R;
   b.index_div = 1;
   b.M = R;
-  b.tiles = s_tiles;
-  b.num_tiles = &s_nt;
+  b.tiles = rs.tiles;
+  b.num_tiles = &rs.nt;
   b.max_tiles = kFusedMaxRecs;
   b.w0 = d.w_down;
   b.E = d.E;
   b.K = d.I;
   b.N = d.H;
   b.out = d.slots;
-  b.row_map = s_perm;
-  b.row_scale = s_w;
+  b.row_map = rs.perm;
+  b.row_scale = rs.w;
   b.out_rows = R;
   b.stages = d.stages4;
   b.status = d.status;
@@ -863,6 +907,303 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_layer_fused(const Deco
   }
 }
 
+// ------------------------------------------------------------------ split-I decode layer
+//
+// decode_layer_split: the single-launch layer with ONE pass over the routed
+// experts' weights, for callers that keep the down weights also transposed,
+// w_down_t [E][I][H] (row i of expert e = column i of Wd[e]).  Phases 1 and 2
+// (router logits; top-k and the record sort in every CTA) are those of
+// decode_layer_fused.  Phase 3 splits every routed expert along I: work item
+// = (expert tile, 8 rows of I), each CTA a contiguous, cost-balanced item
+// range.  One producer warp streams an item's 8 gate rows, 8 up rows and 8
+// rows of w_down_t into a ring stage (contiguous bulk copies); each of the 8
+// consumer warps forms h = bf16(silu(x . Wg) * (x . Wu)) for one of the rows,
+// and every consumer thread then adds Wd[8t .. 8t+7, 8 cols] . h to fp32
+// partials it keeps in registers for 8 output columns.  When the range leaves
+// a tile, the partials go to scratch as one segment (CTA c, tile ti) at slot
+// c + ti (unique: the ranges are contiguous and ascending).  After a grid
+// barrier, phase 4 sums each slot's segments in CTA order, rounds the slot row
+// bf16(w * D) and adds the k slots of a token in slot order (the rounding of
+// the down GEMV and combine_rows).  Gate, up and down weights stream from HBM
+// once, in contiguous copies, with no second pass over the down weights.  The
+// output equals decode_layer_fused's up to fp32 summation order over I (a
+// bf16 rounding flip on a few elements) and repeats bit for bit on a GPU.
+
+constexpr int kFusedMaxT = 4;      // records of one expert tile <= T
+constexpr int kSplitRows = gemv_row_block<true>();  // I rows per item
+constexpr int kFusedConsumers = 32 * kGemvConsumerWarps;
+constexpr int kSplitMaxH = 8 * kFusedConsumers;     // 8 output columns per consumer thread
+constexpr int kFusedMaxGrid = 160;
+
+struct SplitArgs {
+  const uint4* x;          // [T][H]
+  const uint4* wr;         // [E][H]
+  const float* bias;       // [E] or null
+  int T, H, I, E, k, norm_topk_prob;
+  const __nv_bfloat16* w_gate;    // [E][I][H]
+  const __nv_bfloat16* w_up;      // [E][I][H]
+  const __nv_bfloat16* w_down_t;  // [E][I][H]
+  float* logits;           // scratch [T][E]
+  float* part;             // scratch [kFusedMaxGrid + kFusedMaxRecs][T][H]: segment partials
+  int2* ranges;            // scratch [gridDim.x]: each CTA's item range
+  unsigned int* bar;       // two counters, zero at launch
+  uint2* y;                // [T][H / 4]
+  int stages;
+  int* status;
+};
+
+// One consumer warp's gate/up row of a stage for n <= NR records (rows[r] =
+// token of record r): h_out[r] = bf16(silu(x . Wg) * (x . Wu)), the
+// arithmetic of gemv_pass<true>.
+template <int NR>
+__device__ __forceinline__ void fused_gate_up(const uint4* w, int vec, const uint4* __restrict__ x,
+                                              const int* rows, int n, int lane, float* h_out) {
+  constexpr int CH = 2 * NR >= 16 ? 2 : 4;
+  float acc[2][NR][CH];
+  stage_dots<2, NR, CH, kActLdg>(w, kGemvConsumerWarps * vec, x, rows, n, vec, lane, acc);
+  float v[2][NR];
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      float t = acc[j][r][0] + acc[j][r][1];
+      if (CH == 4) t += acc[j][r][CH - 2] + acc[j][r][CH - 1];
+      v[j][r] = t;
+    }
+  reduce_records<2, NR>(v, lane);
+  const int r = reduced_record<NR>(lane);
+  if ((lane & (32 / NR - 1)) == 0 && r < n) h_out[r] = bf16_round_f(silu_f(v[0][0]) * v[1][0]);
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 1) decode_layer_split(const SplitArgs d) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];  // ring, then its barriers
+  __shared__ RouteSmem rs;
+  __shared__ float s_h[2][kSplitRows][kFusedMaxT];  // h of an item, double-buffered
+  __shared__ int2 s_rng[kFusedMaxGrid];
+  __shared__ int s_first[kFusedMaxRecs], s_last[kFusedMaxRecs];  // CTAs holding a tile
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + kGemvRingBytes);
+  uint64_t* empty = full + kGemvMaxStages;
+  uint64_t* hbar = empty + kGemvMaxStages;  // [2]: every consumer warp wrote its h row
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(hbar + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < d.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGemvConsumerWarps);
+    }
+    mbar_init(&hbar[0], kGemvConsumerWarps);
+    mbar_init(&hbar[1], kGemvConsumerWarps);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (!route_and_sort(d.x, d.wr, d.bias, d.T, d.H, d.E, d.k, d.norm_topk_prob, d.logits, d.bar,
+                      abort_flag, d.status, rs))
+    return;
+  const int nt = rs.nt, R = d.T * d.k, vec = d.H / 8;
+
+  // ----------------------------------------- 3: gate/up and down in one pass
+  const int ipt = d.I / kSplitRows;  // items per tile
+  StreamArgs a{};
+  a.M = R;
+  a.tiles = rs.tiles;
+  a.num_tiles = &rs.nt;
+  a.max_tiles = kFusedMaxRecs;
+  long long lo, hi;
+  balanced_range(a, nt, ipt, &lo, &hi);
+  if (threadIdx.x == 0) d.ranges[blockIdx.x] = make_int2(static_cast<int>(lo), static_cast<int>(hi));
+  const uint32_t mat_bytes = static_cast<uint32_t>(kSplitRows) * d.H * 2;  // 8 rows of one matrix
+  const uint32_t stage_bytes = 3u * mat_bytes;                            // gate, up, down^T
+  if (warp == kGemvConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, issued = 0;
+      for (long long w = lo; w < hi; ++w) {
+        const int ti = static_cast<int>(w / ipt);
+        const int rb = static_cast<int>(w - static_cast<long long>(ti) * ipt);
+        const int e = rs.tiles[ti].x;
+        if (e < 0 || e >= d.E) break;  // the consumers report it
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, d.status, kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        const size_t row0 =
+            (static_cast<size_t>(e) * d.I + static_cast<size_t>(rb) * kSplitRows) * d.H;
+        uint8_t* dst = smem_raw + s * stage_bytes;
+        bulk_load(dst, d.w_gate + row0, mat_bytes, &full[s]);
+        bulk_load(dst + mat_bytes, d.w_up + row0, mat_bytes, &full[s]);
+        bulk_load(dst + 2 * mat_bytes, d.w_down_t + row0, mat_bytes, &full[s]);
+        ++issued;
+        if (++s == d.stages) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      if (*abort_flag) {
+        // Let every copy still in flight land before the CTA exits.
+        const uint32_t first = issued > static_cast<uint32_t>(d.stages) ? issued - d.stages : 0u;
+        for (uint32_t i = first; i < issued; ++i) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[i % d.stages], (i / d.stages) & 1u)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+          }
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- consumers
+    // Thread ct owns output columns 8ct .. 8ct+7 of the down projection.
+    const int ct = threadIdx.x;
+    const bool owns = 8 * ct < d.H;
+    float acc[8][kFusedMaxT];
+    int rows[kFusedMaxT];
+    int cur_ti = -1, n = 0, s = 0;
+    uint32_t ph = 0, hph = 0;  // ring phase; bit b = phase of hbar[b]
+    bool ok = true;
+    auto flush = [&]() {
+      if (!owns) return;
+      float* dst = d.part + static_cast<size_t>(blockIdx.x + cur_ti) * d.T * d.H + 8 * ct;
+#pragma unroll
+      for (int r = 0; r < kFusedMaxT; ++r) {
+        if (r < n) {
+          float4* o = reinterpret_cast<float4*>(dst + static_cast<size_t>(r) * d.H);
+          o[0] = make_float4(acc[0][r], acc[1][r], acc[2][r], acc[3][r]);
+          o[1] = make_float4(acc[4][r], acc[5][r], acc[6][r], acc[7][r]);
+        }
+      }
+    };
+    int buf = 0;
+    for (long long w = lo; w < hi; ++w, buf ^= 1) {
+      const int ti = static_cast<int>(w / ipt);
+      const int4 t = rs.tiles[ti];
+      if (t.x < 0 || t.x >= d.E || t.y < 0 || t.z - t.y > kFusedMaxT || t.z - t.y > d.T ||
+          t.z > R) {
+        if (ct == 0) record_status(d.status, kErrBadRow);
+        ok = false;
+        break;
+      }
+      if (ti != cur_ti) {
+        if (cur_ti >= 0) flush();
+        cur_ti = ti;
+        n = t.z - t.y;
+#pragma unroll
+        for (int r = 0; r < kFusedMaxT; ++r) {
+          rows[r] = r < n ? rs.perm[t.y + r] / d.k : 0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j][r] = 0.0f;
+        }
+      }
+      if (!mbar_wait(&full[s], ph, abort_flag, d.status, kErrTimeoutFull)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* stage = smem_raw + s * stage_bytes;
+      const uint4* w0 = reinterpret_cast<const uint4*>(stage) + warp * vec;
+      float* h_out = s_h[buf][warp];
+      if (n == 1)
+        fused_gate_up<1>(w0, vec, d.x, rows, n, lane, h_out);
+      else if (n == 2)
+        fused_gate_up<2>(w0, vec, d.x, rows, n, lane, h_out);
+      else
+        fused_gate_up<4>(w0, vec, d.x, rows, n, lane, h_out);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&hbar[buf]);
+      if (!mbar_wait(&hbar[buf], (hph >> buf) & 1u, abort_flag, d.status, kErrTimeoutFull)) {
+        ok = false;
+        break;
+      }
+      hph ^= 1u << buf;
+      if (owns) {
+        // Row c of the stage's down^T block = column c of the item in Wd.
+        const uint4* dt = reinterpret_cast<const uint4*>(stage + 2 * mat_bytes) + ct;
+        const float(*hh)[kFusedMaxT] = s_h[buf];
+#pragma unroll
+        for (int c = 0; c < kSplitRows; ++c) {
+          const uint4 wv = dt[c * vec];
+          const uint32_t w4[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float wlo = __uint_as_float(w4[q] << 16);
+            const float whi = __uint_as_float(w4[q] & 0xffff0000u);
+#pragma unroll
+            for (int r = 0; r < kFusedMaxT; ++r) {
+              if (r < n) {
+                acc[2 * q][r] = fmaf(wlo, hh[c][r], acc[2 * q][r]);
+                acc[2 * q + 1][r] = fmaf(whi, hh[c][r], acc[2 * q + 1][r]);
+              }
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (++s == d.stages) {
+        s = 0;
+        ph ^= 1u;
+      }
+    }
+    if (ok && cur_ti >= 0) flush();
+  }
+  if (!grid_barrier(d.bar + 1, abort_flag, d.status)) return;
+
+  // ----------------------------------------------------- 4: segment sums, combine
+  for (int c = threadIdx.x; c < static_cast<int>(gridDim.x); c += blockDim.x)
+    s_rng[c] = __ldcg(d.ranges + c);
+  __syncthreads();
+  for (int c = threadIdx.x; c < static_cast<int>(gridDim.x); c += blockDim.x) {
+    const int2 r = s_rng[c];
+    if (r.x >= r.y) continue;
+    for (int ti = (r.x + ipt - 1) / ipt; ti * ipt < r.y; ++ti) s_first[ti] = c;  // holds item ti*ipt
+    for (int ti = r.x / ipt; (ti + 1) * ipt - 1 < r.y; ++ti)
+      if ((ti + 1) * ipt - 1 >= r.x) s_last[ti] = c;  // holds the tile's last item
+  }
+  __syncthreads();
+  // Work item = (token, group of 4 columns), one warp each: lane 4j + q sums
+  // every fourth segment of slot t*k + j (q = 0..3), the four partial sums meet
+  // over shuffles, and every lane adds the k slot values in slot order.
+  const int groups = d.H / 4;
+  const int jj = lane >> 2, q = lane & 3;
+  constexpr int kWarps = kGemvThreads / 32;
+  const int warps_all = static_cast<int>(gridDim.x) * kWarps;
+  for (int item = blockIdx.x * kWarps + warp; item < d.T * groups; item += warps_all) {
+    const int t = item / groups, col = (item - t * groups) * 4;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    float w = 0.0f;
+    if (jj < d.k) {
+      const int slot = t * d.k + jj;
+      const int ti = rs.tile_of[slot];
+      const int r = rs.pos[slot] - rs.tiles[ti].y;
+      w = rs.w[slot];
+      for (int c = s_first[ti] + q; c <= s_last[ti]; c += 4) {
+        if (s_rng[c].x >= s_rng[c].y) continue;  // an empty range holds no segment
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(
+            d.part + (static_cast<size_t>(c + ti) * d.T + r) * d.H + col));
+        sum.x += p.x;
+        sum.y += p.y;
+        sum.z += p.z;
+        sum.w += p.w;
+      }
+    }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      sum.x += __shfl_xor_sync(0xffffffffu, sum.x, o);
+      sum.y += __shfl_xor_sync(0xffffffffu, sum.y, o);
+      sum.z += __shfl_xor_sync(0xffffffffu, sum.z, o);
+      sum.w += __shfl_xor_sync(0xffffffffu, sum.w, o);
+    }
+    // slot value bf16(w * D), as the down GEMV writes its slot rows
+    const float v0 = bf16_round_f(sum.x * w), v1 = bf16_round_f(sum.y * w);
+    const float v2 = bf16_round_f(sum.z * w), v3 = bf16_round_f(sum.w * w);
+    float y0 = 0.f, y1 = 0.f, y2 = 0.f, y3 = 0.f;
+    for (int j = 0; j < d.k; ++j) {
+      y0 += __shfl_sync(0xffffffffu, v0, 4 * j);
+      y1 += __shfl_sync(0xffffffffu, v1, 4 * j);
+      y2 += __shfl_sync(0xffffffffu, v2, 4 * j);
+      y3 += __shfl_sync(0xffffffffu, v3, 4 * j);
+    }
+    if (lane == 0) d.y[item] = make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y2, y3));
+  }
+}
+
 // ------------------------------------------------------------------ launchers
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -877,7 +1218,8 @@ static bool allow_smem(Kernel* fn, int bytes, std::atomic<uint64_t>& done) {
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   const uint64_t bit = 1ull << (dev & 63);
   if ((done.load(std::memory_order_acquire) & bit) != 0) return true;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+  if (note_cuda_error(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           bytes)) != cudaSuccess)
     return false;
   done.fetch_or(bit, std::memory_order_acq_rel);
   return true;
@@ -922,14 +1264,16 @@ bool gemv_ok(int n_out, int K, bool swiglu) {
 }
 
 template <bool SWIGLU>
-static int launch_stream(StreamArgs a, cudaStream_t stream) {
+static int launch_stream(StreamArgs a, cudaStream_t stream, int max_sms) {
   a.stages = gemv_stages(a.K, SWIGLU);
   const size_t stage = (SWIGLU ? 2u : 1u) * static_cast<size_t>(gemv_row_block<SWIGLU>()) * a.K * 2;
   const size_t sh = a.stages * stage + 2 * kGemvMaxStages * sizeof(uint64_t) + 16;
   static std::atomic<uint64_t> attr{0};
   if (!allow_smem(gemv_stream<SWIGLU>, kGemvMaxDynSmem, attr)) return kRcCudaError;
   const long long work = static_cast<long long>(a.max_tiles) * (a.N / gemv_row_block<SWIGLU>());
-  const int grid = static_cast<int>(std::min<long long>(work, device_sm_count()));
+  const long long sms =
+      max_sms > 0 ? std::min(max_sms, device_sm_count()) : device_sm_count();
+  const int grid = static_cast<int>(std::min<long long>(work, sms));
   const cudaError_t e =
       launch_pdl(gemv_stream<SWIGLU>, dim3(grid), dim3(kGemvThreads), sh, stream, a);
   return e == cudaSuccess ? kRcOk : kRcCudaError;
@@ -938,7 +1282,7 @@ static int launch_stream(StreamArgs a, cudaStream_t stream) {
 int launch_w13_gemv(const void* src, int src_rows, const int* index, int index_div, int M,
                     const int4* tiles, const int* num_tiles, int max_tiles, const void* w_gate,
                     const void* w_up, int E, int H, int I, void* h_out, int* status,
-                    cudaStream_t stream, const void* w_down_prefetch) {
+                    cudaStream_t stream, const void* w_down_prefetch, int max_sms) {
   if (!gemv_ok(I, H, true) || !aligned16(src) || !aligned16(w_gate) || !aligned16(w_up))
     return kRcUnsupported;
   if (M == 0 || max_tiles == 0) return kRcOk;
@@ -964,13 +1308,13 @@ int launch_w13_gemv(const void* src, int src_rows, const int* index, int index_d
     a.next_N = H;  // down weights are [E][H][I]
     a.next_K = I;
   }
-  return launch_stream<true>(a, stream);
+  return launch_stream<true>(a, stream, max_sms);
 }
 
 int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
                    const void* w_down, int E, int H, int I, const int* row_map,
                    const float* row_scale, void* out, int out_rows, int* status,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, int max_sms) {
   if (!gemv_ok(H, I, false) || !aligned16(h) || !aligned16(w_down)) return kRcUnsupported;
   if (M == 0 || max_tiles == 0) return kRcOk;
   StreamArgs a{};
@@ -990,7 +1334,7 @@ int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles
   a.row_scale = row_scale;
   a.out_rows = out_rows;
   a.status = status;
-  return launch_stream<false>(a, stream);
+  return launch_stream<false>(a, stream, max_sms);
 }
 
 bool fused_decode_ok(int T, int H, int I, int E, int k) {
@@ -1058,6 +1402,106 @@ int launch_decode_fused(const void* x, const void* wr, const float* bias, int T,
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, decode_layer_fused, d) == cudaSuccess ? kRcOk : kRcCudaError;
+}
+
+// Ring stages of the split layer: an item is 8 rows each of gate, up and down^T.
+static int split_stages(int H) {
+  const long long stage = 3LL * kSplitRows * H * 2;
+  return static_cast<int>(std::min<long long>(kGemvMaxStages, kGemvRingBytes / stage));
+}
+
+bool split_decode_ok(int T, int H, int I, int E, int k) {
+  const long long R = static_cast<long long>(T) * k;
+  return R >= 1 && R <= kFusedMaxRecs && T <= kFusedMaxT && router_small_ok(T, H, E, k) &&
+         gemv_ok(I, H, true) && (I % kSplitRows) == 0 && (H % 8) == 0 && H <= kSplitMaxH &&
+         split_stages(H) >= 2;
+}
+
+// Scratch of the split layer: logits [T][E] fp32, segment partials
+// [kFusedMaxGrid + kFusedMaxRecs][T][H] fp32, the CTAs' item ranges and the
+// barrier counters.
+namespace {
+struct SplitScratch {
+  size_t logits, part, ranges, bar, total;
+};
+SplitScratch split_scratch(int T, int H, int E) {
+  auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+  SplitScratch f{};
+  f.logits = 0;
+  f.part = up(static_cast<size_t>(T) * E * sizeof(float));
+  f.ranges = f.part + up(static_cast<size_t>(kFusedMaxGrid + kFusedMaxRecs) * T * H * sizeof(float));
+  f.bar = f.ranges + up(kFusedMaxGrid * sizeof(int2));
+  f.total = f.bar + 256;
+  return f;
+}
+}  // namespace
+
+size_t split_decode_scratch_bytes(int T, int H, int E) { return split_scratch(T, H, E).total; }
+
+int launch_decode_split(const void* x, const void* wr, const float* bias, int T, int H, int I,
+                        int E, int k, int norm_topk_prob, const void* w_gate, const void* w_up,
+                        const void* w_down_t, void* scratch, void* y, int* status,
+                        cudaStream_t stream) {
+  if (!split_decode_ok(T, H, I, E, k)) return kRcUnsupported;
+  if (!aligned16(x) || !aligned16(wr) || !aligned16(w_gate) || !aligned16(w_up) ||
+      !aligned16(w_down_t) || !aligned16(y) || scratch == nullptr || !aligned16(scratch))
+    return kRcBadArgument;
+  const int grid = device_sm_count();
+  if (grid < 1 || grid > kFusedMaxGrid) return kRcUnsupported;
+  const SplitScratch f = split_scratch(T, H, E);
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  SplitArgs d{};
+  d.x = static_cast<const uint4*>(x);
+  d.wr = static_cast<const uint4*>(wr);
+  d.bias = bias;
+  d.T = T;
+  d.H = H;
+  d.I = I;
+  d.E = E;
+  d.k = k;
+  d.norm_topk_prob = norm_topk_prob;
+  d.w_gate = static_cast<const __nv_bfloat16*>(w_gate);
+  d.w_up = static_cast<const __nv_bfloat16*>(w_up);
+  d.w_down_t = static_cast<const __nv_bfloat16*>(w_down_t);
+  d.logits = reinterpret_cast<float*>(base + f.logits);
+  d.part = reinterpret_cast<float*>(base + f.part);
+  d.ranges = reinterpret_cast<int2*>(base + f.ranges);
+  d.bar = reinterpret_cast<unsigned int*>(base + f.bar);
+  d.y = static_cast<uint2*>(y);
+  d.stages = split_stages(H);
+  d.status = status;
+  const size_t sh = kGemvRingBytes + (2 * kGemvMaxStages + 2) * sizeof(uint64_t) + 16;
+  static std::atomic<uint64_t> attr{0};
+  if (!allow_smem(decode_layer_split, static_cast<int>(sh), attr)) return kRcCudaError;
+  // The grid barriers need every CTA resident: one per SM (checked once per device).
+  static std::atomic<uint64_t> resident{0};
+  int dev = 0;
+  if (note_cuda_error(cudaGetDevice(&dev)) != cudaSuccess) return kRcCudaError;
+  const uint64_t dev_bit = 1ull << (dev & 63);
+  if ((resident.load(std::memory_order_acquire) & dev_bit) == 0) {
+    int per_sm = 0;
+    if (note_cuda_error(cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &per_sm, decode_layer_split, kGemvThreads, sh)) != cudaSuccess)
+      return kRcCudaError;
+    if (per_sm < 1) return kRcUnsupported;
+    resident.fetch_or(dev_bit, std::memory_order_acq_rel);
+  }
+  if (note_cuda_error(cudaMemsetAsync(d.bar, 0, 2 * sizeof(unsigned int), stream)) != cudaSuccess)
+    return kRcCudaError;
+  // Cooperative: every CTA is resident at once, as the grid barriers need.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = sh;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeCooperative;
+  attrs[0].val.cooperative = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  return note_cuda_error(cudaLaunchKernelEx(&cfg, decode_layer_split, d)) == cudaSuccess
+             ? kRcOk
+             : kRcCudaError;
 }
 
 }  // namespace moe

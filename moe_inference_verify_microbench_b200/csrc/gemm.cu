@@ -81,9 +81,18 @@ int device_sms() {
   return v;
 }
 
+// Grid of a persistent GEMM: one CTA per SM, at most `max_sms` SMs when > 0
+// (the caller leaves the others to concurrent work, e.g. an expert-parallel
+// exchange on another stream).
+long long sm_budget(int max_sms) {
+  const long long sms = device_sms();
+  return max_sms > 0 && max_sms < sms ? max_sms : sms;
+}
+
 template <int BN, int EPI, int STAGES, bool GATHER_A = false>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
-                const GemmArgs& args, long long work_units, cudaStream_t stream) {
+                const GemmArgs& args, long long work_units, cudaStream_t stream,
+                int max_sms = 0) {
   using L = GemmSmem<BN, STAGES, gemm_out_bytes<EPI, GATHER_A>()>;
   static_assert(L::kTotal <= kMaxSmemPerBlock, "shared memory budget");
   static std::atomic<uint64_t> attr_done{0};  // one bit per device
@@ -96,7 +105,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
       return kRcCudaError;
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  const long long sms = device_sms();
+  const long long sms = sm_budget(max_sms);
   const int grid = static_cast<int>(work_units < sms ? work_units : sms);
   if (grid <= 0) return kRcOk;
   const cudaError_t e = launch_pdl(grouped_gemm_kernel<BN, EPI, STAGES, GATHER_A>, dim3(grid),
@@ -107,7 +116,8 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& 
 
 template <int EPI, int STAGES, bool GATHER_A = false>
 int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensorMap& b1,
-                     const GemmArgs& args, long long work_units, cudaStream_t stream) {
+                     const GemmArgs& args, long long work_units, cudaStream_t stream,
+                     int max_sms = 0) {
   using L = PairSmem<STAGES>;
   static_assert(L::kTotal <= kMaxSmemPerBlock, "shared memory budget");
   static std::atomic<uint64_t> attr_done{0};  // one bit per device
@@ -120,7 +130,7 @@ int launch_gemm_pair(const CUtensorMap& a, const CUtensorMap& b0, const CUtensor
       return kRcCudaError;
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  const long long pairs = device_sms() / 2;
+  const long long pairs = sm_budget(max_sms) / 2;
   const int grid = 2 * static_cast<int>(work_units < pairs ? work_units : pairs);
   if (grid <= 0) return kRcOk;
   const cudaError_t e =
@@ -161,6 +171,17 @@ GemmArgs blank_args(int* status) {
 }  // namespace
 
 int device_sm_count() { return device_sms(); }
+
+namespace {
+thread_local int t_last_cuda_error = 0;
+}
+
+int last_cuda_error() { return t_last_cuda_error; }
+
+cudaError_t note_cuda_error(cudaError_t e) {
+  if (e != cudaSuccess) t_last_cuda_error = static_cast<int>(e);
+  return e;
+}
 
 int launch_router(const void* x, const void* wr, const float* bias, int T, int H, int E, int k,
                   int norm_topk_prob, int* ids_out, float* w_out, void* logits_out, int* status,
@@ -260,7 +281,7 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
                              int M, const int4* tiles, const int* num_tiles, int max_tiles,
                              const void* w_gate, const void* w_up, int E, int H, int I,
                              void* h_out, int* status, cudaStream_t stream, int tile_rows,
-                             const void* w_down_prefetch) {
+                             const void* w_down_prefetch, int max_sms) {
   if ((M > 0 && (src == nullptr || h_out == nullptr)) || tiles == nullptr ||
       num_tiles == nullptr || w_gate == nullptr || w_up == nullptr || M < 0 || E <= 0 || H <= 0 ||
       I <= 0 || max_tiles < 0 || src_rows < 0 || index_div <= 0)
@@ -270,7 +291,8 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
   if (src_rows == 0) return kRcBadArgument;  // rows to gather, but nothing to gather from
   if (use_gemv_w13(M) && gemv_ok(I, H, true))
     return launch_w13_gemv(src, src_rows, index, index_div, M, tiles, num_tiles, max_tiles,
-                           w_gate, w_up, E, H, I, h_out, status, stream, w_down_prefetch);
+                           w_gate, w_up, E, H, I, h_out, status, stream, w_down_prefetch,
+                           max_sms);
   if ((H % kBK) != 0 || (I % 32) != 0) return kRcUnsupported;
   if (tile_rows == kPairTileRows) {
     if ((I % (kPairBN / 2)) != 0) return kRcUnsupported;
@@ -297,7 +319,7 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
     g.a_index_div = index_div;
     // A is gathered by the loader warps; the gate map stands in for the unused A map.
     return launch_gemm_pair<kEpiSwiGLU, kPairStages, true>(
-        mg, mg, mu, g, static_cast<long long>(max_tiles) * g.n_tiles, stream);
+        mg, mg, mu, g, static_cast<long long>(max_tiles) * g.n_tiles, stream, max_sms);
   }
   if (tile_rows != kBM) return kRcBadArgument;
   const int bn = pick_bn(I, M, max_tiles, 7, [](int b) { return b / 2; });
@@ -323,9 +345,11 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
   g.a_index_div = index_div;
   const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
   // A is gathered by the loader warps; the gate map stands in for the unused A map.
-  if (bn == 256) return launch_gemm<256, kEpiSwiGLU, 4, true>(mg, mg, mu, g, units, stream);
-  if (bn == 128) return launch_gemm<128, kEpiSwiGLU, 6, true>(mg, mg, mu, g, units, stream);
-  return launch_gemm<64, kEpiSwiGLU, 8, true>(mg, mg, mu, g, units, stream);
+  if (bn == 256)
+    return launch_gemm<256, kEpiSwiGLU, 4, true>(mg, mg, mu, g, units, stream, max_sms);
+  if (bn == 128)
+    return launch_gemm<128, kEpiSwiGLU, 6, true>(mg, mg, mu, g, units, stream, max_sms);
+  return launch_gemm<64, kEpiSwiGLU, 8, true>(mg, mg, mu, g, units, stream, max_sms);
 }
 
 // Down GEMM on 256-row pair tiles or 128-row tiles; EPI = kEpiStore writes
@@ -336,7 +360,7 @@ static int launch_w2_gemm(const void* h, int M, const int4* tiles, const int* nu
                           int max_tiles, const void* w_down, int E, int H, int I,
                           const int* row_map, const float* row_scale, void* out, float* out_f32,
                           int red_div, int out_rows, int* status, cudaStream_t stream,
-                          int tile_rows) {
+                          int tile_rows, int max_sms) {
   if ((I % kBK) != 0 || (H % 64) != 0) return kRcUnsupported;
   GemmArgs g = blank_args(status);
   g.tiles = tiles;
@@ -361,7 +385,7 @@ static int launch_w2_gemm(const void* h, int M, const int4* tiles, const int* nu
     g.n_tiles = H / kPairBN;
     g.b_rows = kPairBN;
     return launch_gemm_pair<EPI, kPairStages>(
-        ma, md, md, g, static_cast<long long>(max_tiles) * g.n_tiles, stream);
+        ma, md, md, g, static_cast<long long>(max_tiles) * g.n_tiles, stream, max_sms);
   }
   if (tile_rows != kBM) return kRcBadArgument;
   const int bn = pick_bn(H, M, max_tiles, 7, [](int b) { return b; });
@@ -372,23 +396,25 @@ static int launch_w2_gemm(const void* h, int M, const int4* tiles, const int* nu
   g.n_tiles = H / bn;
   g.b_rows = bn;
   const long long units = static_cast<long long>(max_tiles) * g.n_tiles;
-  if (bn == 256) return launch_gemm<256, EPI, 4>(ma, md, md, g, units, stream);
-  if (bn == 128) return launch_gemm<128, EPI, 6>(ma, md, md, g, units, stream);
-  return launch_gemm<64, EPI, 8>(ma, md, md, g, units, stream);
+  if (bn == 256) return launch_gemm<256, EPI, 4>(ma, md, md, g, units, stream, max_sms);
+  if (bn == 128) return launch_gemm<128, EPI, 6>(ma, md, md, g, units, stream, max_sms);
+  return launch_gemm<64, EPI, 8>(ma, md, md, g, units, stream, max_sms);
 }
 
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
-              void* out, int out_rows, int* status, cudaStream_t stream, int tile_rows) {
+              void* out, int out_rows, int* status, cudaStream_t stream, int tile_rows,
+              int max_sms) {
   if ((M > 0 && (h == nullptr || out == nullptr)) || tiles == nullptr || num_tiles == nullptr ||
       w_down == nullptr || M < 0 || E <= 0 || H <= 0 || I <= 0 || max_tiles < 0 || out_rows < 0)
     return kRcBadArgument;
   if (M == 0 || max_tiles == 0) return kRcOk;
   if (use_gemv_w2(M) && gemv_ok(H, I, false))
     return launch_w2_gemv(h, M, tiles, num_tiles, max_tiles, w_down, E, H, I, row_map, row_scale,
-                          out, out_rows, status, stream);
+                          out, out_rows, status, stream, max_sms);
   return launch_w2_gemm<kEpiStore>(h, M, tiles, num_tiles, max_tiles, w_down, E, H, I, row_map,
-                                   row_scale, out, nullptr, 1, out_rows, status, stream, tile_rows);
+                                   row_scale, out, nullptr, 1, out_rows, status, stream, tile_rows,
+                                   max_sms);
 }
 
 int launch_w2_atomic(const void* h, int M, const int4* tiles, const int* num_tiles,
@@ -403,7 +429,7 @@ int launch_w2_atomic(const void* h, int M, const int4* tiles, const int* num_til
   if (M == 0 || max_tiles == 0) return kRcOk;
   return launch_w2_gemm<kEpiAtomic>(h, M, tiles, num_tiles, max_tiles, w_down, E, H, I, row_map,
                                     row_scale, nullptr, out_f32, red_div, n_slots, status, stream,
-                                    tile_rows);
+                                    tile_rows, 0);
 }
 
 }  // namespace moe

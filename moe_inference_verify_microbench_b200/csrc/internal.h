@@ -70,6 +70,8 @@ int launch_combine(const void* rows, int n_rows, const int* slot_src, const floa
 int launch_router(const void* x, const void* wr, const float* bias, int T, int H, int E, int k,
                   int norm_topk_prob, int* ids_out, float* w_out, void* logits_out, int* status,
                   cudaStream_t stream);
+// max_sms (grouped GEMMs and GEMVs): at most this many SMs (<= 0: all), the
+// others left to concurrent work on other streams.
 // tile_rows: the height of the tile table's row blocks, 128 (MOE_BLOCK_M) or
 // kPairTileRows (CTA-pair kernels, large batches).
 constexpr int kPairTileRows = 256;
@@ -80,11 +82,12 @@ int launch_w13_swiglu_gather(const void* src, int src_rows, const int* index, in
                              int M, const int4* tiles, const int* num_tiles, int max_tiles,
                              const void* w_gate, const void* w_up, int E, int H, int I,
                              void* h_out, int* status, cudaStream_t stream, int tile_rows = 128,
-                             const void* w_down_prefetch = nullptr);
+                             const void* w_down_prefetch = nullptr, int max_sms = 0);
 
 int launch_w2(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
               const void* w_down, int E, int H, int I, const int* row_map, const float* row_scale,
-              void* out, int out_rows, int* status, cudaStream_t stream, int tile_rows = 128);
+              void* out, int out_rows, int* status, cudaStream_t stream, int tile_rows = 128,
+              int max_sms = 0);
 
 // CTA-pair GEMMs pay off once the average expert has kPairMinRowsPerExpert
 // rows: below that the padding of its last 256-row tile costs more tensor
@@ -102,6 +105,11 @@ inline bool use_pair_gemm(long long R, int E, int H, int I) {
 }
 
 int device_sm_count();
+
+// The cudaError_t of the most recent failed CUDA call a launcher recorded on
+// this thread (0 = none), and the recorder: returns `e` unchanged.
+int last_cuda_error();
+cudaError_t note_cuda_error(cudaError_t e);
 
 // Small-batch kernels (decode.cu).  Below these sizes the layer streams the
 // routed experts' weights through the CUDA cores instead of 128-row
@@ -126,11 +134,11 @@ int launch_router_sort_small(const void* x, const void* wr, const float* bias, i
 int launch_w13_gemv(const void* src, int src_rows, const int* index, int index_div, int M,
                     const int4* tiles, const int* num_tiles, int max_tiles, const void* w_gate,
                     const void* w_up, int E, int H, int I, void* h_out, int* status,
-                    cudaStream_t stream, const void* w_down_prefetch = nullptr);
+                    cudaStream_t stream, const void* w_down_prefetch = nullptr, int max_sms = 0);
 int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles, int max_tiles,
                    const void* w_down, int E, int H, int I, const int* row_map,
                    const float* row_scale, void* out, int out_rows, int* status,
-                   cudaStream_t stream);
+                   cudaStream_t stream, int max_sms = 0);
 
 // Whole decode layer in one cooperative launch (T * k <= kGemvW2MaxRows records):
 // router, top-k, sort, gate/up and down GEMVs and the k-way combine, bitwise
@@ -142,6 +150,17 @@ int launch_decode_fused(const void* x, const void* wr, const float* bias, int T,
                         int E, int k, int norm_topk_prob, const void* w_gate, const void* w_up,
                         const void* w_down, void* scratch, void* h, void* slots, void* y,
                         int* status, cudaStream_t stream);
+
+// The single-launch layer with one pass over the weights (T <= 4 tokens,
+// T * k <= 32 records), given the down weights transposed, w_down_t [E][I][H]:
+// equal to the above up to fp32 summation order over I.  `scratch` holds
+// split_decode_scratch_bytes(T, H, E) bytes.
+bool split_decode_ok(int T, int H, int I, int E, int k);
+size_t split_decode_scratch_bytes(int T, int H, int E);
+int launch_decode_split(const void* x, const void* wr, const float* bias, int T, int H, int I,
+                        int E, int k, int norm_topk_prob, const void* w_gate, const void* w_up,
+                        const void* w_down_t, void* scratch, void* y, int* status,
+                        cudaStream_t stream);
 
 // Down GEMM with the atomic combine: out_f32[row_map[p] / red_div] +=
 // row_scale[row_map[p]] * (h[p] @ w_down[e]^T) in fp32 (row_map[p] < n_slots).

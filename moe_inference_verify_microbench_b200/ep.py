@@ -65,16 +65,19 @@ class CudaKernels:
 
     @staticmethod
     def expert_compute(src, index, index_div, s, w_gate, w_up, w_down, row_map=None,
-                       slot_scale=None, out_rows=None):
+                       slot_scale=None, out_rows=None, max_sms=0):
         """SwiGLU experts on rows src[index[p] // index_div] of the sorted order,
         gathered inside the gate/up GEMM (only the rows the tile table covers,
         i.e. the sort's valid records, are read or computed), w2 output to
-        row_map[p] scaled by slot_scale[row_map[p]]."""
+        row_map[p] scaled by slot_scale[row_map[p]]; both GEMMs on at most
+        ``max_sms`` SMs when > 0."""
         M = s.perm.numel()
         h = ops.grouped_w13_swiglu_gather(src, index, index_div, M, s.tiles, s.num_tiles,
-                                          s.max_tiles, w_gate, w_up, tile_rows=s.tile_rows)
+                                          s.max_tiles, w_gate, w_up, tile_rows=s.tile_rows,
+                                          max_sms=max_sms)
         return ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, w_down, row_map=row_map,
-                              slot_scale=slot_scale, out_rows=out_rows, tile_rows=s.tile_rows)
+                              slot_scale=slot_scale, out_rows=out_rows, tile_rows=s.tile_rows,
+                              max_sms=max_sms)
 
 
 class _EPBase(nn.Module):
@@ -226,21 +229,138 @@ def dispatch_combine_peer(mod: _EPBase, local_x: torch.Tensor, px: PeerExchange)
     return K.combine(px.ret_rows, N, ep, slot_src=plan.inv)           # sum over owner ranks
 
 
+class _Streams:
+    """Side stream and events of the pipelined exchange on a CUDA device; on
+    CPU tensors (the gloo stand-ins) every operation runs in program order and
+    these are no-ops."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.cuda = device.type == "cuda"
+        self.side = torch.cuda.Stream(device) if self.cuda else None
+
+    def on_side(self):
+        import contextlib
+        return torch.cuda.stream(self.side) if self.cuda else contextlib.nullcontext()
+
+    def mark(self, side: bool = False):
+        """An event recorded on the side (or the current) stream."""
+        if not self.cuda:
+            return None
+        ev = torch.cuda.Event()
+        ev.record(self.side if side else torch.cuda.current_stream())
+        return ev
+
+    def side_waits(self, ev) -> None:
+        if ev is not None:
+            self.side.wait_event(ev)
+
+    def main_waits(self, ev) -> None:
+        if ev is not None:
+            torch.cuda.current_stream().wait_event(ev)
+
+    def keep(self, *tensors) -> None:
+        """Tensors allocated on the main stream and used on the side stream."""
+        if self.cuda:
+            for t in tensors:
+                if t is not None:
+                    t.record_stream(self.side)
+
+
+def dispatch_combine_peer_pipelined(mod: _EPBase, local_x: torch.Tensor, pxs, st: _Streams,
+                                    exchange_sms: int) -> torch.Tensor:
+    """``dispatch_combine_peer`` in len(pxs) token chunks whose exchanges
+    overlap the other chunks' expert GEMMs (D = dispatch, G = local sort and
+    GEMMs, R = return of chunk i):
+
+        main stream   D0 | G0       | G1       | ... | G(n-1)   | R(n-1) | combine
+        side stream      | D1       | R0, D2   | ... | R(n-2)   |
+
+    The GEMMs leave ``exchange_sms`` SMs free, on which the side stream's
+    exchange kernels (SM-issued NVLink stores) run; only the first chunk's
+    dispatch and the last chunk's return stay on the critical path, at the
+    price of one more pass over the local experts' weights per chunk.  Each
+    chunk has its own peer exchange (own buffers and epochs) and every rank
+    issues the exchanges in the same order.  A token's records stay in one
+    chunk, so every owner rank sums the same records in the same order as in
+    the one-chunk forward: the output is bit for bit the same."""
+    K = mod._kernels
+    n_ch = len(pxs)
+    N, k, epr, ep = local_x.shape[0], mod.top_k, mod.experts_per_rank, mod.ep_size
+    step = -(-N // n_ch)
+    bounds = [(min(i * step, N), min((i + 1) * step, N)) for i in range(n_ch)]
+    ids, w = mod._route(local_x)                                       # local router (C7:141-146)
+    plans = [K.sort_align(K.ep_keys(ids[a:b], epr, ep), ep + 1, 0, ep, want_inv=True)
+             for a, b in bounds]
+    wg, wu, wd = mod.pack()
+    budget = 0
+    if st.cuda and exchange_sms > 0:
+        budget = max(2, ops.device_sm_count() - int(exchange_sms))
+    # Tile height of the one-chunk exchange (a function of the whole batch's
+    # capacity), so both forwards run the same GEMM configuration.
+    rows = K.tile_rows(n_ch * pxs[0].cap_rows * k // ep, epr, mod.hidden, mod.intermediate)
+
+    def dispatch(i):
+        a, b = bounds[i]
+        pxs[i].dispatch(plans[i].counts, local_x[a:b], plans[i].perm, ids[a:b], w[a:b], epr)
+
+    dispatch(0)
+    if n_ch > 1:
+        st.keep(local_x, ids, w, *[t for p in plans[1:] for t in (p.counts, p.perm)])
+        st.side_waits(st.mark())               # the plans are ready
+        with st.on_side():
+            dispatch(1)
+    arrived = [None] + [st.mark(side=True) if i == 1 else None for i in range(1, n_ch)]
+    for i in range(n_ch):
+        st.main_waits(arrived[i])              # chunk i has arrived
+        s_i = K.sort_align(pxs[i].recv_ids, epr + 1, 0, epr, want_inv=True, tile_rows=rows)
+        out_i = K.expert_compute(pxs[i].recv_rows, s_i.perm, k, s_i, wg, wu, wd,
+                                 max_sms=budget if n_ch > 1 else 0)
+        if i == n_ch - 1:
+            pxs[i].give_back(out_i, s_i.inv)   # the last return: critical path
+            break
+        st.keep(out_i, s_i.inv)
+        st.side_waits(st.mark())               # chunk i's expert outputs are ready
+        with st.on_side():
+            pxs[i].give_back(out_i, s_i.inv)
+            if i + 2 < n_ch:
+                dispatch(i + 2)
+        if i + 2 < n_ch:
+            arrived[i + 2] = st.mark(side=True)
+    st.main_waits(st.mark(side=True))          # every return has landed
+    y = local_x.new_empty((N, local_x.shape[1]))
+    for (a, b), p, px in zip(bounds, plans, pxs):
+        K.combine(px.ret_rows, b - a, ep, slot_src=p.inv, out=y[a:b])
+    return y
+
+
 class _A2ABase(_EPBase):
     """Transport selection shared by the all_to_all schedules."""
 
     def _init_transport(self, transport: str, max_tokens_per_rank: int | None,
-                        check_errors: bool) -> None:
+                        check_errors: bool, overlap: bool | int = False,
+                        exchange_sms: int = 16) -> None:
         if transport not in TRANSPORTS:
             raise ValueError(f"transport must be one of {TRANSPORTS}, got {transport!r}")
+        if overlap and transport != "peer":
+            raise ValueError("overlap needs transport='peer'")
+        chunks = 2 if overlap is True else int(overlap)
+        if overlap and chunks < 2:
+            raise ValueError(f"overlap takes True or a chunk count >= 2, got {overlap!r}")
         self.transport = transport
         self.max_tokens_per_rank = max_tokens_per_rank
         self.check_errors = check_errors
+        self.overlap = bool(overlap)
+        self.overlap_chunks = chunks if overlap else 1
+        self.exchange_sms = exchange_sms
         self._peer: PeerExchange | None = None
+        self._peer_chunks: list | None = None
+        self._streams: _Streams | None = None
 
     def _exchange(self, local_x: torch.Tensor, group) -> torch.Tensor:
         if self.transport == "nccl":
             return dispatch_combine(self, local_x, group)
+        if self.overlap:
+            return self._exchange_pipelined(local_x, group)
         if self._peer is None:
             # Collective, on the first forward of every rank: the capacity is
             # ep x the largest per-rank token count, then the buffers are swapped.
@@ -264,14 +384,43 @@ class _A2ABase(_EPBase):
                              "complete); pass max_tokens_per_rank to size the exchange")
         return dispatch_combine_peer(self, local_x, px)
 
+    def _exchange_pipelined(self, local_x: torch.Tensor, group) -> torch.Tensor:
+        n_ch = self.overlap_chunks
+        if self._peer_chunks is None:
+            # Collective, on the first forward: one exchange per token chunk,
+            # each sized for its share of the largest per-rank batch.
+            n_max = self.max_tokens_per_rank
+            if n_max is None:
+                n_max = max(_all_gather(local_x.shape[0], group))
+            cap = self.ep_size * (-(-int(n_max) // n_ch))
+            self._peer_chunks = [PeerExchange(group, cap, self.hidden, self.top_k, local_x.device)
+                                 for _ in range(n_ch)]
+            self._streams = _Streams(local_x.device)
+        pxs = self._peer_chunks
+        if any(getattr(px, "broken", False) for px in pxs):
+            raise RuntimeError("the peer exchange timed out in an earlier forward and its ranks "
+                               "may be out of step; call close() on every rank to rebuild it")
+        if -(-local_x.shape[0] // n_ch) * self.ep_size > pxs[0].cap_rows:
+            # As in the one-chunk exchange: take part with an empty batch, then refuse.
+            dispatch_combine_peer_pipelined(self, local_x[:0], pxs, self._streams,
+                                            self.exchange_sms)
+            raise ValueError(f"{local_x.shape[0]} tokens on this rank exceed the peer exchange "
+                             f"capacity of {n_ch * pxs[0].cap_rows // self.ep_size} tokens per "
+                             "rank; this rank sent nothing in this step; pass "
+                             "max_tokens_per_rank to size the exchange")
+        return dispatch_combine_peer_pipelined(self, local_x, pxs, self._streams,
+                                               self.exchange_sms)
+
     def _checked(self, y: torch.Tensor) -> torch.Tensor:
         if not self.check_errors:
             return y
         try:
             ops.check_status(y.device)
         except ops.MoEKernelError as err:
-            if err.code == ops.ERR_PEER_TIMEOUT and self._peer is not None:
-                self._peer.broken = True
+            if err.code == ops.ERR_PEER_TIMEOUT:
+                for px in [self._peer] + list(self._peer_chunks or []):
+                    if px is not None:
+                        px.broken = True
             raise
         return y
 
@@ -280,6 +429,12 @@ class _A2ABase(_EPBase):
         if self._peer is not None:
             self._peer.close()
             self._peer = None
+        if self._peer_chunks is not None:
+            if self._streams is not None and self._streams.cuda:
+                self._streams.side.synchronize()
+            for px in self._peer_chunks:
+                px.close()
+            self._peer_chunks = None
 
 
 class EPSparseMoEPure(_A2ABase):
@@ -291,10 +446,11 @@ class EPSparseMoEPure(_A2ABase):
     def __init__(self, hidden: int, intermediate: int, num_experts: int, top_k: int, ep_size: int,
                  ep_rank: int, group: dist.ProcessGroup | None = None,
                  norm_topk_prob: bool = True, *, transport: str = "nccl",
-                 max_tokens_per_rank: int | None = None, check_errors: bool = False) -> None:
+                 max_tokens_per_rank: int | None = None, check_errors: bool = False,
+                 overlap: bool | int = False, exchange_sms: int = 16) -> None:
         super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
         self.ep_group = group
-        self._init_transport(transport, max_tokens_per_rank, check_errors)
+        self._init_transport(transport, max_tokens_per_rank, check_errors, overlap, exchange_sms)
 
     def forward(self, local_x: torch.Tensor) -> torch.Tensor:
         shape = local_x.shape
@@ -310,13 +466,14 @@ class HybridMoE(_A2ABase):
                  tp_rank: int, tp_group: dist.ProcessGroup | None, ep_size: int, ep_rank: int,
                  ep_group: dist.ProcessGroup | None, norm_topk_prob: bool = True, *,
                  transport: str = "nccl", max_tokens_per_rank: int | None = None,
-                 check_errors: bool = False) -> None:
+                 check_errors: bool = False, overlap: bool | int = False,
+                 exchange_sms: int = 16) -> None:
         super().__init__(hidden, intermediate, num_experts, top_k, ep_size, ep_rank, norm_topk_prob)
         self.tp_size = tp_size
         self.tp_rank = tp_rank
         self.tp_group = tp_group
         self.ep_group = ep_group
-        self._init_transport(transport, max_tokens_per_rank, check_errors)
+        self._init_transport(transport, max_tokens_per_rank, check_errors, overlap, exchange_sms)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         shape = x.shape

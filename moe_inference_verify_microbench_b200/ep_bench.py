@@ -44,11 +44,14 @@ def zipf_router_bias(num_experts: int, s: float = 1.2) -> torch.Tensor:
 
 
 def _build(rank: int, world: int, dev: torch.device, T: int, transport: str,
-           schedule: str = "c7", tp: int = 1, zipf: bool = False):
+           schedule: str = "c7", tp: int = 1, zipf: bool = False, overlap: int = 0,
+           exchange_sms: int = 16):
     """The schedule's module with seeded weights (the same global expert e gets
     the same weights on every rank and in every schedule) and this rank's
     input: T own tokens (c7), the T replicated tokens (c6), or the T/dp tokens
-    of its TP group (c8).  ``zipf``: the router carries the Zipf(1.2) bias."""
+    of its TP group (c8).  ``zipf``: the router carries the Zipf(1.2) bias;
+    ``overlap``: chunk count of the exchange that overlaps the GEMMs (peer
+    only; 0 = one chunk, no overlap)."""
     from .ep import EPSparseMoELean, EPSparseMoEPure, HybridMoE
 
     x_rows, x_seed = T, 10 + rank
@@ -60,11 +63,13 @@ def _build(rank: int, world: int, dev: torch.device, T: int, transport: str,
             # Every rank creates every TP group, in the same order.
             groups = [dist.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(world // tp)]
             mod = HybridMoE(H, I, E, K_TOP, tp, rank % tp, groups[rank // tp], world, rank, None,
-                            transport=transport, max_tokens_per_rank=T // world)
+                            transport=transport, max_tokens_per_rank=T // world,
+                            overlap=overlap, exchange_sms=exchange_sms)
             x_rows, x_seed = T // (world // tp), 10 + rank // tp  # replicated within TP
         else:
             mod = EPSparseMoEPure(H, I, E, K_TOP, world, rank, group=None, transport=transport,
-                                  max_tokens_per_rank=T)
+                                  max_tokens_per_rank=T, overlap=overlap,
+                                  exchange_sms=exchange_sms)
         mod = mod.to(torch.bfloat16)
     wg, wu, wd = mod.pack()
     g = torch.Generator(device=dev)
@@ -151,7 +156,11 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
     schedule = getattr(args, "ep_schedule", "c7")
     tp = getattr(args, "tp", 1) if schedule == "c8" else 1
     zipf = bool(getattr(args, "zipf", False))
-    mod, x = _build(rank, world, dev, T, transport, schedule, tp, zipf)
+    overlap = int(getattr(args, "ep_overlap", 0) or 0)
+    if transport != "peer" or schedule == "c6":
+        overlap = 0
+    exchange_sms = int(getattr(args, "exchange_sms", 16))
+    mod, x = _build(rank, world, dev, T, transport, schedule, tp, zipf, overlap, exchange_sms)
     stream = torch.cuda.current_stream(dev)
     with torch.no_grad():
         for _ in range(args.warmup):
@@ -195,7 +204,11 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
         # router, ep_keys, plan sort, local sort (3), gate/up, down, combine
         # + (nccl) ep_meta, gather, partial combine
         # + (peer) publish, dispatch, recv wait, return, return wait
+        # + (overlap) every further chunk's ep_keys, plan sort, local sort (3),
+        #   gate/up, down, combine and exchange (5)
         launches = 14 if transport == "peer" else 12
+        if overlap:
+            launches += 13 * (overlap - 1)
     peaks = {}
     try:
         with open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
@@ -210,6 +223,8 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
     config = config_block(T, world, schedule, tp, zipf)
     if schedule != "c6":
         config["ep_transport"] = transport
+        if overlap:
+            config["ep_overlap"] = f"{overlap} token chunks, GEMMs on all but {exchange_sms} SMs"
     line = {
         "metric": metric, "value": job_tokens / (ms_step * 1e-3), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,

@@ -29,6 +29,7 @@ class MoEKernelError(RuntimeError):
 
 
 ERR_PEER_TIMEOUT = 0x105  # MOE_ERR_PEER_TIMEOUT
+RC_UNSUPPORTED = -2       # MOE_RC_UNSUPPORTED
 
 
 _status: dict[int, torch.Tensor] = {}
@@ -253,9 +254,12 @@ def grouped_w13_swiglu(a: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Te
 def grouped_w13_swiglu_gather(src: torch.Tensor, index: torch.Tensor, index_div: int, M: int,
                               tiles: torch.Tensor, num_tiles: torch.Tensor, max_tiles_: int,
                               w_gate: torch.Tensor, w_up: torch.Tensor,
-                              out: torch.Tensor | None = None, tile_rows: int = 128) -> torch.Tensor:
+                              out: torch.Tensor | None = None, tile_rows: int = 128,
+                              max_sms: int = 0) -> torch.Tensor:
     """``grouped_w13_swiglu`` whose A row r is ``src[index[r] // index_div]``: the
-    permutation gather (C5/python/solution.py:137) fused into the GEMM."""
+    permutation gather (C5/python/solution.py:137) fused into the GEMM.
+    ``max_sms`` > 0 caps the SMs the GEMM occupies (others stay free for
+    concurrent work); the result does not depend on it."""
     _need(src, "src", torch.bfloat16, 2)
     _need(index, "index", torch.int32)
     _need(w_gate, "w_gate", torch.bfloat16, 3)
@@ -268,19 +272,21 @@ def grouped_w13_swiglu_gather(src: torch.Tensor, index: torch.Tensor, index_div:
         raise ValueError("index must hold at least M entries")
     h = out if out is not None else torch.empty((M, I), dtype=torch.bfloat16, device=src.device)
     lib = _native.load()
-    _rc(lib.moe_grouped_w13_swiglu_gather_rows(_p(src), src.shape[0], _p(index), index_div, M,
-                                               _p(tiles), _p(num_tiles), max_tiles_, _p(w_gate),
-                                               _p(w_up), E, H, I, _p(h), tile_rows,
-                                               _p(status_word(src.device)), _stream(src.device)),
-        "moe_grouped_w13_swiglu_gather_rows")
+    _rc(lib.moe_grouped_w13_swiglu_gather_ex(_p(src), src.shape[0], _p(index), index_div, M,
+                                             _p(tiles), _p(num_tiles), max_tiles_, _p(w_gate),
+                                             _p(w_up), E, H, I, _p(h), tile_rows, int(max_sms),
+                                             _p(status_word(src.device)), _stream(src.device)),
+        "moe_grouped_w13_swiglu_gather_ex")
     return h
 
 
 def grouped_w2(h: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor, max_tiles_: int,
                w_down: torch.Tensor, row_map: torch.Tensor | None = None,
                slot_scale: torch.Tensor | None = None, out: torch.Tensor | None = None,
-               out_rows: int | None = None, tile_rows: int = 128) -> torch.Tensor:
-    """out[map(r)] = scale(map(r)) * (h[r] @ w_down[e]^T) (C9/python/solution.py:221)."""
+               out_rows: int | None = None, tile_rows: int = 128,
+               max_sms: int = 0) -> torch.Tensor:
+    """out[map(r)] = scale(map(r)) * (h[r] @ w_down[e]^T) (C9/python/solution.py:221);
+    ``max_sms`` as for ``grouped_w13_swiglu_gather``."""
     _need(h, "h", torch.bfloat16, 2)
     _need(w_down, "w_down", torch.bfloat16, 3)
     M, I = h.shape
@@ -295,10 +301,10 @@ def grouped_w2(h: torch.Tensor, tiles: torch.Tensor, num_tiles: torch.Tensor, ma
         out = torch.empty((out_rows if out_rows is not None else M, H), dtype=torch.bfloat16,
                           device=h.device)
     lib = _native.load()
-    _rc(lib.moe_grouped_w2_rows(_p(h), M, _p(tiles), _p(num_tiles), max_tiles_, _p(w_down), E, H,
-                                I, _p(row_map), _p(slot_scale), _p(out), out.shape[0], tile_rows,
-                                _p(status_word(h.device)), _stream(h.device)),
-        "moe_grouped_w2_rows")
+    _rc(lib.moe_grouped_w2_ex(_p(h), M, _p(tiles), _p(num_tiles), max_tiles_, _p(w_down), E, H,
+                              I, _p(row_map), _p(slot_scale), _p(out), out.shape[0], tile_rows,
+                              int(max_sms), _p(status_word(h.device)), _stream(h.device)),
+        "moe_grouped_w2_ex")
     return out
 
 
@@ -406,12 +412,23 @@ def moe_layer(x: torch.Tensor, router_weight: torch.Tensor, w_gate: torch.Tensor
               w_up: torch.Tensor, w_down: torch.Tensor, top_k: int, norm_topk_prob: bool = True,
               bias: torch.Tensor | None = None, out: torch.Tensor | None = None,
               workspace: torch.Tensor | None = None,
-              index_add: str = "deterministic") -> torch.Tensor:
+              index_add: str = "deterministic",
+              w_down_t: torch.Tensor | None = None) -> torch.Tensor:
     """Single-device MoE layer (C5/python/solution.py:108-161) in one C-ABI call.
     ``index_add``: "deterministic" (slot rows + k-sum in slot order, bitwise
     reproducible) or "atomic" (fp32 atomic accumulation per token, the
-    reference's index_add_ on CUDA; decode-size batches keep the slot rows)."""
+    reference's index_add_ on CUDA; decode-size batches keep the slot rows).
+    ``w_down_t`` (optional, [E, I, H]): with it, batches of up to 4 tokens and
+    32 records take the one-pass decode layer (``decode_layer_split``)."""
     mode = _combine_mode(index_add)
+    if (w_down_t is not None and mode == 0 and x.dim() == 2 and 0 < x.shape[0] <= 4
+            and x.shape[0] * top_k <= 32 and x.shape[1] <= 2048):
+        try:
+            return decode_layer_split(x, router_weight, w_gate, w_up, w_down_t, top_k,
+                                      norm_topk_prob, bias, out, workspace)
+        except MoEKernelError as err:
+            if err.code != RC_UNSUPPORTED:
+                raise
     _need(x, "x", torch.bfloat16, 2)
     for name, t in (("router_weight", router_weight), ("w_gate", w_gate), ("w_up", w_up),
                     ("w_down", w_down)):
@@ -438,6 +455,52 @@ def moe_layer(x: torch.Tensor, router_weight: torch.Tensor, w_gate: torch.Tensor
                                      _p(status_word(x.device)), _stream(x.device)),
             "moe_layer_forward_ex")
     return y
+
+
+def transpose_down_weights(w_down: torch.Tensor) -> torch.Tensor:
+    """w_down [E, H, I] -> w_down_t [E, I, H], the layout of the one-pass
+    decode layer (built once next to the weights)."""
+    _need(w_down, "w_down", torch.bfloat16, 3)
+    return w_down.transpose(1, 2).contiguous()
+
+
+def decode_layer_split(x: torch.Tensor, router_weight: torch.Tensor, w_gate: torch.Tensor,
+                       w_up: torch.Tensor, w_down_t: torch.Tensor, top_k: int,
+                       norm_topk_prob: bool = True, bias: torch.Tensor | None = None,
+                       out: torch.Tensor | None = None,
+                       workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The decode layer (T <= 4, T * top_k <= 32) in one launch and one pass
+    over the weights, on transposed down weights ``w_down_t`` [E, I, H].
+    Raises if it cannot run (no fallback); equals ``moe_layer`` up to fp32
+    summation order."""
+    _need(x, "x", torch.bfloat16, 2)
+    for name, t in (("router_weight", router_weight), ("w_gate", w_gate), ("w_up", w_up),
+                    ("w_down_t", w_down_t)):
+        _need(t, name, torch.bfloat16)
+    if bias is not None:
+        _need(bias, "bias", torch.float32, 1)
+    T, H = x.shape
+    E, I, _ = w_gate.shape
+    if tuple(w_down_t.shape) != (E, I, H):
+        raise ValueError(f"w_down_t must be [E, I, H] = {(E, I, H)}, got {tuple(w_down_t.shape)}")
+    lib = _native.load()
+    ws_bytes = int(lib.moe_decode_layer_workspace_bytes(T, H, E))
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+    y = out if out is not None else torch.empty_like(x)
+    rc = lib.moe_decode_layer_split(_p(x), _p(router_weight), _p(bias), _p(w_gate), _p(w_up),
+                                    _p(w_down_t), T, H, I, E, top_k, int(bool(norm_topk_prob)),
+                                    _p(workspace), workspace.numel(), _p(y),
+                                    _p(status_word(x.device)), _stream(x.device))
+    if rc != 0:
+        raise MoEKernelError(f"moe_decode_layer_split: {_native.error_string(rc)} (rc={rc}, "
+                             f"cuda error {lib.moe_last_cuda_error()})", rc)
+    return y
+
+
+def device_sm_count() -> int:
+    """SMs of the current CUDA device."""
+    return int(_native.load().moe_device_sm_count())
 
 
 def layer_workspace_bytes(T: int, H: int, I: int, E: int, top_k: int,

@@ -78,7 +78,7 @@ class CpuContractKernels:
 
     @staticmethod
     def expert_compute(src, index, index_div, s, w_gate, w_up, w_down, row_map=None,
-                       slot_scale=None, out_rows=None):
+                       slot_scale=None, out_rows=None, max_sms=0):
         M = index.numel()
         n = int(s.offsets[-1])
         xs = torch.zeros((M, src.shape[1]), dtype=src.dtype)
@@ -108,7 +108,11 @@ class CpuContractKernels:
             e = ids.reshape(-1).long()
             valid &= (e >= e_range[0]) & (e < e_range[1])
         contrib = rows.float()[s.clamp(min=0)] * (w * valid)[:, None]
-        return contrib.reshape(T, k, rows.shape[1]).sum(1).to(torch.bfloat16)
+        y = contrib.reshape(T, k, rows.shape[1]).sum(1).to(torch.bfloat16)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
 
 
 class CpuPeerExchange:

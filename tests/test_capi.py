@@ -39,7 +39,7 @@ def test_exported_dynamic_symbols_match_header():
 
 def test_host_queries():
     lib = _native.load()
-    assert lib.moe_abi_version() == 4
+    assert lib.moe_abi_version() == 5
     assert lib.moe_max_tiles(131072, 128) == 1024 + 128
     assert lib.moe_max_tiles(0, 16) == 16
     assert lib.moe_max_tiles_rows(131072, 128, 256) == 512 + 128

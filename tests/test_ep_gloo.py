@@ -36,21 +36,28 @@ def _worker(rank, world, port, name, transport, q):
         wu = [to_t(d["w_up"][e]) for e in range(E)]
         wd = [to_t(d["w_down"][e]) for e in range(E)]
         kind = str(g["kind"])
+        overlap = int(transport[12:] or 2) if transport.startswith("peer_overlap") else 0
+        tr = "peer" if overlap else transport
         if kind == "c6":
             mod = Lean(H, I, E, k, world, rank, group=None)
             x = xall[:T]
         elif kind == "c7":
-            mod = Pure(H, I, E, k, world, rank, group=None, transport=transport)
+            mod = Pure(H, I, E, k, world, rank, group=None, transport=tr, overlap=overlap)
             x = xall[rank * T:(rank + 1) * T]
         else:
             groups = [dist.new_group(list(range(i * tp, (i + 1) * tp))) for i in range(world // tp)]
             mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None,
-                            transport=transport)
+                            transport=tr, overlap=overlap)
             x = xall[(rank // tp) * T:(rank // tp + 1) * T]
         mod = mod.to(torch.bfloat16)
         mod._kernels = CpuContractKernels
         if transport == "peer":  # the exchange's buffer semantics, moved by gloo
             mod._peer = CpuPeerExchange(None, world * x.shape[0], H, k)
+        if overlap:  # one exchange per token chunk, in program order on CPU
+            from moe_inference_verify_microbench_b200.ep import _Streams
+            part = -(-x.shape[0] // overlap)
+            mod._peer_chunks = [CpuPeerExchange(None, world * part, H, k) for _ in range(overlap)]
+            mod._streams = _Streams(torch.device("cpu"))
         mod.weight_loader(wr, wg, wu, wd)
         if int(g["zipf"]):
             lin = torch.nn.Linear(H, E, bias=True).to(torch.bfloat16)
@@ -78,7 +85,10 @@ def _worker(rank, world, port, name, transport, q):
     # eight ranks: C6 ep=8, C7 dp=ep=8 with the Zipf skew, C8 tp=4 x dp=2 and tp=2 x dp=4
     ("ep_c6_w8.npz", 8, "nccl"), ("ep_c7_w8_zipf.npz", 8, "nccl"),
     ("ep_c7_w8_zipf.npz", 8, "peer"), ("ep_c8_w8_tp4.npz", 8, "nccl"),
-    ("ep_c8_w8_tp4.npz", 8, "peer"), ("ep_c8_w8_tp2.npz", 8, "peer")])
+    ("ep_c8_w8_tp4.npz", 8, "peer"), ("ep_c8_w8_tp2.npz", 8, "peer"),
+    # two token chunks, each exchange overlapping the other chunk's GEMMs
+    ("ep_c7_w4_zipf.npz", 4, "peer_overlap"), ("ep_c8_w4_tp2.npz", 4, "peer_overlap"),
+    ("ep_c7_w8_zipf.npz", 8, "peer_overlap"), ("ep_c7_w4_zipf.npz", 4, "peer_overlap3")])
 def test_ep_schedule_matches_reference(name, world, transport):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
@@ -95,6 +105,12 @@ def test_ep_schedule_matches_reference(name, world, transport):
     for rank, err, tie in res:
         assert tie <= 0.2, (rank, tie)
         assert err <= 2e-2, (rank, err)
+
+
+def test_overlap_needs_the_peer_transport():
+    from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE
+    with pytest.raises(ValueError):
+        EPSparseMoE(64, 32, 8, 2, 1, 0, group=None, transport="nccl", overlap=True)
 
 
 def test_unknown_transport_is_refused():

@@ -52,17 +52,19 @@ def _check_fixture(rank, world, dev, name, transport):
     wu = [to_t(d["w_up"][e], dev) for e in range(E)]
     wd = [to_t(d["w_down"][e], dev) for e in range(E)]
     kind = str(g["kind"])
+    overlap = int(transport[12:] or 2) if transport.startswith("peer_overlap") else 0
+    tr = "peer" if overlap else transport
     with torch.device(dev):
         if kind == "c6":
             mod = Lean(H, I, E, k, world, rank, group=None)
             x = xall[:T]
         elif kind == "c7":
-            mod = Pure(H, I, E, k, world, rank, group=None, transport=transport)
+            mod = Pure(H, I, E, k, world, rank, group=None, transport=tr, overlap=overlap)
             x = xall[rank * T:(rank + 1) * T]
         else:
             groups = [dist.new_group(list(range(i * tp, (i + 1) * tp))) for i in range(world // tp)]
             mod = HybridMoE(H, I, E, k, tp, rank % tp, groups[rank // tp], world, rank, None,
-                            transport=transport)
+                            transport=tr, overlap=overlap)
             x = xall[(rank // tp) * T:(rank // tp + 1) * T]
         mod = mod.to(torch.bfloat16)
     mod.weight_loader(wr, wg, wu, wd)
@@ -176,8 +178,9 @@ def test_ep_full_shapes_match_single_gpu_layer(kind):
 
 
 def _check_peer_vs_nccl(rank, world, dev):
-    """Four forwards with ragged per-rank token counts on both transports:
-    whether each pair of outputs is bit-identical."""
+    """Four forwards with ragged per-rank token counts on both transports and
+    on the peer transport with the two- and three-chunk overlapped exchange: whether
+    each peer output is bit-identical to the NCCL one."""
     import torch.distributed as dist
     from moe_inference_verify_microbench_b200 import ops
     from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
@@ -190,10 +193,12 @@ def _check_peer_vs_nccl(rank, world, dev):
     wu = (torch.randn(E, I, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
     wd = (torch.randn(E, H, I, generator=g, device=dev) * 0.02).to(torch.bfloat16)
     mods = {}
-    for tr in ("nccl", "peer"):
+    for name, tr, ov in (("nccl", "nccl", 0), ("peer", "peer", 0), ("overlap", "peer", 2),
+                         ("overlap3", "peer", 3)):
         with torch.device(dev):
-            mods[tr] = Pure(H, I, E, k, world, rank, group=None, transport=tr).to(torch.bfloat16)
-        mods[tr].weight_loader(wr, list(wg), list(wu), list(wd))
+            mods[name] = Pure(H, I, E, k, world, rank, group=None, transport=tr,
+                              overlap=ov).to(torch.bfloat16)
+        mods[name].weight_loader(wr, list(wg), list(wu), list(wd))
     same = []
     g.manual_seed(100 + rank)
     with torch.no_grad():
@@ -202,11 +207,16 @@ def _check_peer_vs_nccl(rank, world, dev):
             x = torch.randn(n, H, generator=g, device=dev).to(torch.bfloat16)
             dist.barrier()
             y_peer = mods["peer"](x)
+            y_over = mods["overlap"](x)
+            y_over3 = mods["overlap3"](x)
             y_nccl = mods["nccl"](x)
             same.append(bool(torch.equal(y_peer, y_nccl)))
+            same.append(bool(torch.equal(y_over, y_nccl)))
+            same.append(bool(torch.equal(y_over3, y_nccl)))
     torch.cuda.synchronize()
     ops.check_status(dev)
-    mods["peer"].close()
+    for name in ("peer", "overlap", "overlap3"):
+        mods[name].close()
     dist.barrier()
     return same
 
@@ -235,7 +245,7 @@ def _all_worker(rank, world, port, q):
     try:
         res = {}
         for name in EP_FIXTURES[world]:
-            for tr in (("nccl",) if "_c6_" in name else ("nccl", "peer")):
+            for tr in (("nccl",) if "_c6_" in name else ("nccl", "peer", "peer_overlap")):
                 res[f"{name}/{tr}"] = _check_fixture(rank, world, dev, name, tr)
         res["peer_bits_equal_nccl"] = _check_peer_vs_nccl(rank, world, dev)
         q.put((rank, res))

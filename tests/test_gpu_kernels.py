@@ -274,6 +274,34 @@ def test_pair_gemms_half_and_full_tiles(cuda, counts, H, I):
     assert mo.rel_err(acc.cpu().numpy(), oref) <= 1e-2
 
 
+@pytest.mark.parametrize("T,rows", [(2048, 128), (16384, 256), (4, 128)])
+def test_sm_budget_leaves_results_bitwise_equal(cuda, T, rows):
+    """The grouped GEMMs (and the decode GEMVs, T=4) on at most 16 SMs
+    (moe_grouped_*_ex with max_sms) produce bit for bit what they produce on
+    every SM: the budget only changes how work units are spread."""
+    H, I, E, k = 2048, 768, 128, 8
+    g = torch.Generator(device=cuda)
+    g.manual_seed(T + rows)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=g, device=cuda).to(bf)
+    wr = (torch.randn(E, H, generator=g, device=cuda) * 0.02).to(bf)
+    wg = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wu = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wd = (torch.randn(E, H, I, generator=g, device=cuda) * 0.02).to(bf)
+    ids, w, _ = ops.router_topk(x, wr, k)
+    s = ops.sort_align(ids, E, tile_rows=rows)
+    outs = []
+    for budget in (0, 16):
+        h = ops.grouped_w13_swiglu_gather(x, s.perm, k, T * k, s.tiles, s.num_tiles, s.max_tiles,
+                                          wg, wu, tile_rows=rows, max_sms=budget)
+        sl = ops.grouped_w2(h, s.tiles, s.num_tiles, s.max_tiles, wd, row_map=s.perm,
+                            slot_scale=w.reshape(-1), tile_rows=rows, max_sms=budget)
+        outs.append((h, sl))
+    ops.check_status(cuda)
+    assert ops.device_sm_count() > 16
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
 @pytest.mark.parametrize("T,k,H,I,E", [(300, 8, 256, 128, 16), (77, 4, 128, 64, 8), (2048, 8, 2048, 768, 128)])
 def test_w13_gather_fused_equals_gather_then_gemm(cuda, T, k, H, I, E):
     """The fused-gather A operand (cp.async, swizzled by hand) must reproduce the
@@ -360,6 +388,21 @@ def test_gemv_w13_w2_small_batches(cuda, counts, H, I):
     assert mo.rel_err(to_f32(out), ref_o) <= 1e-2
 
 
+def _decode_reference_f32(x, wr, wg, wu, wd, ids, w, k):
+    """fp32 torch restatement of the layer for given routing: bf16 h as the
+    kernels round it, fp32 down projection, bf16 slot rows, fp32 k-sum."""
+    T = x.shape[0]
+    xf = x.float()
+    y = torch.zeros(T, x.shape[1], device=x.device)
+    for n in range(T):
+        for j in range(k):
+            e = int(ids[n, j])
+            h = (torch.nn.functional.silu(xf[n] @ wg[e].float().T) * (xf[n] @ wu[e].float().T))
+            h = h.to(torch.bfloat16).float()
+            y[n] += ((wd[e].float() @ h) * w[n, j]).to(torch.bfloat16).float()
+    return y
+
+
 @pytest.mark.parametrize("T,norm,with_bias", [(1, True, False), (2, False, False), (4, True, True)])
 def test_single_launch_decode_layer_bitwise(cuda, T, norm, with_bias):
     """Up to 32 routing records (T <= 4 at top-8) run the whole layer as one
@@ -389,6 +432,79 @@ def test_single_launch_decode_layer_bitwise(cuda, T, norm, with_bias):
     ops.check_status(cuda)
     assert torch.equal(y, y2)
     assert torch.equal(y, y_again)
+
+
+def _decode_reference_f32(x, wr, wg, wu, wd, ids, w, k):
+    """fp32 torch restatement of the layer for given routing: bf16 h as the
+    kernels round it, fp32 down projection, bf16 slot rows, fp32 k-sum."""
+    T = x.shape[0]
+    xf = x.float()
+    y = torch.zeros(T, x.shape[1], device=x.device)
+    for n in range(T):
+        for j in range(k):
+            e = int(ids[n, j])
+            h = (torch.nn.functional.silu(xf[n] @ wg[e].float().T) * (xf[n] @ wu[e].float().T))
+            h = h.to(torch.bfloat16).float()
+            y[n] += ((wd[e].float() @ h) * w[n, j]).to(torch.bfloat16).float()
+    return y
+
+
+@pytest.mark.parametrize("T,norm,with_bias", [(1, True, False), (2, False, False), (3, True, False),
+                                              (4, True, True)])
+def test_one_pass_decode_layer(cuda, T, norm, with_bias):
+    """The one-pass decode layer on transposed down weights (router, top-k,
+    sort, one split-I stream over gate, up and w_down_t, segment sums and the
+    combine, one launch) at the full shapes (H=2048 I=768 E=128 k=8): equal
+    to the layer's own decode path up to fp32 summation order (at least 98 %
+    of the elements bit for bit, the rest within the bf16 rounding of the slot
+    rows), within 1e-2 of an fp32 restatement, and repeatable bit for bit.
+    ``moe_layer`` given w_down_t runs the same kernel."""
+    H, I, E, k = 2048, 768, 128, 8
+    g = torch.Generator(device=cuda)
+    g.manual_seed(500 + T)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=g, device=cuda).to(bf)
+    wr = (torch.randn(E, H, generator=g, device=cuda) * 0.02).to(bf)
+    wg = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wu = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wd = (torch.randn(E, H, I, generator=g, device=cuda) * 0.02).to(bf)
+    wdt = ops.transpose_down_weights(wd)
+    bias = torch.randn(E, generator=g, device=cuda) * 0.1 if with_bias else None
+    y = ops.decode_layer_split(x, wr, wg, wu, wdt, k, norm_topk_prob=norm, bias=bias)
+    y_again = ops.decode_layer_split(x, wr, wg, wu, wdt, k, norm_topk_prob=norm, bias=bias)
+    y_layer = ops.moe_layer(x, wr, wg, wu, wd, k, norm_topk_prob=norm, bias=bias, w_down_t=wdt)
+    y2 = ops.moe_layer(x, wr, wg, wu, wd, k, norm_topk_prob=norm, bias=bias)
+    ids, w, _ = ops.router_topk(x, wr, k, norm_topk_prob=norm, bias=bias)
+    ops.check_status(cuda)
+    assert torch.equal(y, y_again) and torch.equal(y, y_layer)
+    assert (y == y2).float().mean().item() >= 0.98
+    d = (y.float() - y2.float()).abs()
+    assert d.max().item() <= 2.0 ** -7 * y2.float().abs().max().item()
+    yref = _decode_reference_f32(x, wr, wg, wu, wd, ids, w, k)
+    assert ((y.float() - yref).norm() / yref.norm()).item() <= 1e-2
+
+
+@pytest.mark.parametrize("T,k,E,I", [(1, 4, 16, 128), (1, 8, 16, 16), (4, 8, 64, 128),
+                                     (2, 1, 128, 768)])
+def test_one_pass_decode_layer_ragged_ranges(cuda, T, k, E, I):
+    """Small shapes where most CTAs get an empty item range, a tile spans a
+    single item or two (I=16), or one CTA range covers several tiles: the
+    segment bookkeeping of the one-pass decode layer must still sum every
+    partial once."""
+    H = 256
+    g = torch.Generator(device=cuda)
+    g.manual_seed(900 + T * 10 + I)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=g, device=cuda).to(bf)
+    wr = (torch.randn(E, H, generator=g, device=cuda) * 0.05).to(bf)
+    wg = (torch.randn(E, I, H, generator=g, device=cuda) * 0.05).to(bf)
+    wu = (torch.randn(E, I, H, generator=g, device=cuda) * 0.05).to(bf)
+    wd = (torch.randn(E, H, I, generator=g, device=cuda) * 0.05).to(bf)
+    y = ops.decode_layer_split(x, wr, wg, wu, ops.transpose_down_weights(wd), k)
+    ids, w, _ = ops.router_topk(x, wr, k)
+    ops.check_status(cuda)
+    yref = _decode_reference_f32(x, wr, wg, wu, wd, ids, w, k)
+    assert ((y.float() - yref).norm() / yref.norm()).item() <= 1e-2
 
 
 @pytest.mark.parametrize("T,k,E", [(1, 4, 16), (3, 8, 64), (16, 8, 128), (17, 4, 32)])
