@@ -195,7 +195,8 @@ def run_reference(args):
         "metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
         "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
-        "scaling": "strong" if args.gpus > 1 and args.ep_schedule in ("c6", "c8") else "weak",
+        "scaling": ("strong" if args.gpus > 1 and args.ep_schedule in ("c6", "c8", "c8block")
+                    else "weak"),
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": config_block(T, args.gpus, args.ep_schedule, args.tp, args.zipf),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
@@ -221,6 +222,12 @@ def config_block(T: int, n: int, schedule: str = "c7", tp: int = 1, zipf: bool =
         per_rank = T // n
         wl = (f"hybrid TP x EP MoE layer (C8 path), {T} tokens in all, tp={tp} x dp={n // tp}, "
               f"a stripe of {per_rank} tokens per rank, E/{n} experts per rank, closing all_gather")
+        par = f"tp{tp}xdp{n // tp}=ep{n}"
+    elif schedule == "c8block":
+        per_rank = T // n
+        wl = (f"hybrid TP x EP decoder block (C8 HybridBlock: add+RMSNorm, TP GQA attention "
+              f"32q/4kv heads of 128 over {T // 2048} sequences of 2048, add+RMSNorm, C8 MoE), "
+              f"{T} tokens in all, tp={tp} x dp={n // tp}, E/{n} experts per rank")
         par = f"tp{tp}xdp{n // tp}=ep{n}"
     else:
         wl = f"expert-parallel all_to_all MoE layer (C7 path), {T} tokens per rank, E/{n} experts per rank"
@@ -255,7 +262,7 @@ class Timer:
 # the gate/up GEMM at T=16384, taken from an ncu capture of that kernel on
 # B200 (not measured by this script: CUDA events cannot count DRAM bytes).
 # The weight bytes do not grow with T, so no other size is scaled from it.
-W13_TRAFFIC = {(16384, 256): 1211178240 + 192313344}
+W13_TRAFFIC = {(16384, 256): 1212910080 + 192624384}
 W13_TRAFFIC_SOURCE = ("ncu capture of the same kernel at T=16384 "
                       "(dram__bytes_read.sum + dram__bytes_write.sum, one launch); "
                       "a recorded constant, not measured in this run")
@@ -519,23 +526,31 @@ def kernel_breakdown(dev, x, wr, wg, wu, wd, T, n_steps):
 def sweep(dev, token_counts, wr, wg, wu, wd, peaks):
     """Decode / prefill sweep: CUDA-graph-captured layer, inputs resident.  A
     512 MB buffer is written before every replay (outside the timed events), so
-    each layer call finds the weights in HBM, not in the 126 MB L2."""
+    each layer call finds the weights in HBM, not in the 126 MB L2.  Batches
+    of up to 4 tokens are also timed on the one-pass decode layer (key
+    "<T>_one_pass"), which takes the down weights transposed as well (built
+    once, before any timing)."""
     from moe_inference_verify_microbench_b200 import ops
     out = {}
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
-    for T in token_counts:
+    wdt = ops.transpose_down_weights(wd) if any(0 < t <= 4 for t in token_counts) else None
+    runs = [(T, None) for T in token_counts] + [(T, wdt) for T in token_counts if 0 < T <= 4]
+    for T, w_down_t in runs:
         g = torch.Generator(device=dev)
         g.manual_seed(T)
         x = torch.randn(T, H, generator=g, device=dev).to(torch.bfloat16)
         ws = torch.empty(ops.layer_workspace_bytes(T, H, I, E, K_TOP), dtype=torch.uint8, device=dev)
+        if w_down_t is not None:
+            ws = torch.empty(ops.decode_layer_workspace_bytes(T, H, E), dtype=torch.uint8,
+                             device=dev)
         y = torch.empty_like(x)
         for _ in range(3):
-            ops.moe_layer(x, wr, wg, wu, wd, K_TOP, out=y, workspace=ws)
+            ops.moe_layer(x, wr, wg, wu, wd, K_TOP, out=y, workspace=ws, w_down_t=w_down_t)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            ops.moe_layer(x, wr, wg, wu, wd, K_TOP, out=y, workspace=ws)
+            ops.moe_layer(x, wr, wg, wu, wd, K_TOP, out=y, workspace=ws, w_down_t=w_down_t)
         n = 50 if T <= 1024 else 20
         for _ in range(3):
             graph.replay()
@@ -555,11 +570,12 @@ def sweep(dev, token_counts, wr, wg, wu, wd, peaks):
         n_act = int(torch.bincount(ids.reshape(-1).long(), minlength=E).gt(0).sum())
         peak_tc = peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]
         t_roof = max(layer_flops(T) / (peak_tc * 1e12), layer_bytes(n_act, T) / (peaks["hbm_gbs"] * 1e9))
-        out[str(T)] = {"tokens_per_s": T / (ms * 1e-3), "us_per_layer": ms * 1e3,
+        out[str(T) + ("_one_pass" if w_down_t is not None else "")] = {
+                       "tokens_per_s": T / (ms * 1e-3), "us_per_layer": ms * 1e3,
                        "roofline_frac": t_roof * 1e3 / ms, "active_experts": n_act,
                        "hbm_gbs": layer_bytes(n_act, T) / (ms * 1e-3) / 1e9}
         del graph
-    del flush
+    del flush, wdt
     return out
 
 
@@ -574,8 +590,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ep-transport", choices=["peer", "nccl"], default="peer",
                     help="N>1: peer-store exchange over NVLink, or NCCL all_to_alls")
-    ap.add_argument("--ep-schedule", choices=["c7", "c6", "c8"], default="c7",
-                    help="N>1: all_to_all (c7), replicated + all_reduce (c6), hybrid TP x EP (c8)")
+    ap.add_argument("--ep-schedule", choices=["c7", "c6", "c8", "c8block"], default="c7",
+                    help="N>1: all_to_all (c7), replicated + all_reduce (c6), hybrid TP x EP (c8), "
+                         "the whole C8 decoder block with attention (c8block)")
     ap.add_argument("--tp", type=int, default=2, help="c8: tensor-parallel group size")
     ap.add_argument("--zipf", action="store_true",
                     help="N>1: Zipf(1.2) router bias (the skewed-routing C7 configuration)")
@@ -594,10 +611,12 @@ def main():
     multi = int(os.environ.get("WORLD_SIZE", "1")) > 1 or args.gpus > 1
     if args.tokens is None:
         args.tokens = 4096 if multi and args.ep_schedule == "c6" else 16384
-    if multi and args.ep_schedule == "c8":
+    if multi and args.ep_schedule in ("c8", "c8block"):
         n = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
         if args.tp < 1 or n % args.tp != 0 or args.tokens % n != 0:
             ap.error(f"c8 needs tp dividing N={n} and tokens divisible by N")
+        if args.ep_schedule == "c8block" and (args.tokens // (n // args.tp)) % 2048 != 0:
+            ap.error("c8block needs whole 2048-token sequences per TP group")
     if args.impl == "reference":
         run_reference(args)
         return

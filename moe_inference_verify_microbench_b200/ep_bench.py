@@ -14,6 +14,11 @@ on N GPUs, one process per GPU, E/N experts per rank.
   every TP group holds T/dp tokens, each rank runs the C7 core on its 1/tp
   stripe (T/N tokens) and the TP group all_gathers the stripes (strong
   scaling).  ``value`` = T / step time.
+* ``c8block``: ``HybridBlock`` (C8/python/solution.py:235-325), the whole
+  pre-norm decoder block (fused residual add + RMSNorms, TP GQA attention
+  over 2048-token sequences with Qwen3-30B-A3B's 32 query / 4 KV heads of
+  128, then the C8 MoE) on T/2048 sequences, tp × dp = N, each TP group
+  holding T/dp tokens (strong scaling).  ``value`` = T / step time.
 
 Timing: W warm-up steps, then K steps bracketed by a barrier and a device
 synchronise on both sides, CUDA events on each rank's stream, the maximum
@@ -32,6 +37,9 @@ import torch
 import torch.distributed as dist
 
 H, I, E, K_TOP = 2048, 768, 128, 8
+# Attention of the decoder block (Qwen3-30B-A3B): 32 query and 4 KV heads of
+# 128, over sequences of 2048 tokens.
+ATTN_HEADS, ATTN_KV_HEADS, ATTN_HEAD_DIM, ATTN_SEQ = 32, 4, 128, 2048
 
 
 def zipf_router_bias(num_experts: int, s: float = 1.2) -> torch.Tensor:
@@ -55,8 +63,28 @@ def _build(rank: int, world: int, dev: torch.device, T: int, transport: str,
     from .ep import EPSparseMoELean, EPSparseMoEPure, HybridMoE
 
     x_rows, x_seed = T, 10 + rank
+    moe_options = dict(transport=transport, max_tokens_per_rank=T // world, overlap=overlap,
+                       exchange_sms=exchange_sms)
     with torch.device(dev):
-        if schedule == "c6":
+        if schedule == "c8block":
+            from .hybrid import HybridBlock
+            groups = [dist.new_group(list(range(g * tp, (g + 1) * tp))) for g in range(world // tp)]
+            blk = HybridBlock(H, I, ATTN_HEADS, ATTN_KV_HEADS, ATTN_HEAD_DIM, E, K_TOP, tp, rank % tp,
+                              groups[rank // tp], world, rank, None, **moe_options)
+            blk = blk.to(torch.bfloat16)
+            g = torch.Generator(device=dev)
+            g.manual_seed(7)  # attention weights, the same on every rank before sharding
+            qd, kvd = ATTN_HEADS * ATTN_HEAD_DIM, ATTN_KV_HEADS * ATTN_HEAD_DIM
+            rnd = lambda *shape: (torch.randn(*shape, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+            wq, wk, wv, wo = rnd(qd, H), rnd(kvd, H), rnd(kvd, H), rnd(H, qd)
+            with torch.no_grad():
+                blk.attn.qkv_proj.weight_loader(wq, "q")
+                blk.attn.qkv_proj.weight_loader(wk, "k")
+                blk.attn.qkv_proj.weight_loader(wv, "v")
+                blk.attn.o_proj.weight_loader(wo)
+            mod = blk.moe  # the MoE weights below; the block is returned
+            x_rows, x_seed = T // (world // tp), 10 + rank // tp
+        elif schedule == "c6":
             mod = EPSparseMoELean(H, I, E, K_TOP, world, rank, group=None)
             x_seed = 10  # replicated input
         elif schedule == "c8":
@@ -87,6 +115,8 @@ def _build(rank: int, world: int, dev: torch.device, T: int, transport: str,
             lin.weight.copy_(mod.gate.weight)
             lin.bias.copy_(zipf_router_bias(E).to(torch.bfloat16))
             mod.gate = lin
+    if schedule == "c8block":
+        return blk, x.reshape(x_rows // ATTN_SEQ, ATTN_SEQ, H)
     return mod, x
 
 
@@ -118,13 +148,21 @@ def run_ep(args, metric, config_block, clock_sampler_cls) -> None:
         dist.destroy_process_group()
 
 
-def schedule_work(schedule: str, T: int, world: int):
+def schedule_work(schedule: str, T: int, world: int, tp: int = 1):
     """(expected FLOP per rank, tokens of the whole job, scaling kind) of one
     step.  c7: every rank routes and computes its own T tokens (a rank's
     experts receive T·k records on average); c6: every rank routes all T
     replicated tokens and computes 1/N of their records; c8: every rank routes
     and computes its stripe of T/N tokens."""
     per_token = 2 * H * E + K_TOP * 6 * H * I
+    if schedule == "c8block":
+        # + attention per token of a rank's stripe: q/k/v/o projections on
+        # 1/tp of the heads and causal attention (half of the 4·S·d per head)
+        tp = max(1, tp)
+        proj = 2 * H * (ATTN_HEADS + 2 * ATTN_KV_HEADS) * ATTN_HEAD_DIM + 2 * ATTN_HEADS * ATTN_HEAD_DIM * H
+        attn = 2 * ATTN_SEQ * ATTN_HEAD_DIM * ATTN_HEADS
+        tokens_tp_group = T // (world // tp)
+        return tokens_tp_group * (proj + attn) / tp + (T // world) * per_token, T, "strong"
     if schedule == "c6":
         return T * 2 * H * E + T * K_TOP * 6 * H * I / world, T, "strong"
     if schedule == "c8":
@@ -154,7 +192,7 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
     T = args.tokens
     transport = getattr(args, "ep_transport", "nccl")
     schedule = getattr(args, "ep_schedule", "c7")
-    tp = getattr(args, "tp", 1) if schedule == "c8" else 1
+    tp = getattr(args, "tp", 1) if schedule in ("c8", "c8block") else 1
     zipf = bool(getattr(args, "zipf", False))
     overlap = int(getattr(args, "ep_overlap", 0) or 0)
     if transport != "peer" or schedule == "c6":
@@ -192,11 +230,17 @@ def _run(args, metric, config_block, clock_sampler_cls, rank, world, dev) -> Non
     ms_step = ms / args.steps
     if rank != 0:
         return
-    flop_rank, job_tokens, scaling = schedule_work(schedule, T, world)
+    flop_rank, job_tokens, scaling = schedule_work(schedule, T, world, tp)
     if schedule == "c6":
         api = "EPSparseMoE.forward (C6 lean schedule, NCCL all_reduce)"
         exchange = "NCCL all_reduce"
         launches = 7  # router, sort (3), gate/up, down, masked combine
+    elif schedule == "c8block":
+        api = f"HybridBlock.forward (C8 block, tp={tp}, transport={transport})"
+        exchange = f"{transport} exchange + NCCL all_gather + attention all_reduce"
+        # two add_rmsnorm rows kernels + the C8 MoE's launches (below); the
+        # attention's projections and SDPA are torch (cuBLAS / flash) kernels
+        launches = 2 + (14 if transport == "peer" else 12) + (13 * (overlap - 1) if overlap else 0)
     else:
         api = (f"EPSparseMoE.forward (C7 schedule, transport={transport})" if schedule == "c7" else
                f"HybridMoE.forward (C8 schedule, tp={tp}, transport={transport})")

@@ -125,14 +125,16 @@ class HybridBlock(nn.Module):
                  head_dim: int, num_experts: int, top_k: int, tp_size: int, tp_rank: int,
                  tp_group: dist.ProcessGroup | None, ep_size: int, ep_rank: int,
                  ep_group: dist.ProcessGroup | None, norm_topk_prob: bool = True,
-                 rope_base: float = 10000.0, rms_eps: float = 1e-6) -> None:
+                 rope_base: float = 10000.0, rms_eps: float = 1e-6, **moe_options) -> None:
+        """``moe_options``: keyword extras of ``HybridMoE`` (transport,
+        max_tokens_per_rank, check_errors, overlap, exchange_sms)."""
         super().__init__()
         self.attn_norm = RMSNorm(hidden, eps=rms_eps)
         self.attn = TPGQA(hidden, n_heads, n_kv_heads, head_dim, rope_base=rope_base,
                           tp_size=tp_size, tp_rank=tp_rank, group=tp_group)
         self.moe_norm = RMSNorm(hidden, eps=rms_eps)
         self.moe = HybridMoE(hidden, intermediate, num_experts, top_k, tp_size, tp_rank, tp_group,
-                             ep_size, ep_rank, ep_group, norm_topk_prob)
+                             ep_size, ep_rank, ep_group, norm_topk_prob, **moe_options)
 
     @torch.no_grad()
     def weight_loader(self, attn_norm_weight, q_weight, k_weight, v_weight, o_weight,

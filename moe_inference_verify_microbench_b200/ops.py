@@ -464,6 +464,11 @@ def transpose_down_weights(w_down: torch.Tensor) -> torch.Tensor:
     return w_down.transpose(1, 2).contiguous()
 
 
+def decode_layer_workspace_bytes(T: int, H: int, E: int) -> int:
+    """Workspace bytes of ``decode_layer_split``."""
+    return int(_native.load().moe_decode_layer_workspace_bytes(T, H, E))
+
+
 def decode_layer_split(x: torch.Tensor, router_weight: torch.Tensor, w_gate: torch.Tensor,
                        w_up: torch.Tensor, w_down_t: torch.Tensor, top_k: int,
                        norm_topk_prob: bool = True, bias: torch.Tensor | None = None,

@@ -104,6 +104,23 @@ def test_bench_config_names_the_schedule(sched, tp, per_rank, par):
     assert sched.upper() in c["workload"]
 
 
+def test_bench_block_schedule_config_and_work():
+    """The decoder-block schedule (HybridBlock at 8 x 2048 tokens): its config
+    names the block and its FLOP count adds the attention of a rank's share
+    (projections on 1/tp of the heads, causal attention over 2048 tokens)."""
+    sys.path.insert(0, os.path.dirname(HERE))
+    import bench
+    from moe_inference_verify_microbench_b200.ep_bench import schedule_work
+    c = bench.config_block(16384, 8, "c8block", 4)
+    assert "HybridBlock" in c["workload"] and c["parallelism"] == "tp4xdp2=ep8"
+    f, t, kind = schedule_work("c8block", 16384, 8, 4)
+    moe = 2048 * 76_021_760
+    proj = 2 * 2048 * (32 + 8) * 128 + 2 * 32 * 128 * 2048
+    attn = 2 * 2048 * 128 * 32
+    assert t == 16384 and kind == "strong"
+    assert f == 8192 * (proj + attn) / 4 + moe
+
+
 def test_roofline_arithmetic_matches_the_per_token_figures():
     """The FLOP counts behind every bench line's roofline: 76,021,760 FLOP per
     token for the layer (2·H·E router + 8 × 6·H·I experts), bytes = 9,437,184
