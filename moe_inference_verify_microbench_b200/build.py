@@ -21,7 +21,8 @@ CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libmoe_b200.so")
 SOURCES = ["capi.cu", "gemm.cu", "sort_align.cu", "rows.cu", "sort_align_static.cu", "decode.cu",
            "ep_plan.cu", "ep_peer.cu"]
-HEADERS = ["ptx.cuh", "grouped_gemm.cuh", "grouped_gemm_pair.cuh", "internal.h", "sort_block.cuh"]
+HEADERS = ["ptx.cuh", "grouped_gemm.cuh", "grouped_gemm_pair.cuh", "internal.h", "sort_block.cuh",
+           "router_splitk.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH_FLAGS + [
     "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",

@@ -6,6 +6,7 @@
 #include "grouped_gemm.cuh"
 #include "grouped_gemm_pair.cuh"
 #include "internal.h"
+#include "router_splitk.cuh"
 
 namespace moe {
 
@@ -87,6 +88,20 @@ int device_sms() {
 long long sm_budget(int max_sms) {
   const long long sms = device_sms();
   return max_sms > 0 && max_sms < sms ? max_sms : sms;
+}
+
+// Raise a kernel's dynamic shared memory limit to `bytes`, once per device.
+template <class Kernel>
+bool allow_kernel_smem(Kernel* fn, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const uint64_t bit = 1ull << (dev & 63);
+  if ((done.load(std::memory_order_acquire) & bit) != 0) return true;
+  if (note_cuda_error(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           bytes)) != cudaSuccess)
+    return false;
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return true;
 }
 
 template <int BN, int EPI, int STAGES, bool GATHER_A = false>
@@ -200,8 +215,46 @@ int launch_router(const void* x, const void* wr, const float* bias, int T, int H
   int rc = map_2d(&ma, x, T, H, kBM);
   if (rc == kRcOk) rc = map_3d(&mb, wr, 1, E, H, E);
   if (rc != kRcOk) return rc;
+  // At most 8 tiles of 128 tokens (T <= 1024): split K over a cluster of 2,
+  // 4 or 8 CTAs per tile (router_splitk.cuh), so up to 8x the SMs stream the
+  // operands.  Measured per layer (graph replay, H=2048 E=128): T=128 242 ->
+  // 236 us, T=1024 264 -> 260 us; at 16 and more tiles the split measured
+  // slower (T=2048 +10 us, T=4096 +4 us, T=8192 +26 us): its 200 KB-smem CTAs
+  // then cover most SMs and delay the next kernels' early start.
+  const int tiles = (T + kBM - 1) / kBM;
+  const int nkb = H / kBK;
+  int split = 1;
+  if (E <= kRsMaxE && tiles <= kRsMaxTiles) {
+    for (int cand : {8, 4, 2}) {
+      if (static_cast<long long>(tiles) * cand <= device_sms() && nkb % cand == 0 &&
+          nkb / cand >= 2) {
+        split = cand;
+        break;
+      }
+    }
+  }
+  if (split > 1) {
+    static std::atomic<uint64_t> attr{0};
+    if (!allow_kernel_smem(router_splitk, static_cast<int>(kRsSmemBytes), attr))
+      return kRcCudaError;
+    RouterSplitArgs ra{};
+    ra.T = T;
+    ra.E = E;
+    ra.k = k;
+    ra.norm_topk_prob = norm_topk_prob;
+    ra.kb_per_split = nkb / split;
+    ra.bias = bias;
+    ra.ids_out = ids_out;
+    ra.w_out = w_out;
+    ra.logits_out = static_cast<__nv_bfloat16*>(logits_out);
+    ra.status = status;
+    const cudaError_t e =
+        launch_pdl_cluster(router_splitk, dim3(tiles * split), dim3(kRsThreads), kRsSmemBytes,
+                           stream, static_cast<unsigned>(split), ma, mb, ra);
+    return note_cuda_error(e) == cudaSuccess ? kRcOk : kRcCudaError;
+  }
   GemmArgs g = blank_args(status);
-  g.max_tiles = (T + kBM - 1) / kBM;
+  g.max_tiles = tiles;
   g.n_tiles = 1;
   g.num_kb = H / kBK;
   g.b_rows = E;

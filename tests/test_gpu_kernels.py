@@ -118,8 +118,13 @@ def test_combine_weighted_indirect(cuda):
 @pytest.mark.parametrize("T,H,E,k,norm,bias", [
     (1, 256, 16, 4, True, False), (5, 256, 128, 8, True, False), (128, 512, 128, 8, True, True),
     (300, 2048, 128, 8, True, False), (257, 256, 64, 8, False, False), (1000, 2048, 128, 8, False, True),
+    (20000, 256, 128, 8, True, False), (4096, 2048, 128, 8, True, True),
 ])
 def test_router_topk(cuda, T, H, E, k, norm, bias):
+    """Router logits, top-k ids and weights against the oracle.  Up to 16
+    tokens: the cluster kernel on the CUDA cores; up to 8 tiles of 128 tokens:
+    the K-split cluster kernel (router_splitk, 2 to 8 ranks per tile); more
+    (T=4096, 20000 here): one tcgen05 CTA per tile."""
     d = mo.make_inputs(T, H, 64, E, seed=T, experts=False)
     x = mo.f32_from_bf16_bits(d["x"])
     wr = mo.f32_from_bf16_bits(d["wr"])

@@ -201,6 +201,79 @@ def test_layer_decode_sizes_full_shapes(cuda, T):
     assert mo.rel_err(to_f32(y), ref) <= REL_TOL
 
 
+@pytest.mark.parametrize("T", [128, 1024])
+@pytest.mark.parametrize("seed", [0, 1, 2, 3, 4])
+def test_layer_sweep_sizes_seeds_full_shapes(cuda, T, seed):
+    """The T sweep's mid sizes at H=2048 I=768 E=128 k=8 on five seeds with the
+    benchmark's distributions (x ~ N(0,1), weights ~ N(0, 0.02)): the routing
+    bit-exact against the oracle's top-k of the kernel's logits, and 32
+    sampled tokens within tolerance of an fp32 evaluation of the same routing
+    (bf16 h and slot rows, as the kernels round them)."""
+    H, I, E, k = 2048, 768, 128, 8
+    g = torch.Generator(device=cuda)
+    g.manual_seed(1000 * seed + T)
+    bf = torch.bfloat16
+    x = torch.randn(T, H, generator=g, device=cuda).to(bf)
+    wr = (torch.randn(E, H, generator=g, device=cuda) * 0.02).to(bf)
+    wg = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wu = (torch.randn(E, I, H, generator=g, device=cuda) * 0.02).to(bf)
+    wd = (torch.randn(E, H, I, generator=g, device=cuda) * 0.02).to(bf)
+    y = ops.moe_layer(x, wr, wg, wu, wd, k)
+    ids, w, lg = ops.router_topk(x, wr, k, return_logits=True)
+    ops.check_status(cuda)
+    _, rid = mo.topk_ids(to_f32(lg), k)
+    assert np.array_equal(ids.cpu().numpy(), rid)
+    tok = torch.linspace(0, T - 1, 32, device=cuda).long().unique()
+    xf = x.float()
+    ref = torch.zeros(tok.numel(), H, device=cuda)
+    for i, n in enumerate(tok.tolist()):
+        for j in range(k):
+            e = int(ids[n, j])
+            h = torch.nn.functional.silu(wg[e].float() @ xf[n]) * (wu[e].float() @ xf[n])
+            ref[i] += ((wd[e].float() @ h.to(bf).float()) * w[n, j]).to(bf).float()
+    err = (y[tok].float() - ref).abs().max() / ref.abs().max()
+    assert err.item() <= REL_TOL
+
+
+def test_permuted_sparse_moe_decode_weights(cuda):
+    """PermutedSparseMoE(decode_weights=True) runs a 1-token batch on the
+    one-pass decode layer (the same output as the op on the module's
+    transposed copy), keeps batches above 4 tokens on the standard path, and
+    follows new per-expert weights after an explicit refresh."""
+    H, I, E, k = 2048, 768, 128, 8
+    g = torch.Generator(device=cuda)
+    g.manual_seed(77)
+    bf = torch.bfloat16
+    r = lambda *s: (torch.randn(*s, generator=g, device=cuda) * 0.02).to(bf)  # noqa: E731
+    wr, wg, wu, wd = r(E, H), r(E, I, H), r(E, I, H), r(E, H, I)
+
+    def load(mod, down):
+        mod.pack()
+        with torch.no_grad():
+            mod.gate.weight.copy_(wr)
+            for e, ex in enumerate(mod.experts):
+                ex.gate_proj.weight.copy_(wg[e])
+                ex.up_proj.weight.copy_(wu[e])
+                ex.down_proj.weight.copy_(down[e])
+
+    with torch.device(cuda):
+        m = PermutedSparseMoE(H, I, E, k, decode_weights=True).to(bf)
+        plain = PermutedSparseMoE(H, I, E, k).to(bf)
+    load(m, wd)
+    load(plain, wd)
+    x1 = torch.randn(1, H, generator=g, device=cuda).to(bf)
+    x8 = torch.randn(8, H, generator=g, device=cuda).to(bf)
+    t = lambda w: w.transpose(1, 2).contiguous()  # noqa: E731
+    with torch.no_grad():
+        assert torch.equal(m(x1), ops.decode_layer_split(x1, wr, wg, wu, t(wd), k))
+        assert torch.equal(m(x8), plain(x8))
+        wd2 = r(E, H, I)
+        load(m, wd2)
+        m.down_weights_transposed(refresh=True)
+        assert torch.equal(m(x1), ops.decode_layer_split(x1, wr, wg, wu, t(wd2), k))
+    ops.check_status(cuda)
+
+
 # ------------------------------------------------------------ index_add_ switch
 
 
