@@ -639,7 +639,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
 // every wait is bounded (kErrTimeoutGrid), and a CTA that gives up skips the
 // rest of the layer.
 
-constexpr int kFusedMaxRecs = kGemvW2MaxRows;
+constexpr int kFusedMaxRecs = 32;  // one warp lane per routing record in the sort
 
 struct DecodeArgs {
   const uint4* x;          // [T][H]
