@@ -276,7 +276,7 @@ def w13_kernel_name(tile_rows):
 
 SORT_CHUNK, SORT_THREADS, CLUSTER_SORT_MAX, CLUSTER_CHUNK = 2048, 256, 8, 4096
 GEMV_W13_MAX_ROWS, ROUTER_SMALL_MAX_T = 128, 16
-FUSED_DECODE_MAX_T, FUSED_DECODE_MAX_RECS = 4, 32
+FUSED_DECODE_MAX_T, FUSED_DECODE_MAX_RECS = 16, 64
 
 
 def sort_launches(R: int, e_local: int = E) -> int:
@@ -291,8 +291,8 @@ def sort_launches(R: int, e_local: int = E) -> int:
 
 
 def layer_launches(T, tile_rows=None):
-    """Kernels moe_layer_forward launches for T tokens.  Up to 4 tokens and 32
-    records: the single-launch decode layer.  Decode (T*k <= 128 records):
+    """Kernels moe_layer_forward launches for T tokens.  Up to 64 records
+    (T <= 8 at top-8): the single-launch decode layer.  Decode (T*k <= 128 records):
     router and sort fused in one kernel for T <= 16, the gate/up
     weight-streaming kernel, the down GEMV or GEMM, the combine.  Otherwise:
     router, sort (``sort_launches``), gate/up GEMM with the row gather fused,

@@ -618,7 +618,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
 // ------------------------------------------------------------------ single-launch decode layer
 //
 // decode_layer_fused: the whole MoE layer for at most kFusedMaxRecs routing
-// records (T * k <= 32: T <= 4 tokens at top-8) in one cooperative launch of
+// records (T * k <= 64: T <= 8 tokens at top-8) in one cooperative launch of
 // one CTA per SM, the phases separated by grid-wide barriers:
 //   1  router logits, one expert per CTA (the arithmetic of router_sort_small)
 //   -  barrier
@@ -639,7 +639,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_stream(const StreamArgs 
 // every wait is bounded (kErrTimeoutGrid), and a CTA that gives up skips the
 // rest of the layer.
 
-constexpr int kFusedMaxRecs = 32;  // one warp lane per routing record in the sort
+constexpr int kFusedMaxRecs = 64;  // routing records of the single-launch layers (T*k)
 
 struct DecodeArgs {
   const uint4* x;          // [T][H]
@@ -691,6 +691,7 @@ __device__ bool grid_barrier(unsigned int* ctr, volatile int* abort_flag, int* s
 // (one tile per expert) into rs.  False when the barrier gave up.
 struct RouteSmem {
   int ids[kFusedMaxRecs];
+  int first[kFusedMaxRecs];    // 1: the record opens its expert's tile
   float w[kFusedMaxRecs];      // routing weight of slot n*k + j
   int perm[kFusedMaxRecs];     // slot of the p-th record in expert order
   int pos[kFusedMaxRecs];      // position of slot s in expert order
@@ -765,34 +766,38 @@ __device__ __forceinline__ bool route_and_sort(const uint4* __restrict__ x,
     }
   }
   __syncthreads();
-  if (warp == 0) {
-    // Stable sort of the R <= 32 records by expert, lane r = slot r, over
-    // shuffles: a record's position counts the records with a smaller id or
-    // the same id and a lower slot; one tile per expert, ascending ids.
-    const int my = lane < R ? rs.ids[lane] : 0x7fffffff;
-    int pos = 0, before = 0, same = 0;
-    bool first = lane < R;
+  // Stable sort of the R <= kFusedMaxRecs records by expert, thread r =
+  // slot r, over the ids in shared memory: a record's position counts the
+  // records with a smaller id or the same id and a lower slot; one tile per
+  // expert, ascending ids (the first record of an expert opens its tile).
+  const int r = static_cast<int>(threadIdx.x);
+  int my = 0x7fffffff, pos = 0, before = 0, same = 0;
+  bool first = false;
+  if (r < R) {
+    my = rs.ids[r];
+    first = true;
     for (int j = 0; j < R; ++j) {
-      const int o = __shfl_sync(0xffffffffu, my, j);
-      pos += (o < my || (o == my && j < lane)) ? 1 : 0;
+      const int o = rs.ids[j];
+      pos += (o < my || (o == my && j < r)) ? 1 : 0;
       before += o < my ? 1 : 0;
       same += o == my ? 1 : 0;
-      if (o == my && j < lane) first = false;
+      if (o == my && j < r) first = false;
     }
-    int tile = 0;
+    rs.first[r] = first ? 1 : 0;
+  }
+  __syncthreads();
+  if (r < R) {
+    int tile = 0, n_tiles = 0;
     for (int j = 0; j < R; ++j) {
-      const int o = __shfl_sync(0xffffffffu, my, j);
-      const bool f = __shfl_sync(0xffffffffu, first ? 1 : 0, j) != 0;
-      tile += (f && o < my) ? 1 : 0;
+      const bool f = rs.first[j] != 0;
+      tile += (f && rs.ids[j] < my) ? 1 : 0;
+      n_tiles += f ? 1 : 0;
     }
-    if (lane < R) {
-      rs.perm[pos] = lane;
-      rs.pos[lane] = pos;
-      rs.tile_of[lane] = tile;
-    }
+    rs.perm[pos] = r;
+    rs.pos[r] = pos;
+    rs.tile_of[r] = tile;
     if (first) rs.tiles[tile] = make_int4(my, before, before + same, 0);
-    const int n_tiles = __popc(__ballot_sync(0xffffffffu, first));
-    if (lane == 0) rs.nt = n_tiles;
+    if (r == 0) rs.nt = n_tiles;
   }
   __syncthreads();
   return true;

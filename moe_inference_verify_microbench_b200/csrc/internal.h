@@ -117,7 +117,7 @@ cudaError_t note_cuda_error(cudaError_t e);
 // gate/up GEMM for M <= kGemvW13MaxRows routing records and the down GEMM for
 // M <= kGemvW2MaxRows (measured crossovers on B200, H=2048, I=768, E=128).
 constexpr int kGemvW13MaxRows = 128;
-constexpr int kGemvW2MaxRows = 48;
+constexpr int kGemvW2MaxRows = 64;
 
 bool router_small_ok(int T, int H, int E, int k);
 bool gemv_ok(int n_out, int K, bool swiglu);
@@ -140,7 +140,7 @@ int launch_w2_gemv(const void* h, int M, const int4* tiles, const int* num_tiles
                    const float* row_scale, void* out, int out_rows, int* status,
                    cudaStream_t stream, int max_sms = 0);
 
-// Whole decode layer in one cooperative launch (T * k <= 32 records):
+// Whole decode layer in one cooperative launch (T * k <= 64 records):
 // router, top-k, sort, gate/up and down GEMVs and the k-way combine, bitwise
 // equal to the four-launch decode path.  `scratch` holds
 // fused_decode_scratch_bytes(T, E) bytes; h [T*k, I] and slots [T*k, H] bf16.

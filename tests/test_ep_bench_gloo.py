@@ -132,8 +132,8 @@ def test_roofline_arithmetic_matches_the_per_token_figures():
     assert bench.layer_flops(16384) == 16384 * 76_021_760
     assert bench.layer_bytes(128, 16384) == 128 * 9_437_184 + 524_288 + 4 * 16384 * 2048
     assert bench.layer_launches(16384, 256) == 7 and bench.layer_launches(64, 128) == 5
-    assert [bench.layer_launches(t) for t in (1, 4, 5, 16, 1024, 4096, 8192)] == [1, 1, 4, 4, 5, 5,
-                                                                                 7]
+    assert [bench.layer_launches(t) for t in (1, 4, 8, 9, 16, 1024, 4096, 8192)] == [
+        1, 1, 1, 4, 4, 5, 5, 7]
     assert schedule_work("c7", 16384, 4) == (16384 * 76_021_760, 4 * 16384, "weak")
     f6, t6, s6 = schedule_work("c6", 4096, 4)
     assert (t6, s6) == (4096, "strong")

@@ -408,9 +408,10 @@ def _decode_reference_f32(x, wr, wg, wu, wd, ids, w, k):
     return y
 
 
-@pytest.mark.parametrize("T,norm,with_bias", [(1, True, False), (2, False, False), (4, True, True)])
+@pytest.mark.parametrize("T,norm,with_bias", [(1, True, False), (2, False, False), (4, True, True),
+                                              (6, True, False), (8, False, True)])
 def test_single_launch_decode_layer_bitwise(cuda, T, norm, with_bias):
-    """Up to 32 routing records (T <= 4 at top-8) run the whole layer as one
+    """Up to 64 routing records (T <= 8 at top-8) run the whole layer as one
     cooperative launch (router, top-k, sort, both GEMVs and the combine, with
     grid barriers between them).  Its output must equal the four-launch
     decode pipeline, op by op through the C ABI, bit for bit, at the full
