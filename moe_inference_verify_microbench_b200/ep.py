@@ -282,7 +282,12 @@ def dispatch_combine_peer_pipelined(mod: _EPBase, local_x: torch.Tensor, pxs, st
     chunk has its own peer exchange (own buffers and epochs) and every rank
     issues the exchanges in the same order.  A token's records stay in one
     chunk, so every owner rank sums the same records in the same order as in
-    the one-chunk forward: the output is bit for bit the same."""
+    the one-chunk forward: the output is bit for bit the same.
+
+    On B200 it measured slower than the one-chunk exchange at 2, 4 and 8
+    ranks (16384 tokens per rank): the SM-issued exchange kernels get too few
+    SMs beside the persistent GEMMs to hide behind them, and every chunk adds
+    a pass over the rank's expert weights.  It is kept as an option."""
     K = mod._kernels
     n_ch = len(pxs)
     N, k, epr, ep = local_x.shape[0], mod.top_k, mod.experts_per_rank, mod.ep_size
