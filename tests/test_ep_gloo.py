@@ -248,3 +248,65 @@ def test_loopback_harness_on_cpu(name, world):
         yref = mo.f32_from_bf16_bits(g[f"y_rank{rank}"])
         assert tie.mean() <= 0.2
         assert mo.rel_err(y.float().numpy()[~tie], yref[~tie]) <= 2e-2, (name, rank)
+
+
+def _ragged_overlap_worker(rank, world, port, q):
+    """Rank r holds 0, 3, 7 or 13 tokens (empty and single-token chunks with
+    four chunks); the chunked exchange must give exactly the one-chunk
+    exchange's output on every rank, over two forwards."""
+    sys.path.insert(0, HERE)
+    sys.path.insert(0, os.path.dirname(HERE))
+    import torch.distributed as dist
+    from cpu_contract import CpuContractKernels, CpuPeerExchange
+    from helpers import to_t
+    from moe_inference_verify_microbench_b200.ep import _Streams
+    from moe_inference_verify_microbench_b200.ep_pure import EPSparseMoE as Pure
+    from oracle import moe_oracle as mo
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        H, I, E, k, n_max = 64, 32, 8, 2, 13
+        d = mo.make_inputs(n_max * world, H, I, E, seed=5)
+        weights = (to_t(d["wr"]), [to_t(d["w_gate"][e]) for e in range(E)],
+                   [to_t(d["w_up"][e]) for e in range(E)], [to_t(d["w_down"][e]) for e in range(E)])
+        mods = {}
+        for chunks in (0, 4):
+            m = Pure(H, I, E, k, world, rank, group=None, transport="peer",
+                     max_tokens_per_rank=n_max, overlap=chunks).to(torch.bfloat16)
+            m._kernels = CpuContractKernels
+            m.weight_loader(*weights)
+            if chunks:
+                part = -(-n_max // chunks)
+                m._peer_chunks = [CpuPeerExchange(None, world * part, H, k) for _ in range(chunks)]
+                m._streams = _Streams(torch.device("cpu"))
+            else:
+                m._peer = CpuPeerExchange(None, world * n_max, H, k)
+            mods[chunks] = m
+        n = [0, 3, 7, 13][rank]
+        x_all = to_t(d["x"])
+        same = []
+        with torch.no_grad():
+            for step in range(2):
+                x = x_all[rank * n_max + step:rank * n_max + step + n]
+                same.append(bool(torch.equal(mods[4](x), mods[0](x))))
+        q.put((rank, same))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_chunked_exchange_ragged_batches_equal_one_chunk():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_ragged_overlap_worker, args=(r, 4, 29977, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, same in res.items():
+        assert all(same), (rank, same)
